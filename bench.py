@@ -1,0 +1,393 @@
+#!/usr/bin/env python
+"""MoE-block benchmark on B200.
+
+Workload: decode, batch 1, through the 40 MoE blocks of a
+Qwen3.5-35B-A3B-shaped stack (hidden 2048, 256 experts, top-8 + 1 shared,
+expert FFN 512), random Q4_K expert weights per layer (N(0,0.02), seeded),
+F32 router and shared-gate vector, token vectors ~N(0,1) from a 128-token
+seeded pool.  One step = one token through all 40 blocks; block l+1 reads
+block l's output plus its input (the residual stream), so the blocks run in
+sequence like in the model.  Metric: microseconds per token per MoE block
+(lower is better); ``value`` is whole-job: time / (steps * 40 * n_gpus).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): independent replicas of the same decode
+stream (the decode path does not shard); max-over-ranks device time.
+--impl reference: the reference's CPU path for the same op (the C
+restatement in oracle/, all host threads), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "qwen-3.5-cuda_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "MoE-block µs/token decode (HBM GB/s) & prefill tokens/s at 1/2/4/8 B200"
+UNIT = "us/token"
+N_LAYERS = 40
+POOL = 128
+SEED = 1234
+# algorithmic bytes of one Q4_K MoE block for one token (router F32 + 8 experts
+# x (gate+up+down) + shared gate/up/down + shared gate vector + x in/out)
+BLOCK_BYTES = 2_097_152 + 8 * 1_769_472 + 1_769_472 + 8_192 + 16_384
+WORKLOAD = ("config2: decode batch 1, 40 MoE blocks of a Qwen3.5-35B-A3B-shaped stack "
+            "(d=2048, E=256, top-8, F=512, shared 512), Q4_K experts, F32 router/shared gate")
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_from_profiles():
+    p = ROOT / "profiles" / "moe_decode_block_q4k.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_block:\s*([0-9]+)", p.read_text())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler(threading.Thread):
+    """NVML clocks/throttle reasons sampled during the timed region."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, dev_index: int):
+        super().__init__(daemon=True)
+        self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(dev_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - NVML is optional
+            self.ok = False
+
+    def run(self):
+        if not self.ok:
+            return
+        nv = self.nv
+        get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = get_r(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
+    def stop(self):
+        self._stop.set()
+        self.join(timeout=2)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qmoe import _lib, synth
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    L = args.layers
+    dims = synth.Dims()
+    dc = dims.c()
+    blocks = [synth.Block(dims, synth.Q4K_TYPES, seed=SEED, layer=l, device="cuda") for l in range(L)]
+    cblocks = [b.c() for b in blocks]
+    inputs = synth.inputs(POOL, dims.d_model, seed=SEED, tag=2)
+    nws = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), 1)
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), nws, None))
+    xbuf = torch.empty((1, dims.d_model), dtype=torch.float32, device="cuda")
+    bufs = [torch.empty_like(xbuf), torch.empty_like(xbuf)]
+    fwd = _lib.lib().qmoe_block_forward
+
+    def step(stream_ptr):
+        x = xbuf
+        for l in range(L):
+            out = bufs[l % 2]
+            st = fwd(ctypes.byref(cblocks[l]), ctypes.byref(dc), x.data_ptr(), out.data_ptr(), x.data_ptr(), 1,
+                     ws.data_ptr(), nws, stream_ptr)
+            if st:
+                raise RuntimeError(f"block_forward layer {l}: {_lib.status_string(st)}")
+            x = out
+        return x
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for i in range(3):
+            xbuf.copy_(inputs[i:i + 1])
+            final = step(s.cuda_stream)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        final = step(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+
+    # warm-up
+    for i in range(args.warmup):
+        xbuf.copy_(inputs[i % POOL:i % POOL + 1], non_blocking=True)
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        xbuf.copy_(inputs[i % POOL:i % POOL + 1], non_blocking=True)
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        dist.barrier()
+
+    # end to end through the C-ABI: pinned host input -> device, 40 blocks,
+    # result -> pinned host, synchronised every token like a decode loop
+    h_in = inputs.cpu().pin_memory()
+    h_out = torch.empty((POOL, dims.d_model), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        xbuf.copy_(h_in[i % POOL:i % POOL + 1], non_blocking=True)
+        g.replay()
+        h_out[i % POOL:i % POOL + 1].copy_(final, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+
+    st, flags, _ = _check_errors(_lib, ws, dc)
+    if st:
+        raise RuntimeError(f"device error word after the run: flags {flags:#x}")
+
+    if world > 1:
+        t = torch.tensor([ms, ems], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ems = float(t[0]), float(t[1])
+    del g
+
+    per_block_us = ms * 1e3 / (args.steps * L)          # one GPU
+    value = ms * 1e3 / (args.steps * L * world)         # whole job
+    e2e = ems * 1e3 / (args.steps * L * world)
+    peak, peak_kind = _peaks()
+    achieved = BLOCK_BYTES / (per_block_us * 1e-6) / 1e9
+    traffic = _traffic_from_profiles()
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K; x ~ N(0,1))",
+        "config": {"workload": WORKLOAD, "tokens_per_step": 1, "layers": L, "parallelism": f"replicas{world}",
+                   "l2": "inputs larger than L2: ~722 MB of distinct weights touched per step vs 126 MB L2",
+                   "launch": "one CUDA graph per step (3 kernels per block)"},
+        "clocks": clk,
+        "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": 4 * dims.d_model,
+                "d2h_bytes_per_step": 4 * dims.d_model,
+                "note": "pinned host token in, 40 blocks via the C-ABI (graph replay), result to host, sync per token"},
+        "gpu_launches": args.steps * L * 3,
+        "roofline": {"kernel": "moe_block (router_topk + gateup + down_combine)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "algorithmic_bytes": BLOCK_BYTES,
+                     "traffic": traffic},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"], line["parity"] = cpu_baseline(args, blocks, inputs, dims, dc, ws, nws)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def _check_errors(_lib, ws, dc):
+    err = (ctypes.c_uint32 * 2)()
+    st = _lib.lib().qmoe_check_errors(ws.data_ptr(), ctypes.byref(dc), err, None)
+    return st, int(err[0]), int(err[1])
+
+
+def cpu_baseline(args, blocks, inputs, dims, dc, ws, nws):
+    """The oracle (C restatement of the reference MoE path) on the host cores
+    over a bounded sample, plus a parity gate on the same sample."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as orc
+    from qmoe import _lib, synth
+
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    S = min(args.cpu_layers, len(blocks))
+    x = inputs[0:1].clone()
+    out = torch.empty_like(x)
+    secs, ids_ok, max_err, within = 0.0, True, 0.0, True
+    for l in range(S):
+        c = blocks[l].c()
+        _lib.check(_lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(), out.data_ptr(),
+                                                 None, 1, ws.data_ptr(), nws, None))
+        torch.cuda.synchronize()
+        p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), 1, _lib.WS_TOPK_IDX)
+        off = p - ws.data_ptr()
+        gid = ws[off:off + 4 * dims.top_k].cpu().numpy().view(np.int32)
+        host = {n: blocks[l].host_bytes(n) for n in synth.TENSORS}
+        xh = x.cpu().numpy()
+        t0 = time.perf_counter()
+        res = orc.moe_forward(host, blocks[l].types, dims, xh)
+        secs += time.perf_counter() - t0
+        got = out.cpu().numpy()
+        ids_ok &= bool(np.array_equal(gid, res["idx"][0]))
+        max_err = max(max_err, float(np.max(np.abs(got - res["out"]))))
+        within &= bool(np.all(np.isclose(got, res["out"], atol=1e-3, rtol=1e-2)))
+        x = (x + out).contiguous()  # residual stream, as in the timed run
+    cpu = {"value": round(secs / S * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"{S} MoE blocks x 1 token (layers 0..{S - 1} of the config-2 stack, step 0), "
+                     "oracle/qmoe_oracle.c, OpenMP over output rows"}
+    parity = {"blocks": S, "ids_bit_exact": ids_ok, "max_abs_err": max_err, "within_tol": within,
+              "tol": "max-abs 1e-3 / rel 1e-2"}
+    return cpu, parity
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU path (oracle port), rank 0 only
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    import numpy as np
+
+    from oracle import oracle as orc
+    from qmoe import _lib, synth
+    from qmoe.quant import GgmlType, calculate_tensor_bytes
+
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    dims = synth.Dims()
+    d, E, k, F, Fs = dims.d_model, dims.num_experts, dims.top_k, dims.expert_dim, dims.shared_dim
+    types = synth.Q4K_TYPES
+    pool = synth.inputs(POOL, d, seed=SEED, tag=2, device="cpu")
+    layer_cache = {}
+
+    def fill_range(name, layer, first, n, dst):
+        sid = synth.stream_id(layer, synth.TENSORS.index(name) + 1)
+        _lib.check(_lib.lib().qmoe_synth_fill_host_range(dst.ctypes.data, int(types[name]), first, n, SEED, sid,
+                                                         synth.WEIGHT_SIGMA))
+
+    def layer_tensors(layer):
+        if layer not in layer_cache:
+            t = {}
+            for n in synth.TENSORS:
+                nb = calculate_tensor_bytes(types[n], dims.elements(n))
+                t[n] = np.zeros(nb, dtype=np.uint8)  # lazily backed; only filled slices are touched
+            for n in ("router", "shared_gate_inp", "shared_gate", "shared_up", "shared_down"):
+                fill_range(n, layer, 0, dims.elements(n), t[n])
+            layer_cache[layer] = (t, set())
+            if len(layer_cache) > 4:
+                layer_cache.pop(next(iter(layer_cache)))
+        return layer_cache[layer]
+
+    def prepare(step):
+        layer = step % N_LAYERS
+        x = pool[(step // N_LAYERS) % POOL]
+        t, have = layer_tensors(layer)
+        logits = orc.gemv(t["router"], 0, E * d, x, E, d)
+        ids, _ = orc.topk(logits, k)
+        for e in ids.tolist():
+            if e in have:
+                continue
+            bpe = calculate_tensor_bytes(GgmlType.Q4_K, F * d)
+            for n in ("gate_exps", "up_exps", "down_exps"):
+                fill_range(n, layer, e * F * d, F * d, t[n][e * bpe:(e + 1) * bpe])
+            have.add(e)
+        return t, x
+
+    for i in range(args.warmup):
+        t, x = prepare(i)
+        orc.moe_forward(t, types, dims, x)
+    secs = 0.0
+    for i in range(args.steps):
+        t, x = prepare(args.warmup + i)
+        t0 = time.perf_counter()
+        res = orc.moe_forward(t, types, dims, x)
+        secs += time.perf_counter() - t0
+        assert res["status"][0] == 0
+    value = secs / args.steps * 1e6
+    sample = (f"{args.steps} MoE blocks x 1 token (layer = step mod 40) of the config-2 stack; "
+              "only the routed experts' bytes are generated; oracle/qmoe_oracle.c, OpenMP over output rows")
+    line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value / 1e3, 3),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": WORKLOAD, "tokens_per_step": 1, "layers": 1,
+                                           "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--cpu-layers", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,188 @@
+/*
+ * qmoe.h -- C-ABI of the B200 MoE block (router, dispatch, grouped expert
+ * products, shared expert, combine) for Qwen3.5-35B-A3B-shaped layers.
+ *
+ * Plain pointers and sizes only.  Every tensor/activation pointer is a DEVICE
+ * pointer; every call is asynchronous on the given CUDA stream (NULL = legacy
+ * default stream) and returns a status code; no C++ exception crosses this
+ * boundary.  The C++ headers include/quantized.hpp, include/matmul_q4.hpp and
+ * include/layer_moe.hpp wrap these calls with the reference's interfaces and
+ * turn status codes back into std::runtime_error.
+ *
+ * Reference interfaces replaced (sahan974/qwen-3.5-cuda, file:line):
+ *   qmoe_type_supported   include/matmul_q4.hpp:10   matmul_type_supported
+ *   qmoe_gemv             include/matmul_q4.hpp:13-21 matmul_dispatch
+ *   qmoe_dequant_row      include/matmul_q4.hpp:24-30 dequantize_row
+ *   qmoe_router_topk      src/layer_moe.cpp:98-99     router GEMV + moe_topk
+ *                         (src/cuda/moe.cu:7-57), plus the host checks of
+ *                         src/layer_moe.cpp:102-124 moved onto the device
+ *   qmoe_dispatch         no counterpart (the reference is single-token)
+ *   qmoe_expert_gateup    src/layer_moe.cpp:131-135, 147-149 (gate/up GEMVs,
+ *                         moe_silu_mul) for all routed pairs + shared expert
+ *   qmoe_down_combine     src/layer_moe.cpp:138-141, 150-154 (down GEMVs,
+ *                         moe_add, moe_shared_add, final copy)
+ *   qmoe_block_forward    src/layer_moe.cpp:82-155   MoeLayer::forward, for
+ *                         T >= 1 tokens at once
+ *   qmoe_workspace_size   src/layer_moe.cpp:51-78    MoeLayer::init buffers
+ */
+#ifndef QMOE_H
+#define QMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QMOE_API __attribute__((visibility("default")))
+#else
+#define QMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; spelled out so this header needs no CUDA header. */
+typedef struct CUstream_st* qmoe_stream_t;
+
+/* Status codes.  Host-side argument checks mirror the reference's exceptions. */
+enum qmoe_status {
+    QMOE_OK = 0,
+    QMOE_ERR_ARG = 1,            /* null / not-loaded tensor (matmul_q4.cu:187-189) or bad argument */
+    QMOE_ERR_TYPE = 2,           /* unsupported GGML type (matmul_q4.cu:190-192) */
+    QMOE_ERR_SHAPE = 3,          /* shape exceeds tensor (matmul_q4.cu:193-195, :215-217) */
+    QMOE_ERR_ALIGN = 4,          /* device pointer not 16-byte aligned */
+    QMOE_ERR_WORKSPACE = 5,      /* workspace missing or too small */
+    QMOE_ERR_UNSUPPORTED = 6,    /* dimensions outside what the kernels support */
+    QMOE_ERR_CUDA = 7,           /* CUDA runtime / launch error */
+    QMOE_ERR_ROUTING = 10,       /* device error word: invalid or non-finite routing (layer_moe.cpp:116-118) */
+    QMOE_ERR_NOT_NORMALIZED = 11,/* device error word: route weights not normalised (layer_moe.cpp:122-124) */
+    QMOE_ERR_TIMEOUT = 12        /* device error word: a bounded device-side wait gave up */
+};
+
+/* Non-owning view of one GGUF tensor on the device (reference QuantTensor,
+ * include/quantized.hpp:38-46: device_ptr, type, num_elements). */
+typedef struct qmoe_tensor {
+    const void* data;       /* device pointer to the raw GGUF payload, 16-byte aligned */
+    uint32_t ggml_type;     /* GgmlType id (include/quantized.hpp:12-36) */
+    uint32_t reserved;      /* must be 0 */
+    uint64_t num_elements;  /* logical element count */
+} qmoe_tensor;
+
+/* MoE dimensions (reference ModelConfig MoE fields, include/config.hpp:33-37). */
+typedef struct qmoe_dims {
+    int32_t d_model;        /* hidden size (2048) */
+    int32_t num_experts;    /* routed experts E (256) */
+    int32_t top_k;          /* experts per token k (8) */
+    int32_t expert_dim;     /* routed expert FFN dim F (512) */
+    int32_t shared_dim;     /* shared expert FFN dim Fs */
+} qmoe_dims;
+
+/* The eight tensors of one MoE block, named as in model.cpp:140-147. */
+typedef struct qmoe_block {
+    qmoe_tensor router;          /* ffn_gate_inp.weight        {d, E}     F32 */
+    qmoe_tensor gate_exps;       /* ffn_gate_exps.weight       {d, F, E}       */
+    qmoe_tensor up_exps;         /* ffn_up_exps.weight         {d, F, E}       */
+    qmoe_tensor down_exps;       /* ffn_down_exps.weight       {F, d, E}       */
+    qmoe_tensor shared_gate_inp; /* ffn_gate_inp_shexp.weight  {d}        F32 */
+    qmoe_tensor shared_gate;     /* ffn_gate_shexp.weight      {d, Fs}         */
+    qmoe_tensor shared_up;       /* ffn_up_shexp.weight        {d, Fs}         */
+    qmoe_tensor shared_down;     /* ffn_down_shexp.weight      {Fs, d}         */
+    const float* expert_bias;    /* optional device F32[E] added to the router logits before
+                                    selection (no counterpart in the reference; used by the
+                                    uneven-routing benchmark); NULL = none */
+} qmoe_block;
+
+/* Named buffers inside a block workspace (see qmoe_ws_view). */
+enum qmoe_ws_buffer {
+    QMOE_WS_LOGITS = 0,   /* float [T][E+1]; column E holds the shared-expert gate logit */
+    QMOE_WS_TOPK_IDX = 1, /* int32 [T][k], selection order */
+    QMOE_WS_TOPK_W = 2,   /* float [T][k] */
+    QMOE_WS_OFFSETS = 3,  /* int32 [E+1] first pair of each expert in the permutation */
+    QMOE_WS_PERM = 4,     /* int32 [T*k]  pair p = t*k + j at each permuted position */
+    QMOE_WS_INV_PERM = 5, /* int32 [T*k]  permuted position of each pair (-1: invalid) */
+    QMOE_WS_HIDDEN = 6,   /* float [T*k + T][max(F,Fs)] silu(gate)*up: routed pairs, then shared per token */
+    QMOE_WS_ERROR = 7     /* uint32 [4]: error flags, first failing token, spare */
+};
+
+/* ABI version of this header (bumped on any incompatible change). */
+QMOE_API int qmoe_abi_version(void);
+/* Static text for a status code. */
+QMOE_API const char* qmoe_status_string(int status);
+
+/* 1 if GGML type `ggml_type` is accepted by qmoe_gemv / qmoe_dequant_row
+ * (F32, F16, BF16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K), else 0. */
+QMOE_API int qmoe_type_supported(uint32_t ggml_type);
+
+/* y[M] = rows [element_offset/K, element_offset/K + M) of W times x[K]. */
+QMOE_API int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, int K,
+              uint64_t element_offset, qmoe_stream_t stream);
+
+/* out[cols] = elements [row*cols, row*cols + cols) of W, dequantised to F32. */
+QMOE_API int qmoe_dequant_row(const qmoe_tensor* w, float* out, int row, int cols, qmoe_stream_t stream);
+
+/* Device workspace bytes needed by the block entry points for up to
+ * `max_tokens` tokens per call; 0 if the dimensions are unsupported. */
+QMOE_API size_t qmoe_workspace_size(const qmoe_dims* dims, int max_tokens);
+
+/* Device pointer to a named buffer inside `workspace` for a call of T tokens. */
+QMOE_API void* qmoe_ws_view(void* workspace, const qmoe_dims* dims, int T, int which);
+
+/* Router logits (reference reduction order, so expert ids are bit-identical),
+ * optional expert bias, top-k selection + softmax over the selected logits,
+ * on-device validation, and the token->expert permutation.  Results stay in
+ * the workspace (QMOE_WS_*); `topk_idx`/`topk_w` (optional, device) receive
+ * copies.  Routing errors are recorded in the device error word. */
+QMOE_API int qmoe_router_topk(const qmoe_block* blk, const qmoe_dims* dims, const float* x, int T,
+                     int32_t* topk_idx, float* topk_w,
+                     void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Stable token->expert permutation of a top-k result: pairs p = t*k + j are
+ * ordered by (expert, t, j).  offsets[E+1], perm[T*k], inv_perm[T*k] (device). */
+QMOE_API int qmoe_dispatch(const int32_t* topk_idx, int T, int k, int E,
+                  int32_t* offsets, int32_t* perm, int32_t* inv_perm,
+                  void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Gate/up products of every routed (token, expert) pair and of the shared
+ * expert, fused with silu(gate)*up, for the routing in the workspace. */
+QMOE_API int qmoe_expert_gateup(const qmoe_block* blk, const qmoe_dims* dims, const float* x, int T,
+                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Down products of every routed pair and of the shared expert, combined per
+ * token in selection order j = 0..k-1, then + sigmoid(shared gate) * shared:
+ * out[t] = (residual ? residual[t] : 0) + moe(x[t]). */
+QMOE_API int qmoe_down_combine(const qmoe_block* blk, const qmoe_dims* dims, int T,
+                      float* out, const float* residual,
+                      void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* The whole MoE block for T tokens: router_topk, expert_gateup, down_combine.
+ * x, out: device F32 [T][d_model]; residual optional (NULL). */
+QMOE_API int qmoe_block_forward(const qmoe_block* blk, const qmoe_dims* dims, const float* x, float* out,
+                       const float* residual, int T,
+                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Waits for `stream`, reads the device error word of `workspace` into
+ * err[0..1] (flags, first failing token) and clears it.  Returns the status
+ * the flags map to (QMOE_OK if none). */
+QMOE_API int qmoe_check_errors(void* workspace, const qmoe_dims* dims, uint32_t* err, qmoe_stream_t stream);
+
+/* Clears the workspace control words (call once after allocating it). */
+QMOE_API int qmoe_workspace_init(void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Synthetic tensors for tests and benchmarks: elements sigma*N(0,1) from a
+ * counter-based stream (seed, stream_id), encoded as `ggml_type`.  The device
+ * and host versions write identical bytes. */
+QMOE_API int qmoe_synth_fill(void* dst, uint32_t ggml_type, uint64_t num_elements, uint64_t seed,
+                    uint64_t stream_id, float sigma, qmoe_stream_t stream);
+QMOE_API int qmoe_synth_fill_host(void* dst, uint32_t ggml_type, uint64_t num_elements, uint64_t seed,
+                         uint64_t stream_id, float sigma);
+/* Host: elements [first_element, first_element + num_elements) of the same
+ * stream (first_element a multiple of the block size), written to dst. */
+QMOE_API int qmoe_synth_fill_host_range(void* dst, uint32_t ggml_type, uint64_t first_element,
+                                        uint64_t num_elements, uint64_t seed, uint64_t stream_id, float sigma);
+/* Bytes of a GGML tensor of `num_elements` elements (quantized.hpp:98-105), 0 if invalid. */
+QMOE_API uint64_t qmoe_tensor_bytes(uint32_t ggml_type, uint64_t num_elements);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QMOE_H */

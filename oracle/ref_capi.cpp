@@ -1,0 +1,87 @@
+// C entry points over the reference's own MoE path (layer_moe.cpp,
+// matmul_q4.cu, moe.cu compiled unmodified from the reference tree), so the
+// parity tests can run the reference on the GPU box with the same device
+// buffers as the product.  TEST INFRASTRUCTURE ONLY.
+#include "layer_moe.hpp"
+#include "matmul_q4.hpp"
+#include <cstring>
+#include <exception>
+#include <string>
+
+namespace qwen {
+void moe_topk(const float* router, int* top_idx, float* top_weight, int experts, int k, cudaStream_t stream);
+}
+
+namespace {
+thread_local std::string g_last_error;
+
+qwen::QuantTensor make_tensor(const char* name, const void* p, int type, unsigned long long n) {
+    qwen::QuantTensor t;
+    t.name = name;
+    t.type = static_cast<qwen::GgmlType>(type);
+    t.shape = {static_cast<int64_t>(n)};
+    t.num_elements = n;
+    t.size_bytes = qwen::calculate_tensor_bytes(t.type, n);
+    t.offset = 0;
+    t.device_ptr = const_cast<void*>(p);
+    return t;
+}
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error(void) { return g_last_error.c_str(); }
+
+// matmul_dispatch (matmul_q4.cu:185-207); returns 0 or 1 (exception text in ref_last_error).
+int ref_gemv(const void* w, int type, unsigned long long n, const float* x, float* y, int M, int K,
+             unsigned long long off, void* stream) {
+    try {
+        qwen::QuantTensor t = make_tensor("w", w, type, n);
+        qwen::matmul_dispatch(t, x, y, M, K, static_cast<cudaStream_t>(stream), off);
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+int ref_dequantize_row(const void* w, int type, unsigned long long n, float* out, int row, int cols, void* stream) {
+    try {
+        qwen::QuantTensor t = make_tensor("w", w, type, n);
+        qwen::dequantize_row(t, out, row, cols, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+int ref_topk(const float* logits, int* idx, float* w, int n, int k, void* stream) {
+    try {
+        qwen::moe_topk(logits, idx, w, n, k, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+// T tokens through MoeLayer::forward, one call per token, as model.cpp:209
+// does.  Tensor arguments: pointer, GGML type, element count, 8 tensors in
+// the order router, gate_exps, up_exps, down_exps, shared_gate_inp,
+// shared_gate, shared_up, shared_down.
+int ref_moe_forward(int d, int E, int k, int F, int Fs, int T, const float* x, float* out,
+                    const void* const* ptrs, const int* types, const unsigned long long* nelem, void* stream) {
+    try {
+        qwen::ModelConfig c;
+        c.d_model = d;
+        c.num_experts = E;
+        c.num_experts_per_tok = k;
+        c.moe_intermediate_dim = F;
+        c.shared_expert_dim = Fs;
+        static const char* names[8] = {"ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps",
+                                       "ffn_gate_inp_shexp", "ffn_gate_shexp", "ffn_up_shexp", "ffn_down_shexp"};
+        qwen::QuantTensor t[8];
+        for (int i = 0; i < 8; ++i) t[i] = make_tensor(names[i], ptrs[i], types[i], nelem[i]);
+        qwen::CudaContext ctx(static_cast<cudaStream_t>(stream));
+        qwen::MoeLayer layer;
+        layer.init(c, 0);
+        for (int i = 0; i < T; ++i)
+            layer.forward(x + (size_t)i * d, out + (size_t)i * d, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[7], ctx);
+        ctx.synchronize();
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+}  // extern "C"

@@ -1,0 +1,301 @@
+// extern "C" entry points of include/qmoe.h: argument checks (the reference's
+// host-side exceptions become status codes), workspace layout, launches.
+#include <algorithm>
+#include <cstring>
+#include "qmoe_dev.cuh"
+#include "qmoe_internal.h"
+
+namespace qmoe {
+cudaError_t launch_router(const DecodeParams& P, cudaStream_t s);
+cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s);
+cudaError_t launch_down(const DecodeParams& P, cudaStream_t s);
+bool decode_supported(const DecodeParams& P);
+int decode_num_sms();
+cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
+                        cudaStream_t s);
+cudaError_t launch_dequant_row(const uint8_t* w, int type, float* out, uint64_t start, int cols, cudaStream_t s);
+cudaError_t launch_synth(void* dst, int type, uint64_t nblocks, uint64_t seed, uint64_t stream_id, float sigma,
+                         cudaStream_t s);
+cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
+                            int32_t* table, cudaStream_t s);
+size_t dispatch_scratch_bytes(int E);
+
+__global__ void k_ws_init(uint32_t* ctrl) {
+    const int i = threadIdx.x;
+    if (i < CTRL_WORDS) ctrl[i] = (i == CTRL_ERR_TOKEN) ? 0xFFFFFFFFu : 0u;
+}
+}  // namespace qmoe
+
+using namespace qmoe;
+
+namespace {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? QMOE_OK : QMOE_ERR_CUDA; }
+
+bool gemv_type(uint32_t t) {
+    return t == 0 || t == 1 || t == 30 || t == 2 || t == 6 || t == 8 || t == 12 || t == 13 || t == 14;
+}
+bool expert_type(uint32_t t) { return t == 8 || t == 12 || t == 13 || t == 14; }
+bool router_type(uint32_t t) { return t == 0 || t == 1 || t == 30; }
+
+bool pow2_in(int v, int lo, int hi) { return v >= lo && v <= hi && (v & (v - 1)) == 0; }
+
+int check_dims(const qmoe_dims* D) {
+    if (!D) return QMOE_ERR_ARG;
+    if (D->d_model <= 0 || D->num_experts <= 0 || D->top_k <= 0 || D->expert_dim <= 0 || D->shared_dim <= 0)
+        return QMOE_ERR_ARG;
+    if (D->top_k > D->num_experts) return QMOE_ERR_ARG;
+    // decode kernels: one 64-element unit per lane, up to 32 units per row;
+    // K-quant rows need multiples of 256
+    if (!pow2_in(D->d_model, 256, 2048) || !pow2_in(D->expert_dim, 256, 2048) || !pow2_in(D->shared_dim, 256, 2048))
+        return QMOE_ERR_UNSUPPORTED;
+    if (D->num_experts > kMaxExperts || D->top_k > kMaxTopK) return QMOE_ERR_UNSUPPORTED;
+    return QMOE_OK;
+}
+
+int check_tensor(const qmoe_tensor& t, uint64_t need, bool (*typeok)(uint32_t)) {
+    if (!t.data) return QMOE_ERR_ARG;
+    if (!typeok(t.ggml_type)) return QMOE_ERR_TYPE;
+    if (t.num_elements < need) return QMOE_ERR_SHAPE;
+    const int be = blk_elems(static_cast<int>(t.ggml_type));
+    if (be == 0 || t.num_elements % be) return QMOE_ERR_SHAPE;
+    if (!aligned16(t.data)) return QMOE_ERR_ALIGN;
+    return QMOE_OK;
+}
+
+int check_block(const qmoe_block* B, const qmoe_dims* D) {
+    if (!B) return QMOE_ERR_ARG;
+    const uint64_t d = D->d_model, E = D->num_experts, F = D->expert_dim, Fs = D->shared_dim;
+    int st;
+    if ((st = check_tensor(B->router, E * d, router_type))) return st;
+    if ((st = check_tensor(B->gate_exps, E * F * d, expert_type))) return st;
+    if ((st = check_tensor(B->up_exps, E * F * d, expert_type))) return st;
+    if ((st = check_tensor(B->down_exps, E * d * F, expert_type))) return st;
+    if (B->up_exps.ggml_type != B->gate_exps.ggml_type) return QMOE_ERR_TYPE;
+    if ((st = check_tensor(B->shared_gate_inp, d, router_type))) return st;
+    if ((st = check_tensor(B->shared_gate, Fs * d, expert_type))) return st;
+    if ((st = check_tensor(B->shared_up, Fs * d, expert_type))) return st;
+    if ((st = check_tensor(B->shared_down, d * Fs, expert_type))) return st;
+    if (B->shared_up.ggml_type != B->shared_gate.ggml_type) return QMOE_ERR_TYPE;
+    if (B->expert_bias && (reinterpret_cast<uintptr_t>(B->expert_bias) & 3u)) return QMOE_ERR_ALIGN;
+    return QMOE_OK;
+}
+
+WArg warg(const qmoe_tensor& t) {
+    WArg a;
+    a.p = static_cast<const uint8_t*>(t.data);
+    a.end = a.p + qmoe_tensor_bytes(t.ggml_type, t.num_elements);
+    a.type = static_cast<int>(t.ggml_type);
+    a.pad = 0;
+    return a;
+}
+
+// DecodeParams for tokens [0, T) of x/out at the given workspace.
+DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out, const float* residual,
+                         int T, void* ws) {
+    DecodeParams P;
+    std::memset(&P, 0, sizeof(P));
+    P.d = D->d_model; P.E = D->num_experts; P.k = D->top_k; P.F = D->expert_dim; P.Fs = D->shared_dim; P.T = T;
+    P.has_shared = 1;
+    P.num_sms = decode_num_sms();
+    P.router = static_cast<const uint8_t*>(B->router.data);
+    P.router_type = static_cast<int>(B->router.ggml_type);
+    P.sgate_inp = static_cast<const uint8_t*>(B->shared_gate_inp.data);
+    P.sgate_type = static_cast<int>(B->shared_gate_inp.ggml_type);
+    P.bias = B->expert_bias;
+    P.gate = warg(B->gate_exps); P.up = warg(B->up_exps); P.down = warg(B->down_exps);
+    P.sgate = warg(B->shared_gate); P.sup = warg(B->shared_up); P.sdown = warg(B->shared_down);
+    P.x = x; P.out = out; P.residual = residual;
+    const WsLayout L = ws_layout(*D, T);
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    P.ctrl = reinterpret_cast<uint32_t*>(w + L.ctrl);
+    P.logits = reinterpret_cast<float*>(w + L.logits);
+    P.topk_idx = reinterpret_cast<int32_t*>(w + L.topk_idx);
+    P.topk_w = reinterpret_cast<float*>(w + L.topk_w);
+    P.offsets = reinterpret_cast<int32_t*>(w + L.offsets);
+    P.perm = reinterpret_cast<int32_t*>(w + L.perm);
+    P.inv_perm = reinterpret_cast<int32_t*>(w + L.inv_perm);
+    P.active = reinterpret_cast<int32_t*>(w + L.active);
+    P.xq = w + L.xq; P.xq_stride = L.xq_stride;
+    P.hidden = reinterpret_cast<float*>(w + L.hidden);
+    P.hq = w + L.hq; P.hq_stride = L.hq_stride; P.H = L.H;
+    return P;
+}
+
+int check_common(const qmoe_block* B, const qmoe_dims* D, int T, void* ws, size_t ws_bytes, int maxT) {
+    int st;
+    if ((st = check_dims(D))) return st;
+    if ((st = check_block(B, D))) return st;
+    if (T <= 0) return QMOE_ERR_ARG;
+    if (T > maxT) return QMOE_ERR_UNSUPPORTED;
+    if (!ws || !aligned16(ws)) return QMOE_ERR_WORKSPACE;
+    if (ws_layout(*D, std::min(T, kDecodeMaxT)).total > ws_bytes) return QMOE_ERR_WORKSPACE;
+    return QMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qmoe_abi_version(void) { return 1; }
+
+const char* qmoe_status_string(int s) {
+    switch (s) {
+        case QMOE_OK: return "ok";
+        case QMOE_ERR_ARG: return "invalid argument (null or not-loaded tensor)";
+        case QMOE_ERR_TYPE: return "unsupported GGML type";
+        case QMOE_ERR_SHAPE: return "shape exceeds tensor";
+        case QMOE_ERR_ALIGN: return "pointer not 16-byte aligned";
+        case QMOE_ERR_WORKSPACE: return "workspace missing or too small";
+        case QMOE_ERR_UNSUPPORTED: return "dimensions not supported by the kernels";
+        case QMOE_ERR_CUDA: return "CUDA error";
+        case QMOE_ERR_ROUTING: return "invalid/non-finite MoE routing result";
+        case QMOE_ERR_NOT_NORMALIZED: return "MoE routing weights are not normalized";
+        case QMOE_ERR_TIMEOUT: return "device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int qmoe_type_supported(uint32_t t) { return gemv_type(t) ? 1 : 0; }
+
+uint64_t qmoe_tensor_bytes(uint32_t t, uint64_t n) {
+    const int be = blk_elems(static_cast<int>(t)), bb = blk_bytes(static_cast<int>(t));
+    if (be == 0 || bb == 0 || n % static_cast<uint64_t>(be)) return 0;
+    return n / be * static_cast<uint64_t>(bb);
+}
+
+int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, int K, uint64_t off, qmoe_stream_t stream) {
+    if (!w || !w->data || !x || !y) return QMOE_ERR_ARG;
+    if (!gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
+    if (M <= 0 || K <= 0 || off + static_cast<uint64_t>(M) * K > w->num_elements) return QMOE_ERR_SHAPE;
+    return cuda_status(launch_gemv(static_cast<const uint8_t*>(w->data), static_cast<int>(w->ggml_type), x, y, M, K,
+                                   off, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_dequant_row(const qmoe_tensor* w, float* out, int row, int cols, qmoe_stream_t stream) {
+    if (!w || !w->data || !out || !gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
+    const uint64_t start = static_cast<uint64_t>(row) * cols;
+    if (row < 0 || cols <= 0 || start + cols > w->num_elements) return QMOE_ERR_SHAPE;
+    return cuda_status(launch_dequant_row(static_cast<const uint8_t*>(w->data), static_cast<int>(w->ggml_type), out,
+                                          start, cols, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t qmoe_workspace_size(const qmoe_dims* D, int max_tokens) {
+    if (check_dims(D) || max_tokens <= 0) return 0;
+    const size_t a = ws_layout(*D, std::min(max_tokens, kDecodeMaxT)).total;
+    const size_t b = dispatch_scratch_bytes(D->num_experts) + 256;
+    return std::max(a, b);
+}
+
+void* qmoe_ws_view(void* ws, const qmoe_dims* D, int T, int which) {
+    if (!ws || check_dims(D) || T <= 0) return nullptr;
+    const WsLayout L = ws_layout(*D, std::min(T, kDecodeMaxT));
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    switch (which) {
+        case QMOE_WS_LOGITS: return w + L.logits;
+        case QMOE_WS_TOPK_IDX: return w + L.topk_idx;
+        case QMOE_WS_TOPK_W: return w + L.topk_w;
+        case QMOE_WS_OFFSETS: return w + L.offsets;
+        case QMOE_WS_PERM: return w + L.perm;
+        case QMOE_WS_INV_PERM: return w + L.inv_perm;
+        case QMOE_WS_HIDDEN: return w + L.hidden;
+        case QMOE_WS_ERROR: return w + L.ctrl + CTRL_ERROR * 4;
+        default: return nullptr;
+    }
+}
+
+int qmoe_workspace_init(void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    if (!ws || ws_bytes < 256) return QMOE_ERR_WORKSPACE;
+    k_ws_init<<<1, CTRL_WORDS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t*>(ws));
+    return cuda_status(cudaGetLastError());
+}
+
+int qmoe_router_topk(const qmoe_block* B, const qmoe_dims* D, const float* x, int T, int32_t* topk_idx,
+                     float* topk_w, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
+    if (st) return st;
+    if (!x || !aligned16(x)) return x ? QMOE_ERR_ALIGN : QMOE_ERR_ARG;
+    DecodeParams P = make_params(B, D, x, nullptr, nullptr, T, ws);
+    P.out_idx = topk_idx;
+    P.out_w = topk_w;
+    return cuda_status(launch_router(P, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_dispatch(const int32_t* idx, int T, int k, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
+                  void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    if (!idx || !offsets || !perm || T <= 0 || k <= 0 || E <= 0) return QMOE_ERR_ARG;
+    if (static_cast<int64_t>(T) * k > (1ll << 30)) return QMOE_ERR_UNSUPPORTED;
+    if (!ws || ws_bytes < dispatch_scratch_bytes(E)) return QMOE_ERR_WORKSPACE;
+    return cuda_status(launch_dispatch(idx, T * k, E, offsets, perm, inv_perm, static_cast<int32_t*>(ws),
+                                       reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_expert_gateup(const qmoe_block* B, const qmoe_dims* D, const float* x, int T, void* ws, size_t ws_bytes,
+                       qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
+    if (st) return st;
+    (void)x;  // the activation planes of x were written by qmoe_router_topk
+    DecodeParams P = make_params(B, D, x, nullptr, nullptr, T, ws);
+    if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    return cuda_status(launch_gateup(P, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_down_combine(const qmoe_block* B, const qmoe_dims* D, int T, float* out, const float* residual, void* ws,
+                      size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
+    if (st) return st;
+    if (!out) return QMOE_ERR_ARG;
+    DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
+    if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    return cuda_status(launch_down(P, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_block_forward(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out, const float* residual,
+                       int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
+    if (st) return st;
+    if (!x || !out) return QMOE_ERR_ARG;
+    if (!aligned16(x)) return QMOE_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
+        const int n = std::min(kDecodeMaxT, T - t0);
+        const size_t o = static_cast<size_t>(t0) * D->d_model;
+        DecodeParams P = make_params(B, D, x + o, out + o, residual ? residual + o : nullptr, n, ws);
+        if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
+        cudaError_t e = launch_router(P, s);
+        if (e == cudaSuccess) e = launch_gateup(P, s);
+        if (e == cudaSuccess) e = launch_down(P, s);
+        if (e != cudaSuccess) return QMOE_ERR_CUDA;
+    }
+    return QMOE_OK;
+}
+
+int qmoe_check_errors(void* ws, const qmoe_dims* D, uint32_t* err, qmoe_stream_t stream) {
+    (void)D;
+    if (!ws) return QMOE_ERR_WORKSPACE;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return QMOE_ERR_CUDA;
+    uint32_t w[2] = {0, 0xFFFFFFFFu};
+    uint32_t* ctrl = static_cast<uint32_t*>(ws);
+    if (cudaMemcpy(w, ctrl + CTRL_ERROR, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) return QMOE_ERR_CUDA;
+    const uint32_t clear[2] = {0u, 0xFFFFFFFFu};
+    if (cudaMemcpy(ctrl + CTRL_ERROR, clear, sizeof(clear), cudaMemcpyHostToDevice) != cudaSuccess)
+        return QMOE_ERR_CUDA;
+    if (err) { err[0] = w[0]; err[1] = w[1]; }
+    if (w[0] & EF_ROUTING) return QMOE_ERR_ROUTING;
+    if (w[0] & EF_NOT_NORMALIZED) return QMOE_ERR_NOT_NORMALIZED;
+    if (w[0] & EF_TIMEOUT) return QMOE_ERR_TIMEOUT;
+    return QMOE_OK;
+}
+
+int qmoe_synth_fill(void* dst, uint32_t type, uint64_t n, uint64_t seed, uint64_t stream_id, float sigma,
+                    qmoe_stream_t stream) {
+    const int be = blk_elems(static_cast<int>(type));
+    if (!dst || be == 0 || n % be) return QMOE_ERR_ARG;
+    return cuda_status(
+        launch_synth(dst, static_cast<int>(type), n / be, seed, stream_id, sigma, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,119 @@
+// Internal host/device structures of the qmoe library (not part of the C-ABI).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "../../include/qmoe.h"
+
+namespace qmoe {
+
+constexpr int kDecodeMaxT = 8;   // tokens per decode-path launch (larger T is sliced)
+constexpr int kMaxExperts = 256; // experts supported by the routing kernels
+constexpr int kMaxTopK = 32;
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// GGML block geometry (reference include/quantized.hpp:49-96).
+__host__ __device__ inline int blk_elems(int t) {
+    switch (t) {
+        case 0: case 1: case 30: return 1;
+        case 2: case 6: case 8: return 32;
+        case 12: case 13: case 14: return 256;
+        default: return 0;
+    }
+}
+__host__ __device__ inline int blk_bytes(int t) {
+    switch (t) {
+        case 0: return 4;
+        case 1: case 30: return 2;
+        case 2: return 18;
+        case 6: return 22;
+        case 8: return 34;
+        case 12: return 144;
+        case 13: return 176;
+        case 14: return 210;
+        default: return 0;
+    }
+}
+__host__ __device__ inline uint64_t row_bytes(int t, int K) {
+    int be = blk_elems(t);
+    return be ? static_cast<uint64_t>(K / be) * static_cast<uint64_t>(blk_bytes(t)) : 0;
+}
+
+// Workspace layout for a call with T tokens (all offsets 256-byte aligned).
+struct WsLayout {
+    size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, xq, hidden, hq, total;
+    size_t xq_stride;  // bytes per token of x planes: 3*d + (d/16)*8
+    size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
+    int H;             // max(F, Fs)
+};
+
+inline WsLayout ws_layout(const qmoe_dims& D, int T) {
+    WsLayout L{};
+    const int E = D.num_experts, k = D.top_k, d = D.d_model;
+    const int H = D.expert_dim > D.shared_dim ? D.expert_dim : D.shared_dim;
+    const int P = T * k;
+    const int nvec = P + T;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 256); return r; };
+    L.ctrl = take(64 * 4);
+    L.logits = take(sizeof(float) * static_cast<size_t>(T) * (E + 1));
+    L.topk_idx = take(sizeof(int32_t) * P);
+    L.topk_w = take(sizeof(float) * P);
+    L.offsets = take(sizeof(int32_t) * (E + 1));
+    L.perm = take(sizeof(int32_t) * P);
+    L.inv_perm = take(sizeof(int32_t) * P);
+    L.active = take(sizeof(int32_t) * (P < E ? P : E));
+    L.xq_stride = align_up(3 * static_cast<size_t>(d) + static_cast<size_t>(d / 16) * 8, 16);
+    L.xq = take(L.xq_stride * T);
+    L.H = H;
+    L.hidden = take(sizeof(float) * static_cast<size_t>(nvec) * H);
+    L.hq_stride = align_up(3 * static_cast<size_t>(H) + static_cast<size_t>(H / 16) * 8, 16);
+    L.hq = take(L.hq_stride * nvec);
+    L.total = o;
+    return L;
+}
+
+// One weight tensor as seen by the kernels.
+struct WArg {
+    const uint8_t* p;    // payload
+    const uint8_t* end;  // one past the last payload byte
+    int type;
+    int pad;
+};
+
+// Everything the decode kernels need (passed by value).
+struct DecodeParams {
+    int d, E, k, F, Fs, T;
+    int has_shared;
+    int num_sms;
+    // router (F32/F16/BF16) and the shared-expert gate vector
+    const uint8_t* router;
+    int router_type;
+    const uint8_t* sgate_inp;
+    int sgate_type;
+    const float* bias;
+    WArg gate, up, down, sgate, sup, sdown;
+    const float* x;  // [T][d]
+    float* out;      // [T][d]
+    const float* residual;
+    int32_t* out_idx;  // optional copies of the routing result
+    float* out_w;
+    // workspace
+    uint32_t* ctrl;
+    float* logits;
+    int32_t* topk_idx;
+    float* topk_w;
+    int32_t* offsets;
+    int32_t* perm;
+    int32_t* inv_perm;
+    int32_t* active;
+    uint8_t* xq;
+    size_t xq_stride;
+    float* hidden;
+    uint8_t* hq;
+    size_t hq_stride;
+    int H;
+};
+
+}  // namespace qmoe

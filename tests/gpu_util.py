@@ -1,0 +1,71 @@
+"""Helpers shared by the GPU parity tests: run the product through its C-ABI
+and the oracle / reference path on the same bytes."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from oracle import oracle as orc
+from qmoe import _lib, synth
+
+# BASELINE tolerance on outputs: max-abs 1e-3 / rel 1e-2 (allclose form)
+ATOL, RTOL = 1e-3, 1e-2
+
+
+def oracle_threads():
+    orc.set_threads(max(1, min(32, os.cpu_count() or 1)))
+
+
+class Run:
+    """One block_forward call through the C-ABI with its workspace."""
+
+    def __init__(self, blk: synth.Block, max_tokens: int = 8):
+        import torch
+        self.blk = blk
+        self.dims = blk.dims.c()
+        self.ws_bytes = _lib.lib().qmoe_workspace_size(ctypes.byref(self.dims), max_tokens)
+        assert self.ws_bytes > 0
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device="cuda")
+        _lib.check(_lib.lib().qmoe_workspace_init(self.ws.data_ptr(), self.ws_bytes, None))
+
+    def forward(self, x, residual=None):
+        import torch
+        T = x.shape[0]
+        out = torch.full_like(x, float("nan"))
+        c = self.blk.c()
+        st = _lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(self.dims), x.data_ptr(), out.data_ptr(),
+                                           None if residual is None else residual.data_ptr(), T,
+                                           self.ws.data_ptr(), self.ws_bytes, None)
+        _lib.check(st, "block_forward")
+        torch.cuda.synchronize()
+        return out
+
+    def view(self, which, T, count, dtype):
+        import torch
+        p = _lib.lib().qmoe_ws_view(self.ws.data_ptr(), ctypes.byref(self.dims), T, which)
+        off = p - self.ws.data_ptr()
+        nbytes = count * np.dtype(dtype).itemsize
+        return self.ws[off:off + nbytes].cpu().numpy().view(dtype)
+
+    def check_errors(self):
+        err = (ctypes.c_uint32 * 2)()
+        st = _lib.lib().qmoe_check_errors(self.ws.data_ptr(), ctypes.byref(self.dims), err, None)
+        return st, int(err[0]), int(err[1])
+
+
+def oracle_run(blk: synth.Block, x_host: np.ndarray):
+    return orc.moe_forward({n: blk.host_bytes(n) for n in synth.TENSORS}, blk.types, blk.dims, x_host,
+                           blk.host_bias())
+
+
+def assert_close(got, want, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    bad = ~np.isclose(got, want, atol=ATOL, rtol=RTOL)
+    if bad.any():
+        i = np.argwhere(bad)[0]
+        raise AssertionError(f"{what}: {int(bad.sum())} of {bad.size} outside atol={ATOL} rtol={RTOL}; "
+                             f"first at {tuple(i)}: got {got[tuple(i)]} want {want[tuple(i)]}; "
+                             f"max abs err {np.max(np.abs(got - want)):.3e}")

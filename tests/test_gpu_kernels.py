@@ -1,0 +1,262 @@
+"""GPU parity tests: every kernel through the C-ABI against the CPU oracle
+(and, where it adds a pin, against the reference's own CUDA path in
+oracle/_ref).  Routing ids, selection order and the permutation must be
+bit-exact; outputs within max-abs 1e-3 / rel 1e-2."""
+import ctypes
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from qmoe import _lib, synth
+from qmoe.quant import GgmlType, calculate_tensor_bytes
+
+from gpu_util import Run, assert_close, oracle_run, oracle_threads
+
+pytestmark = pytest.mark.gpu
+GOLD = json.loads((Path(__file__).parent / "golden" / "quant_kat.json").read_text())
+REAL = synth.Dims()  # 2048 / 256 / 8 / 512 / 512
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _setup(cuda):
+    oracle_threads()
+
+
+def _tensor(buf, ty, n):
+    return _lib.QmoeTensor(buf.data_ptr(), int(ty), 0, n)
+
+
+@pytest.mark.parametrize("ty", [GgmlType.F32, GgmlType.F16, GgmlType.BF16, GgmlType.Q4_0, GgmlType.Q5_0,
+                                GgmlType.Q8_0, GgmlType.Q4_K, GgmlType.Q5_K, GgmlType.Q6_K])
+def test_synth_device_matches_host(ty):
+    import torch
+    n = 256 * 64
+    h = np.empty(calculate_tensor_bytes(ty, n), dtype=np.uint8)
+    synth.fill(h, ty, n, 99, 5, 0.02)
+    d = torch.empty(h.size, dtype=torch.uint8, device="cuda")
+    synth.fill(d, ty, n, 99, 5, 0.02)
+    assert np.array_equal(d.cpu().numpy(), h)
+
+
+@pytest.mark.parametrize("name", sorted(GOLD["quant"]))
+def test_dequant_row_kat(name):
+    import torch
+    fx = GOLD["quant"][name]
+    raw = torch.tensor(list(bytes.fromhex(fx["bytes"])), dtype=torch.uint8, device="cuda")
+    exp = np.array(fx["expected"], dtype=np.float32)
+    out = torch.empty(exp.size, dtype=torch.float32, device="cuda")
+    t = _tensor(raw, fx["ggml_type"], exp.size)
+    _lib.check(_lib.lib().qmoe_dequant_row(ctypes.byref(t), out.data_ptr(), 0, exp.size, None))
+    torch.cuda.synchronize()
+    assert np.max(np.abs(out.cpu().numpy() - exp)) < 1e-6
+
+
+@pytest.mark.parametrize("ty", [GgmlType.F32, GgmlType.F16, GgmlType.BF16, GgmlType.Q4_0, GgmlType.Q5_0,
+                                GgmlType.Q8_0, GgmlType.Q4_K, GgmlType.Q5_K, GgmlType.Q6_K])
+@pytest.mark.parametrize("K", [2048, 768])
+def test_gemv_vs_oracle(ty, K):
+    import torch
+    if K % 256 and ty in (GgmlType.Q4_K, GgmlType.Q5_K, GgmlType.Q6_K):
+        pytest.skip("K-quant rows need K % 256 == 0")
+    rows, M, row0 = 96, 37, 11
+    n = rows * K
+    h = np.empty(calculate_tensor_bytes(ty, n), dtype=np.uint8)
+    synth.fill(h, ty, n, 5, 17, 0.02)
+    xh = np.random.default_rng(2).standard_normal(K).astype(np.float32)
+    w = torch.from_numpy(h).cuda()
+    x = torch.from_numpy(xh).cuda()
+    y = torch.empty(M, dtype=torch.float32, device="cuda")
+    t = _tensor(w, ty, n)
+    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, row0 * K, None))
+    torch.cuda.synchronize()
+    want = orc.gemv(h, int(ty), n, xh, M, K, row0 * K)
+    got = y.cpu().numpy()
+    if ty == GgmlType.F32:
+        assert np.array_equal(got, want)  # same reduction order, bit for bit
+    else:
+        assert np.allclose(got, want, rtol=1e-5, atol=1e-6)
+    if orc.ref_available():
+        yr = torch.empty(M, dtype=torch.float32, device="cuda")
+        st = orc.ref_lib().ref_gemv(w.data_ptr(), int(ty), n, x.data_ptr(), yr.data_ptr(), M, K, row0 * K, None)
+        assert st == 0
+        torch.cuda.synchronize()
+        ref = yr.cpu().numpy()
+        if ty in (GgmlType.F32, GgmlType.F16, GgmlType.BF16):
+            assert np.array_equal(got, ref)
+            assert np.array_equal(want, ref)
+        else:
+            assert np.allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def _router_block(dims, bias, seed):
+    return synth.Block(dims, synth.Q4K_TYPES, seed=seed, device="cuda", bias=bias)
+
+
+@pytest.mark.parametrize("T,bias,seed", [(1, False, 1), (3, False, 2), (8, False, 3), (8, True, 4), (5, True, 5)])
+def test_router_topk_bit_exact(T, bias, seed):
+    import torch
+    blk = _router_block(REAL, bias, seed)
+    r = Run(blk)
+    x = synth.inputs(T, REAL.d_model, seed=seed, tag=7)
+    idx = torch.empty((T, REAL.top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, REAL.top_k), dtype=torch.float32, device="cuda")
+    c = blk.c()
+    _lib.check(_lib.lib().qmoe_router_topk(ctypes.byref(c), ctypes.byref(r.dims), x.data_ptr(), T, idx.data_ptr(),
+                                           w.data_ptr(), r.ws.data_ptr(), r.ws_bytes, None))
+    torch.cuda.synchronize()
+    E, k = REAL.num_experts, REAL.top_k
+    logits = r.view(_lib.WS_LOGITS, T, T * (E + 1), np.float32).reshape(T, E + 1)
+    xh = x.cpu().numpy()
+    router = blk.host_bytes("router")
+    bh = blk.host_bias()
+    for t in range(T):
+        want = orc.gemv(router, 0, E * REAL.d_model, xh[t], E, REAL.d_model)
+        if bh is not None:
+            want = (want + bh).astype(np.float32)
+        assert np.array_equal(logits[t, :E], want), t  # bit-exact logits
+        oi, ow = orc.topk(want, k)
+        assert idx[t].cpu().numpy().tolist() == oi.tolist()
+        assert np.allclose(w[t].cpu().numpy(), ow, rtol=2e-6, atol=0)
+        sg = orc.gemv(blk.host_bytes("shared_gate_inp"), 0, REAL.d_model, xh[t], 1, REAL.d_model)
+        assert logits[t, E] == sg[0]
+        if orc.ref_available():  # the reference's own top-k kernel on the same logits
+            lt = torch.from_numpy(np.ascontiguousarray(logits[t, :E])).cuda()
+            ri = torch.empty(k, dtype=torch.int32, device="cuda")
+            rw = torch.empty(k, dtype=torch.float32, device="cuda")
+            assert orc.ref_lib().ref_topk(lt.data_ptr(), ri.data_ptr(), rw.data_ptr(), E, k, None) == 0
+            torch.cuda.synchronize()
+            assert ri.cpu().numpy().tolist() == idx[t].cpu().numpy().tolist()
+            assert np.array_equal(rw.cpu().numpy(), w[t].cpu().numpy())  # same expf, same order
+    st, flags, tok = r.check_errors()
+    assert st == 0 and flags == 0
+
+
+def test_routing_kat_through_router_kernel():
+    """tests/kernel_tests.cu:424-453: logits {-2,.4,3,1.2,-.7,2.1}, K=3 -> {2,5,3}."""
+    import torch
+    g = GOLD["routing"]
+    dims = synth.Dims(d_model=256, num_experts=6, top_k=3, expert_dim=256, shared_dim=256)
+    blk = synth.Block(dims, synth.Q4K_TYPES, seed=1, device="cuda")
+    W = np.zeros((6, 256), dtype=np.float32)
+    W[:, 0] = g["logits"]
+    blk.buf["router"].copy_(torch.from_numpy(W.view(np.uint8).ravel()))
+    x = torch.zeros((1, 256), dtype=torch.float32, device="cuda")
+    x[0, 0] = 1.0
+    r = Run(blk)
+    idx = torch.empty(3, dtype=torch.int32, device="cuda")
+    w = torch.empty(3, dtype=torch.float32, device="cuda")
+    c = blk.c()
+    _lib.check(_lib.lib().qmoe_router_topk(ctypes.byref(c), ctypes.byref(r.dims), x.data_ptr(), 1, idx.data_ptr(),
+                                           w.data_ptr(), r.ws.data_ptr(), r.ws_bytes, None))
+    torch.cuda.synchronize()
+    assert idx.cpu().numpy().tolist() == g["ids"]
+    wh = w.cpu().numpy()
+    assert np.all(wh > 0) and abs(float(wh.sum()) - 1) < g["sum_tol"] and wh[0] > wh[1] > wh[2]
+
+
+CASES = [
+    ("config1_q4k_T4", REAL, synth.Q4K_TYPES, False, 4),
+    ("q4k_T1", REAL, synth.Q4K_TYPES, False, 1),
+    ("mixed_bias_T1", REAL, synth.MIXED_TYPES, True, 1),
+    ("mixed_bias_T2", REAL, synth.MIXED_TYPES, True, 2),
+    ("mixed_bias_T8", REAL, synth.MIXED_TYPES, True, 8),
+    ("small_q5k_q80", synth.Dims(512, 64, 6, 256, 512),
+     {**synth.Q4K_TYPES, "gate_exps": GgmlType.Q5_K, "up_exps": GgmlType.Q5_K, "down_exps": GgmlType.Q8_0,
+      "shared_gate": GgmlType.Q6_K, "shared_up": GgmlType.Q6_K, "shared_down": GgmlType.Q5_K}, False, 3),
+    ("small_q6k_F1024", synth.Dims(1024, 32, 4, 1024, 256),
+     {**synth.Q4K_TYPES, "down_exps": GgmlType.Q6_K, "shared_down": GgmlType.Q6_K}, True, 5),
+]
+
+
+@pytest.mark.parametrize("name,dims,types,bias,T", CASES, ids=[c[0] for c in CASES])
+def test_block_forward_vs_oracle(name, dims, types, bias, T):
+    blk = synth.Block(dims, types, seed=hash(name) & 0xFFFF, device="cuda", bias=bias)
+    r = Run(blk)
+    x = synth.inputs(T, dims.d_model, seed=77, tag=T)
+    out = r.forward(x).cpu().numpy()
+    want = oracle_run(blk, x.cpu().numpy())
+    assert np.all(want["status"] == 0)
+    k = dims.top_k
+    idx = r.view(_lib.WS_TOPK_IDX, T, T * k, np.int32).reshape(T, k)
+    assert np.array_equal(idx, want["idx"])
+    wts = r.view(_lib.WS_TOPK_W, T, T * k, np.float32).reshape(T, k)
+    assert np.allclose(wts, want["w"], rtol=2e-6, atol=0)
+    H = max(dims.expert_dim, dims.shared_dim)
+    hid = r.view(_lib.WS_HIDDEN, T, (T * k + T) * H, np.float32).reshape(T * k + T, H)
+    F, Fs = dims.expert_dim, dims.shared_dim
+    assert_close(hid[: T * k, :F].reshape(T, k, F), want["h"], f"{name} hidden")
+    assert_close(hid[T * k:, :Fs], want["hs"], f"{name} shared hidden")
+    assert_close(out, want["out"], f"{name} out")
+    # permutation = stable order by (expert, token, slot)
+    offs, perm, _ = orc.dispatch(want["idx"], dims.num_experts)
+    assert np.array_equal(r.view(_lib.WS_OFFSETS, T, dims.num_experts + 1, np.int32), offs)
+    assert np.array_equal(r.view(_lib.WS_PERM, T, T * k, np.int32)[: perm.size], perm)
+    st, flags, _ = r.check_errors()
+    assert st == 0 and flags == 0
+
+
+def test_block_forward_vs_reference_cuda_path():
+    """Config 1 through the reference's own MoeLayer::forward (oracle/_ref):
+    pins the oracle to the reference and the product to both."""
+    import torch
+    if not orc.ref_available():
+        pytest.skip("oracle/_ref not built")
+    dims, T = REAL, 4
+    blk = synth.Block(dims, synth.Q4K_TYPES, seed=4242, device="cuda")
+    x = synth.inputs(T, dims.d_model, seed=4242, tag=1)
+    ref_out = torch.full_like(x, float("nan"))
+    names = synth.TENSORS
+    orc.ref_moe_forward(dims, [blk.buf[n].data_ptr() for n in names], [blk.types[n] for n in names],
+                        [dims.elements(n) for n in names], x.data_ptr(), ref_out.data_ptr(), T)
+    torch.cuda.synchronize()
+    ref = ref_out.cpu().numpy()
+    want = oracle_run(blk, x.cpu().numpy())
+    # oracle vs reference: same formulas and reduction order; only expf/contraction may differ
+    assert np.allclose(want["out"], ref, rtol=1e-5, atol=1e-6)
+    got = Run(blk).forward(x).cpu().numpy()
+    assert_close(got, ref, "product vs reference CUDA path")
+
+
+def test_slabs_residual_and_nonfinite_token():
+    import torch
+    dims, T = REAL, 12  # two decode slabs (8 + 4)
+    blk = synth.Block(dims, synth.Q4K_TYPES, seed=9, device="cuda")
+    r = Run(blk)
+    x = synth.inputs(T, dims.d_model, seed=9, tag=12).clone()
+    x[10, 5] = float("nan")
+    resid = synth.inputs(T, dims.d_model, seed=10, tag=13)
+    out = r.forward(x, residual=resid).cpu().numpy()
+    xh = x.cpu().numpy()
+    want = oracle_run(blk, xh)
+    assert want["status"].tolist() == [0] * 10 + [10, 0]
+    good = [t for t in range(T) if t != 10]
+    assert_close(out[good], want["out"][good] + resid.cpu().numpy()[good], "residual")
+    assert np.all(np.isnan(out[10]))
+    st, flags, tok = r.check_errors()
+    assert st == _lib.QMOE_ERR_ROUTING and flags & 1 and tok == 2  # token 2 of the second slab
+    st, flags, tok = r.check_errors()  # cleared
+    assert st == 0 and flags == 0
+
+
+def test_dispatch_vs_oracle():
+    import torch
+    rng = np.random.default_rng(3)
+    T, k, E = 4096, 8, 256
+    p = 1.0 / np.arange(1, E + 1) ** 1.1
+    p /= p.sum()
+    idx = np.stack([rng.choice(E, k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    offs, perm, inv = orc.dispatch(idx, E)
+    d_idx = torch.from_numpy(idx).cuda()
+    o = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+    pm = torch.empty(T * k, dtype=torch.int32, device="cuda")
+    iv = torch.empty(T * k, dtype=torch.int32, device="cuda")
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_dispatch(d_idx.data_ptr(), T, k, E, o.data_ptr(), pm.data_ptr(), iv.data_ptr(),
+                                        ws.data_ptr(), ws.numel(), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(o.cpu().numpy(), offs)
+    assert np.array_equal(pm.cpu().numpy(), perm)
+    assert np.array_equal(iv.cpu().numpy(), inv)
