@@ -5,9 +5,11 @@ Workload: decode, batch 1, through the 40 MoE blocks of a
 Qwen3.5-35B-A3B-shaped stack (hidden 2048, 256 experts, top-8 + 1 shared,
 expert FFN 512), random Q4_K expert weights per layer (N(0,0.02), seeded),
 F32 router and shared-gate vector, token vectors ~N(0,1) from a 128-token
-seeded pool.  One step = one token through all 40 blocks; block l+1 reads
-block l's output plus its input (the residual stream), so the blocks run in
-sequence like in the model.  Metric: microseconds per token per MoE block
+seeded pool.  One step = one token through all 40 blocks; each block is the
+MoE half of a decoder layer as model.cpp:208-211 runs it -- RMSNorm of the
+residual stream, MoE block, residual add -- with the norm and the add fused
+into the block's kernels, so block l+1 reads block l's output and the 40
+blocks run in sequence like in the model.  Metric: microseconds per token per MoE block
 (lower is better); ``value`` is whole-job: time / (steps * 40 * n_gpus).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -41,6 +43,7 @@ UNIT = "us/token"
 N_LAYERS = 40
 POOL = 128
 SEED = 1234
+EPS = 1e-6
 # algorithmic bytes of one Q4_K MoE block for one token (router F32 + 8 experts
 # x (gate+up+down) + shared gate/up/down + shared gate vector + x in/out)
 BLOCK_BYTES = 2_097_152 + 8 * 1_769_472 + 1_769_472 + 8_192 + 16_384
@@ -72,7 +75,7 @@ class ClockSampler(threading.Thread):
     def __init__(self, dev_index: int):
         super().__init__(daemon=True)
         self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -89,7 +92,7 @@ class ClockSampler(threading.Thread):
         nv = self.nv
         get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
             nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        while not self._stop.is_set():
+        while not self._halt.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
                 r = get_r(self.h)
@@ -101,7 +104,7 @@ class ClockSampler(threading.Thread):
             time.sleep(0.002)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         self.join(timeout=2)
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
@@ -136,19 +139,21 @@ def run_ours(args):
     blocks = [synth.Block(dims, synth.Q4K_TYPES, seed=SEED, layer=l, device="cuda") for l in range(L)]
     cblocks = [b.c() for b in blocks]
     inputs = synth.inputs(POOL, dims.d_model, seed=SEED, tag=2)
+    gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")  # pre-MoE RMSNorm weight
     nws = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), 1)
     ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
     _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), nws, None))
     xbuf = torch.empty((1, dims.d_model), dtype=torch.float32, device="cuda")
     bufs = [torch.empty_like(xbuf), torch.empty_like(xbuf)]
-    fwd = _lib.lib().qmoe_block_forward
+    fwd = _lib.lib().qmoe_block_forward_prenorm
 
     def step(stream_ptr):
+        # residual stream r: r <- r + MoE_l(rmsnorm(r) * gamma), layer by layer
         x = xbuf
         for l in range(L):
             out = bufs[l % 2]
-            st = fwd(ctypes.byref(cblocks[l]), ctypes.byref(dc), x.data_ptr(), out.data_ptr(), x.data_ptr(), 1,
-                     ws.data_ptr(), nws, stream_ptr)
+            st = fwd(ctypes.byref(cblocks[l]), ctypes.byref(dc), x.data_ptr(), gamma.data_ptr(), EPS, out.data_ptr(),
+                     1, ws.data_ptr(), nws, stream_ptr)
             if st:
                 raise RuntimeError(f"block_forward layer {l}: {_lib.status_string(st)}")
             x = out
@@ -252,6 +257,13 @@ def _check_errors(_lib, ws, dc):
     return st, int(err[0]), int(err[1])
 
 
+def _ws_array(_lib, ws, dc, which, count, dtype):
+    import numpy as np
+    p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), 1, which)
+    off = p - ws.data_ptr()
+    return ws[off:off + count * np.dtype(dtype).itemsize].cpu().numpy().view(dtype)
+
+
 def cpu_baseline(args, blocks, inputs, dims, dc, ws, nws):
     """The oracle (C restatement of the reference MoE path) on the host cores
     over a bounded sample, plus a parity gate on the same sample."""
@@ -267,24 +279,25 @@ def cpu_baseline(args, blocks, inputs, dims, dc, ws, nws):
     x = inputs[0:1].clone()
     out = torch.empty_like(x)
     secs, ids_ok, max_err, within = 0.0, True, 0.0, True
+    gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")
     for l in range(S):
         c = blocks[l].c()
-        _lib.check(_lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(), out.data_ptr(),
-                                                 None, 1, ws.data_ptr(), nws, None))
+        _lib.check(_lib.lib().qmoe_block_forward_prenorm(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(),
+                                                         gamma.data_ptr(), EPS, out.data_ptr(), 1, ws.data_ptr(),
+                                                         nws, None))
         torch.cuda.synchronize()
-        p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), 1, _lib.WS_TOPK_IDX)
-        off = p - ws.data_ptr()
-        gid = ws[off:off + 4 * dims.top_k].cpu().numpy().view(np.int32)
+        gid = _ws_array(_lib, ws, dc, _lib.WS_TOPK_IDX, dims.top_k, np.int32)
+        xin = _ws_array(_lib, ws, dc, _lib.WS_INPUT, dims.d_model, np.float32)  # rmsnorm(r) as the block saw it
         host = {n: blocks[l].host_bytes(n) for n in synth.TENSORS}
-        xh = x.cpu().numpy()
         t0 = time.perf_counter()
-        res = orc.moe_forward(host, blocks[l].types, dims, xh)
+        res = orc.moe_forward(host, blocks[l].types, dims, xin)
         secs += time.perf_counter() - t0
         got = out.cpu().numpy()
+        want = x.cpu().numpy() + res["out"]
         ids_ok &= bool(np.array_equal(gid, res["idx"][0]))
-        max_err = max(max_err, float(np.max(np.abs(got - res["out"]))))
-        within &= bool(np.all(np.isclose(got, res["out"], atol=1e-3, rtol=1e-2)))
-        x = (x + out).contiguous()  # residual stream, as in the timed run
+        max_err = max(max_err, float(np.max(np.abs(got - want))))
+        within &= bool(np.all(np.isclose(got, want, atol=1e-3, rtol=1e-2)))
+        x = out.clone()  # the residual stream, as in the timed run
     cpu = {"value": round(secs / S * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
            "sample": f"{S} MoE blocks x 1 token (layers 0..{S - 1} of the config-2 stack, step 0), "
                      "oracle/qmoe_oracle.c, OpenMP over output rows"}

@@ -101,7 +101,8 @@ enum qmoe_ws_buffer {
     QMOE_WS_PERM = 4,     /* int32 [T*k]  pair p = t*k + j at each permuted position */
     QMOE_WS_INV_PERM = 5, /* int32 [T*k]  permuted position of each pair (-1: invalid) */
     QMOE_WS_HIDDEN = 6,   /* float [T*k + T][max(F,Fs)] silu(gate)*up: routed pairs, then shared per token */
-    QMOE_WS_ERROR = 7     /* uint32 [4]: error flags, first failing token, spare */
+    QMOE_WS_ERROR = 7,    /* uint32 [4]: error flags, first failing token, spare */
+    QMOE_WS_INPUT = 8     /* float [T][d] the block input as the router saw it (after the fused norm) */
 };
 
 /* ABI version of this header (bumped on any incompatible change). */
@@ -160,10 +161,27 @@ QMOE_API int qmoe_block_forward(const qmoe_block* blk, const qmoe_dims* dims, co
                        const float* residual, int T,
                        void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 
+/* The MoE half of a decoder layer (model.cpp:208-211 of the reference:
+ * rmsnorm_forward, MoeLayer::forward, residual_add) in the same three
+ * launches: out = resid + MoE(rmsnorm(resid) * norm_weight), with the
+ * reference's RMSNorm arithmetic (src/cuda/ops.cu:25-65: sum of squares in
+ * the GEMV's reduction order, rsqrtf(mean + eps), (x * scale) * weight). */
+QMOE_API int qmoe_block_forward_prenorm(const qmoe_block* blk, const qmoe_dims* dims, const float* resid,
+                                        const float* norm_weight, float eps, float* out, int T,
+                                        void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
 /* Waits for `stream`, reads the device error word of `workspace` into
  * err[0..1] (flags, first failing token) and clears it.  Returns the status
  * the flags map to (QMOE_OK if none). */
 QMOE_API int qmoe_check_errors(void* workspace, const qmoe_dims* dims, uint32_t* err, qmoe_stream_t stream);
+
+/* Phase tracer (profiling): while a device buffer of qmoe_trace_bytes() is
+ * registered, the decode kernels write %globaltimer stamps (ns) of their
+ * phases into it, laid out [kernel 0..2][CTA 0..159][event 0..7] (uint64;
+ * kernel 0 router, 1 gate/up, 2 down).  Later launches overwrite earlier
+ * ones.  NULL disables it (the default). */
+QMOE_API int qmoe_trace_enable(uint64_t* device_buffer, size_t bytes);
+QMOE_API size_t qmoe_trace_bytes(void);
 
 /* Clears the workspace control words (call once after allocating it). */
 QMOE_API int qmoe_workspace_init(void* workspace, size_t workspace_bytes, qmoe_stream_t stream);

@@ -56,6 +56,8 @@ def lib() -> ctypes.CDLL:
                                            c_void_p]
         L.or_dispatch.restype = c_int
         L.or_dispatch.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
+        L.or_rmsnorm.restype = None
+        L.or_rmsnorm.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_float]
         L.or_set_threads.restype = None
         L.or_set_threads.argtypes = [c_int]
         L.or_max_threads.restype = c_int
@@ -90,6 +92,14 @@ def gemv(data: np.ndarray, ggml_type: int, n: int, x: np.ndarray, M: int, K: int
     if st:
         raise RuntimeError(f"oracle gemv status {st}")
     return y
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().or_rmsnorm(_p(x), _p(w), _p(out), x.size, eps)
+    return out
 
 
 def topk(logits: np.ndarray, k: int):
@@ -162,6 +172,8 @@ def ref_lib() -> ctypes.CDLL:
         L.ref_gemv.argtypes = [c_void_p, c_int, c_uint64, c_void_p, c_void_p, c_int, c_int, c_uint64, c_void_p]
         L.ref_dequantize_row.restype = c_int
         L.ref_dequantize_row.argtypes = [c_void_p, c_int, c_uint64, c_void_p, c_int, c_int, c_void_p]
+        L.ref_rmsnorm.restype = c_int
+        L.ref_rmsnorm.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p]
         L.ref_topk.restype = c_int
         L.ref_topk.argtypes = [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]
         L.ref_moe_forward.restype = c_int

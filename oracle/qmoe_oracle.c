@@ -19,6 +19,9 @@
  *   - or_add                src/cuda/moe.cu:76-81   (out += a*x, one fma)
  *   - or_shared_add         src/cuda/moe.cu:90-96   (out += x*sigmoid(g))
  *   - or_moe_forward        src/layer_moe.cpp:95-155 (validation :114-124)
+ *   - or_rmsnorm            src/cuda/ops.cu:25-65 (pre-MoE norm, model.cpp:208);
+ *                           the reference scales by rsqrtf, a hardware
+ *                           approximation, here 1/sqrtf (within 2 ulp)
  *   - or_dispatch           no counterpart in the reference (single token);
  *                           stable counting sort of (token, slot) pairs by
  *                           expert, key order (expert, token, slot).
@@ -191,6 +194,24 @@ OR_EXPORT int or_gemv(const uint8_t* w, int type, uint64_t num_elements, const f
     for (int row = 0; row < M; ++row)
         y[row] = or_gemv_row(w, type, x, K, element_offset + (uint64_t)row * (uint64_t)K);
     return OR_OK;
+}
+
+/* ops.cu:25-65: sum of squares with the 256-thread GEMV reduction structure
+ * (fmaf chain per thread, shuffle trees), scale = 1/sqrt(mean + eps) (the
+ * reference uses rsqrtf), out = (x * scale) * w. */
+OR_EXPORT void or_rmsnorm(const float* x, const float* w, float* out, int n, float eps) {
+    float part[256];
+    for (int t = 0; t < 256; ++t) {
+        float s = 0.0f;
+        for (int i = t; i < n; i += 256) s = fmaf(x[i], x[i], s);
+        part[t] = s;
+    }
+    float warp[32];
+    for (int wi = 0; wi < 8; ++wi) warp[wi] = or_tree32(part + 32 * wi);
+    for (int i = 8; i < 32; ++i) warp[i] = 0.0f;
+    float ss = or_tree32(warp);
+    float scale = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = 0; i < n; ++i) out[i] = (x[i] * scale) * w[i];
 }
 
 /* matmul_q4.cu:209-227 */

@@ -4,6 +4,7 @@
 // buffers as the product.  TEST INFRASTRUCTURE ONLY.
 #include "layer_moe.hpp"
 #include "matmul_q4.hpp"
+#include "ops.hpp"
 #include <cstring>
 #include <exception>
 #include <string>
@@ -46,6 +47,14 @@ int ref_dequantize_row(const void* w, int type, unsigned long long n, float* out
     try {
         qwen::QuantTensor t = make_tensor("w", w, type, n);
         qwen::dequantize_row(t, out, row, cols, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+// rmsnorm_forward (ops.cu:143-154): out = x * rsqrt(mean(x^2) + eps) * weight.
+int ref_rmsnorm(const float* x, const float* weight, float* out, int n, float eps, void* stream) {
+    try {
+        qwen::rmsnorm_forward(x, weight, out, n, eps, static_cast<cudaStream_t>(stream));
         return 0;
     } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
 }

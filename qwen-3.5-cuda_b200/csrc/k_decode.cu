@@ -1,21 +1,27 @@
-// Decode-path kernels of the MoE block (T <= kDecodeMaxT tokens per launch).
+// Decode-path kernels of the MoE block (T <= kDecodeMaxT tokens per launch),
+// three launches per block chained with programmatic dependent launch (PDL):
+// every kernel fetches the weights that do not depend on the previous
+// kernel's output before it waits for that output.
 //
-//   k_router   router logits in the reference's exact F32 reduction order
+//   k_router   [prologue: router rows into registers]  optional fused
+//              pre-MoE RMSNorm (src/cuda/ops.cu:25-65, same arithmetic),
+//              router logits in the reference's exact F32 reduction order
 //              (src/cuda/matmul_q4.cu:140-167), the shared-expert gate logit,
-//              24-bit activation planes of x, then -- in the last CTA to
-//              finish -- top-k + softmax over the selected logits
-//              (src/cuda/moe.cu:7-52), the host checks of
-//              src/layer_moe.cpp:114-124 as a device error word, and the
-//              stable token->expert permutation.
-//   k_gateup   gate and up rows of every active expert and of the shared
-//              expert, staged into shared memory with 1-D bulk copies (TMA)
-//              from the GGUF payload in place, dp4a dot products against the
-//              activation planes, silu(g)*u (src/cuda/moe.cu:61-67), and the
-//              24-bit planes of the result.
-//   k_down     down rows of every active expert and the shared expert for a
-//              slice of output rows, then the combine in selection order
-//              j = 0..k-1 (src/cuda/moe.cu:76-81) and the sigmoid-gated
-//              shared expert (src/cuda/moe.cu:90-96), optional residual.
+//              the block input and its 24-bit planes; the last CTA selects
+//              the experts (src/cuda/moe.cu:7-52), checks the result on the
+//              device (src/layer_moe.cpp:114-124) and writes the stable
+//              token->expert permutation as a packed schedule.
+//   k_gateup   [prologue: shared-expert gate/up rows -> shared memory (TMA)]
+//              routed gate/up rows of every active expert, staged with 1-D
+//              bulk copies straight from the GGUF payload, dp4a dot products
+//              against 24-bit planes of the block input (written once by the
+//              router), silu(g)*u (moe.cu:61-67), and the 24-bit planes of
+//              each 32-row block of silu(g)*u for the down kernel.
+//   k_down     [prologue: shared-expert and routed down rows -> shared memory]
+//              planes of silu(g)*u (one bulk copy), down products, then the
+//              combine in selection order j = 0..k-1 (moe.cu:76-81) and the
+//              sigmoid-gated shared expert (moe.cu:90-96), optional residual.
+#include <algorithm>
 #include "qmoe_dev.cuh"
 #include "qmoe_units.cuh"
 #include "qmoe_internal.h"
@@ -23,6 +29,13 @@
 namespace qmoe {
 
 constexpr unsigned FULL = 0xffffffffu;
+
+// Phase timestamp (one thread per CTA) when a trace buffer is registered.
+#define QMOE_TRACE(P, kind, ev)                                                                          \
+    do {                                                                                                 \
+        if ((P).trace && blockIdx.x < kTraceCtas)                                                        \
+            (P).trace[((kind) * kTraceCtas + blockIdx.x) * kTraceEvents + (ev)] = gtimer();             \
+    } while (0)
 
 // ---------------------------------------------------------------------------
 // Router
@@ -50,16 +63,13 @@ __device__ __forceinline__ void load_router_row(float4 (&w)[CH][2], const uint8_
         }
 }
 
-// One logit with the reference's order.  Lane L plays the 8 "threads"
-// t = 4L + c + 128h (c = 0..3, h = 0..1) of the reference's 256-thread block:
-// each keeps the fmaf chain over k = t, t+256, ...  The reference's warp
-// w' = L/8 + 4h holds these values at positions 4*(L%8) + c, so its shuffle
-// tree (offsets 16, 8, 4, 2, 1) is shuffles by 4, 2, 1 lanes followed by the
-// in-lane pairs (c, c+2), (c, c+1).  Warp 0's final tree over the 8 warp
-// sums p0..p7 (lanes 8..31 zero) is ((q0+q4)+(q2+q6))+((q1+q5)+(q3+q7)) with
-// q = (p + 0) + 0.  Valid in lane 0.
+// Activations produced by the previous kernel: read through L2 (ld.global.cg).
+__device__ __forceinline__ float4 ld_act4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Dot product of two register-resident vectors in the router lane layout
+// (lane L holds elements 256i + 128h + 4L + c) with the reference's order.
 template <int CH>
-__device__ __forceinline__ float router_dot(const float4 (&w)[CH][2], const float* x, int lane) {
+__device__ __forceinline__ float reg_dot(const float4 (&w)[CH][2], const float4 (&x)[CH][2]) {
     float acc[2][4];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh)
@@ -69,11 +79,10 @@ __device__ __forceinline__ float router_dot(const float4 (&w)[CH][2], const floa
     for (int i = 0; i < CH; ++i)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-            const float4 xv = __ldg(reinterpret_cast<const float4*>(x + 256 * i + 128 * hh + 4 * lane));
-            acc[hh][0] = __fmaf_rn(w[i][hh].x, xv.x, acc[hh][0]);
-            acc[hh][1] = __fmaf_rn(w[i][hh].y, xv.y, acc[hh][1]);
-            acc[hh][2] = __fmaf_rn(w[i][hh].z, xv.z, acc[hh][2]);
-            acc[hh][3] = __fmaf_rn(w[i][hh].w, xv.w, acc[hh][3]);
+            acc[hh][0] = __fmaf_rn(w[i][hh].x, x[i][hh].x, acc[hh][0]);
+            acc[hh][1] = __fmaf_rn(w[i][hh].y, x[i][hh].y, acc[hh][1]);
+            acc[hh][2] = __fmaf_rn(w[i][hh].z, x[i][hh].z, acc[hh][2]);
+            acc[hh][3] = __fmaf_rn(w[i][hh].w, x[i][hh].w, acc[hh][3]);
         }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh)
@@ -99,50 +108,120 @@ __device__ __forceinline__ float router_dot(const float4 (&w)[CH][2], const floa
                      __fadd_rn(__fadd_rn(q[1], q[5]), __fadd_rn(q[3], q[7])));
 }
 
+// The block input of one token in registers: x, or with the fused norm
+// (ops.cu:33-64) (x * rsqrt(mean(x^2) + eps)) * weight -- the sum of squares
+// has exactly the GEMV's thread/shuffle structure, so reg_dot(x, x) is it.
+template <int CH>
+__device__ __forceinline__ void load_input(float4 (&xr)[CH][2], const DecodeParams& P, const float* x, int lane) {
+#pragma unroll
+    for (int i = 0; i < CH; ++i)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) xr[i][hh] = ld_act4(x + 256 * i + 128 * hh + 4 * lane);
+    if (P.prenorm) {
+        const float ss = reg_dot<CH>(xr, xr);
+        const float sc = rsqrtf(ss / static_cast<float>(P.d) + P.eps);
+#pragma unroll
+        for (int i = 0; i < CH; ++i)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const float4 nv = __ldg(reinterpret_cast<const float4*>(P.norm_w + 256 * i + 128 * hh + 4 * lane));
+                xr[i][hh].x = __fmul_rn(__fmul_rn(xr[i][hh].x, sc), nv.x);
+                xr[i][hh].y = __fmul_rn(__fmul_rn(xr[i][hh].y, sc), nv.y);
+                xr[i][hh].z = __fmul_rn(__fmul_rn(xr[i][hh].z, sc), nv.z);
+                xr[i][hh].w = __fmul_rn(__fmul_rn(xr[i][hh].w, sc), nv.w);
+            }
+    }
+}
+
 __device__ __forceinline__ int router_esize(int type) { return type == T_F32 ? 4 : 2; }
 
-// Top-k + softmax + validation for every token, then the permutation.
-// Runs in the single CTA that finished the router last (RT_WARPS warps).
-__device__ void topk_and_dispatch(const DecodeParams& P) {
-    __shared__ int s_cnt[kMaxExperts];
-    __shared__ int s_cur[kMaxExperts];
+// 24-bit planes (qmoe_dev.cuh) of four consecutive elements e0..e0+3 per lane,
+// where the 8 lanes 8m..8m+7 of a warp hold one 32-block: block maximum over
+// the 8 lanes, 16-run sums over 4 lanes, one 32-bit store per plane.
+__device__ __forceinline__ void write_planes4(float4 v, uint8_t* base, int K, int e0, int lane) {
+    uint32_t ab = max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                      max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ab = max(ab, __shfl_xor_sync(FULL, ab, o));
+    float s16 = (v.x + v.y) + (v.z + v.w);
+    s16 += __shfl_xor_sync(FULL, s16, 1);
+    s16 += __shfl_xor_sync(FULL, s16, 2);
+    const bool bad = ab >= 0x7F800000u;
+    const uint32_t eb = ab >> 23;
+    int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
+    sh = sh > 126 ? 126 : sh;
+    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
+    float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+    if (bad) scale = __uint_as_float(0x7FC00000u);
+    const uint32_t X0 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.x * mul));
+    const uint32_t X1 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.y * mul));
+    const uint32_t X2 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.z * mul));
+    const uint32_t X3 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.w * mul));
+    const uint32_t w0 = (X0 & 255u) | ((X1 & 255u) << 8) | ((X2 & 255u) << 16) | ((X3 & 255u) << 24);
+    const uint32_t w1 = ((X0 >> 8) & 255u) | (((X1 >> 8) & 255u) << 8) | (((X2 >> 8) & 255u) << 16) | (((X3 >> 8) & 255u) << 24);
+    const uint32_t w2 = ((X0 >> 16) & 255u) | (((X1 >> 16) & 255u) << 8) | (((X2 >> 16) & 255u) << 16) | (((X3 >> 16) & 255u) << 24);
+    *reinterpret_cast<uint32_t*>(base + e0) = w0;
+    *reinterpret_cast<uint32_t*>(base + K + e0) = w1;
+    *reinterpret_cast<uint32_t*>(base + 2 * K + e0) = w2;
+    if ((lane & 3) == 0) reinterpret_cast<float2*>(base + 3 * K)[e0 >> 4] = make_float2(scale, s16);
+}
+
+// Order-preserving key of a finite float (-0 and +0 map to the same key).
+__device__ __forceinline__ uint32_t fkey(float v) {
+    const uint32_t u = __float_as_uint(v + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Top-k + softmax + validation for every token, then the permutation and the
+// packed schedule.  Runs in the single CTA that finished the router last.
+//
+// Selection (moe.cu:19-36): k rounds of "largest remaining logit, lowest index
+// on ties": each lane offers its best unused logit (ascending scan with a
+// strict >, so its lowest index among equals), one redux picks the largest
+// key, a second the lowest expert id among lanes holding that key.
+__device__ void topk_and_schedule(const DecodeParams& P) {
+    constexpr int MP = kDecodeMaxT * kMaxTopK;
+    __shared__ int s_idx[MP];
+    __shared__ int s_rank[MP];
+    __shared__ int s_perm[MP];
+    __shared__ int s_first[MP + 1];
+    __shared__ int s_nact;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int E = P.E, k = P.k, LS = E + 1;
+    const int NP = P.T * k;
 
     for (int t = warp; t < P.T; t += RT_WARPS) {
         float v[8];
-        bool finite = true;
+        uint32_t key[8];
+        uint32_t amax = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane + 32 * i;
-            v[i] = e < E ? __ldcg(P.logits + t * LS + e) : -INFINITY;
-            if (e < E && !isfinite(v[i])) finite = false;
+            v[i] = e < E ? __ldcg(P.logits + t * LS + e) : 0.0f;
+            key[i] = e < E ? fkey(v[i]) : 0u;
+            amax = max(amax, e < E ? (__float_as_uint(v[i]) & 0x7FFFFFFFu) : 0u);
         }
-        finite = __all_sync(FULL, finite);
+        const bool finite = __reduce_max_sync(FULL, amax) < 0x7F800000u;
         uint32_t used = 0;
         int my_idx = -1;
         float my_v = 0.0f;
         if (finite) {
             for (int j = 0; j < k; ++j) {
-                float bv = -INFINITY;
+                uint32_t bk = 0;
                 int bi = 0x7fffffff;
+                float bv = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int e = lane + 32 * i;
-                    if (e < E && !((used >> i) & 1u) && v[i] > bv) { bv = v[i]; bi = e; }
-                }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) {
-                    const float ov = __shfl_xor_sync(FULL, bv, o);
-                    const int oi = __shfl_xor_sync(FULL, bi, o);
-                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-                }
-                if ((bi & 31) == lane) used |= 1u << (bi >> 5);
-                if (lane == j) { my_idx = bi; my_v = bv; }
+                for (int i = 0; i < 8; ++i)
+                    if (!((used >> i) & 1u) && key[i] > bk) { bk = key[i]; bi = lane + 32 * i; bv = v[i]; }
+                const uint32_t mk = __reduce_max_sync(FULL, bk);
+                const int win = static_cast<int>(__reduce_min_sync(FULL, bk == mk ? static_cast<uint32_t>(bi) : 0xFFFFFFFFu));
+                if (bi == win) used |= 1u << (win >> 5);
+                const float wv = __shfl_sync(FULL, bv, win & 31);
+                if (lane == j) { my_idx = win; my_v = wv; }
             }
         }
-        // softmax over the selected logits (moe.cu:41-51): max, then a
-        // sequential sum j = 0..k-1, then division
+        // softmax over the selected logits (moe.cu:41-51): max, sequential
+        // sum j = 0..k-1, division
         float mx = __shfl_sync(FULL, my_v, 0);
         for (int j = 1; j < k; ++j) mx = fmaxf(mx, __shfl_sync(FULL, my_v, j));
         const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
@@ -150,14 +229,10 @@ __device__ void topk_and_dispatch(const DecodeParams& P) {
         for (int j = 0; j < k; ++j) sum += __shfl_sync(FULL, ex, j);
         const float wj = ex / sum;
         // host-side checks of layer_moe.cpp:114-124, on the device
-        bool ok = finite;
         float rs = 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const float w = __shfl_sync(FULL, wj, j);
-            const int id = __shfl_sync(FULL, my_idx, j);
-            ok = ok && id >= 0 && id < E && isfinite(w) && w >= 0.0f;
-            rs += w;
-        }
+        for (int j = 0; j < k; ++j) rs += __shfl_sync(FULL, wj, j);
+        const bool lane_ok = lane >= k || (my_idx >= 0 && my_idx < E && isfinite(wj) && wj >= 0.0f);
+        const bool ok = finite && __all_sync(FULL, lane_ok);
         uint32_t flag = 0;
         if (!ok) flag = EF_ROUTING;
         else if (!isfinite(rs) || fabsf(rs - 1.0f) > 1e-4f) flag = EF_NOT_NORMALIZED;
@@ -168,6 +243,7 @@ __device__ void topk_and_dispatch(const DecodeParams& P) {
         if (lane < k) {
             const int oi = flag ? -1 : my_idx;
             const float ow = flag ? __uint_as_float(0x7FC00000u) : wj;
+            s_idx[t * k + lane] = oi;
             P.topk_idx[t * k + lane] = oi;
             P.topk_w[t * k + lane] = ow;
             if (P.out_idx) P.out_idx[t * k + lane] = oi;
@@ -176,159 +252,147 @@ __device__ void topk_and_dispatch(const DecodeParams& P) {
     }
     __syncthreads();
 
-    // ---- stable permutation: pairs p = t*k + j sorted by (expert, t, j) ----
-    const int NP = P.T * k;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
-    __syncthreads();
+    // stable permutation by (expert, pair): rank of pair p = #pairs with a
+    // smaller expert + #earlier pairs with the same expert
     for (int p = threadIdx.x; p < NP; p += blockDim.x) {
-        const int e = P.topk_idx[p];
-        if (e >= 0 && e < E) atomicAdd(&s_cnt[e], 1);
+        const int e = s_idx[p];
+        int rank = -1;
+        if (e >= 0 && e < E) {
+            rank = 0;
+            for (int q = 0; q < NP; ++q) {
+                const int f = s_idx[q];
+                rank += (f >= 0 && (f < e || (f == e && q < p))) ? 1 : 0;
+            }
+            s_perm[rank] = p;
+        }
+        s_rank[p] = rank;
+        P.inv_perm[p] = rank;
     }
     __syncthreads();
-    if (warp == 0) {
-        // experts [8*lane, 8*lane+8): exclusive scan of counts and of "active"
-        int c[8], loc = 0, nz = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = 8 * lane + i;
-            c[i] = e < E ? s_cnt[e] : 0;
-            loc += c[i];
-            nz += c[i] > 0;
-        }
-        int inc = loc, incz = nz;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int a = __shfl_up_sync(FULL, inc, o), b = __shfl_up_sync(FULL, incz, o);
-            if (lane >= o) { inc += a; incz += b; }
-        }
-        int off = inc - loc, pos = incz - nz;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = 8 * lane + i;
-            if (e < E) {
-                P.offsets[e] = off;
-                s_cur[e] = off;
-                if (c[i] > 0) P.active[pos++] = e;
-            }
-            off += c[i];
-        }
-        if (lane == 31) {
-            P.offsets[E] = inc;
-            P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(inc);
-            P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(incz);
+    int npairs = 0;
+    for (int q = 0; q < NP; ++q) npairs += s_rank[q] >= 0 ? 1 : 0;
+    for (int i = threadIdx.x; i < npairs; i += blockDim.x)
+        s_first[i] = (i == 0 || s_idx[s_perm[i]] != s_idx[s_perm[i - 1]]) ? 1 : 0;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int i = 0; i < npairs; ++i) n += s_first[i];
+        s_nact = n;
+    }
+    // offsets[e] = number of valid pairs routed to experts < e
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+        int c = 0;
+        for (int q = 0; q < NP; ++q) c += (s_idx[q] >= 0 && s_idx[q] < e) ? 1 : 0;
+        P.offsets[e] = c;
+    }
+    const int maxs = sched_max_src(P.T, k, E);
+    const int poff = sched_perm_off(P.T, k, E), toff = sched_tok_off(P.T, k, E);
+    for (int i = threadIdx.x; i < npairs; i += blockDim.x) {
+        P.perm[i] = s_perm[i];
+        P.sched[poff + i] = s_perm[i];
+        P.sched[toff + i] = s_perm[i] / k;
+        if (s_first[i]) {
+            int s = 0, c = 1;
+            for (int q = 0; q < i; ++q) s += s_first[q];
+            while (i + c < npairs && !s_first[i + c]) ++c;
+            const int e = s_idx[s_perm[i]];
+            P.active[s] = e;
+            P.sched[SCHED_HDR + 3 * s] = e;
+            P.sched[SCHED_HDR + 3 * s + 1] = i;
+            P.sched[SCHED_HDR + 3 * s + 2] = c;
         }
     }
     __syncthreads();
-    if (warp == 0) {
-        const unsigned lt = (1u << lane) - 1u;
-        for (int base = 0; base < NP; base += 32) {
-            const int p = base + lane;
-            const int e = p < NP ? P.topk_idx[p] : -1;
-            const bool valid = e >= 0 && e < E;
-            const unsigned peers = __match_any_sync(FULL, valid ? e : -1);
-            const int rank = __popc(peers & lt);
-            const int pos = valid ? s_cur[e] + rank : -1;
-            __syncwarp();
-            const bool top = (peers >> lane) == 1u;
-            if (valid && top) s_cur[e] += __popc(peers);
-            __syncwarp();
-            if (p < NP) {
-                if (valid) P.perm[pos] = p;
-                P.inv_perm[p] = pos;
-            }
-        }
+    if (threadIdx.x == 0) {
+        P.sched[0] = s_nact;
+        P.sched[1] = npairs;
+        P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(s_nact);
+        P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(npairs);
     }
 }
 
 template <int CH>
 __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = blockIdx.x * RT_WARPS + warp, nw = gridDim.x * RT_WARPS;
+    const int gw = blockIdx.x * RT_WARPS + warp;
     const int nrows = P.E + (P.has_shared ? 1 : 0);
     const int LS = P.E + 1;
 
-    for (int r = gw; r < nrows; r += nw) {
-        const uint8_t* row;
-        int type;
-        if (r < P.E) {
-            type = P.router_type;
-            row = P.router + static_cast<size_t>(r) * P.d * router_esize(type);
-        } else {
-            type = P.sgate_type;
-            row = P.sgate_inp;
-        }
-        float4 w[CH][2];
+    if (threadIdx.x == 0) QMOE_TRACE(P, 0, 0);
+    // prologue: this warp's router row does not depend on the previous kernel
+    float4 w[CH][2];
+    const bool has_row = gw < nrows;
+    const bool writer = gw < P.T * CH;  // publishes 256 elements of the block input
+    if (has_row) {
+        const int type = gw < P.E ? P.router_type : P.sgate_type;
+        const uint8_t* row = gw < P.E ? P.router + static_cast<size_t>(gw) * P.d * router_esize(type) : P.sgate_inp;
         load_router_row<CH>(w, row, type, lane);
+    }
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) QMOE_TRACE(P, 0, 1);
+
+    if (has_row || writer) {
         for (int t = 0; t < P.T; ++t) {
-            float v = router_dot<CH>(w, P.x + static_cast<size_t>(t) * P.d, lane);
-            if (lane == 0) {
-                if (r < P.E && P.bias) v = __fadd_rn(v, P.bias[r]);
-                P.logits[t * LS + r] = v;
+            float4 xr[CH][2];
+            load_input<CH>(xr, P, P.x + static_cast<size_t>(t) * P.d, lane);
+            if (has_row) {
+                float v = reg_dot<CH>(w, xr);
+                if (lane == 0) {
+                    if (gw < P.E && P.bias) v = __fadd_rn(v, __ldg(P.bias + gw));
+                    P.logits[t * LS + gw] = v;
+                }
+            }
+            if (writer && gw / CH == t) {
+                const int i = gw % CH;
+#pragma unroll
+                for (int ii = 0; ii < CH; ++ii)
+                    if (ii == i)
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            const int e0 = 256 * ii + 128 * hh + 4 * lane;
+                            *reinterpret_cast<float4*>(P.xnorm + static_cast<size_t>(t) * P.d + e0) = xr[ii][hh];
+                            write_planes4(xr[ii][hh], P.xq + static_cast<size_t>(t) * P.xq_stride, P.d, e0, lane);
+                        }
             }
         }
     }
 
-    // 24-bit planes of x for the expert kernels
-    const int nb = P.d / 32;
-    for (int task = gw; task < P.T * nb; task += nw) {
-        const int t = task / nb, b = task % nb;
-        const float v = P.x[static_cast<size_t>(t) * P.d + 32 * b + lane];
-        uint8_t* base = P.xq + static_cast<size_t>(t) * P.xq_stride;
-        xq_block32(v, base + 32 * b + lane, base + P.d + 32 * b + lane, base + 2 * P.d + 32 * b + lane,
-                   reinterpret_cast<float2*>(base + 3 * P.d) + 2 * b, lane);
-    }
-
-    // last CTA to arrive selects the experts (threadfence reduction pattern)
+    // last CTA to arrive selects the experts.  The CTA barrier orders every
+    // thread's logit writes before thread 0's release; the acquire side of the
+    // same atomic makes all CTAs' logits visible to the last one.
     __shared__ int s_last;
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(P.ctrl + CTRL_ARRIVE, 1u);
+        QMOE_TRACE(P, 0, 2);
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(P.ctrl + CTRL_ARRIVE), "r"(1u)
+                     : "memory");
         s_last = (old == gridDim.x - 1);
+        QMOE_TRACE(P, 0, 3);
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
-    topk_and_dispatch(P);
-    if (threadIdx.x == 0) P.ctrl[CTRL_ARRIVE] = 0;
+    topk_and_schedule(P);
+    if (threadIdx.x == 0) {
+        P.ctrl[CTRL_ARRIVE] = 0;
+        QMOE_TRACE(P, 0, 4);
+    }
 }
 
 // ---------------------------------------------------------------------------
-// Expert gate/up
+// Expert kernels: shared pieces
 // ---------------------------------------------------------------------------
-constexpr int NCW = 8;                    // consumer warps
-constexpr int XK_THREADS = (NCW + 1) * 32; // + one producer warp
-constexpr int MAXCH = 128;
+constexpr int NCW = 8;                      // consumer warps
+constexpr int XK_THREADS = (NCW + 1) * 32;  // + one producer warp
+constexpr int SCHED_SMEM_WORDS = SCHED_HDR + 3 * kDecodeMaxT * kMaxTopK + 2 * kDecodeMaxT * kMaxTopK;
 
-struct Chunk {
-    int src;    // source index (== n_active: shared expert)
-    int r0;     // first row inside the source
-    int n;      // rows
-    int task0;  // first task index
-    int rflat;  // flattened row index of r0
-    int ntok;
-    int steps;
-    int pad;
-};
-
-struct SrcInfo {
-    int expert;   // -1 for the shared expert
-    int ntok;
-    int pair0;    // first permuted position (routed)
-};
-
-__device__ __forceinline__ SrcInfo src_info(const DecodeParams& P, int s, int n_active) {
-    SrcInfo si;
-    if (s < n_active) {
-        si.expert = P.active[s];
-        si.pair0 = P.offsets[si.expert];
-        si.ntok = P.offsets[si.expert + 1] - si.pair0;
-    } else {
-        si.expert = -1;
-        si.pair0 = 0;
-        si.ntok = P.T;
-    }
-    return si;
+template <int TYPE>
+__device__ __forceinline__ float unit_dot_t(uint32_t row, int u, const XU& x) {
+    if (TYPE == T_Q4_K) return dot_qk45<false>(row, u, x);
+    if (TYPE == T_Q5_K) return dot_qk45<true>(row, u, x);
+    if (TYPE == T_Q6_K) return dot_q6_k(row, u, x);
+    return dot_q8_0(row, u, x);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -336,22 +400,24 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return s * u;
 }
 
-__device__ __forceinline__ XPlanesView planes_view(const uint8_t* base, int K) {
+__device__ __forceinline__ XPlanesView planes_view(uint32_t base, int K) {
     XPlanesView v;
     v.p0 = base;
-    v.p1 = base + K;
-    v.p2 = base + 2 * K;
-    v.meta = reinterpret_cast<const float2*>(base + 3 * K);
+    v.p1 = base + static_cast<uint32_t>(K);
+    v.p2 = base + 2u * static_cast<uint32_t>(K);
+    v.meta = base + 3u * static_cast<uint32_t>(K);
     return v;
 }
 
 struct StagePlan {
     const uint8_t* lo;
     uint32_t tx;
-    uint32_t skew;
 };
 
-// Plans (and performs the unaligned tail of) a copy of [src, src+bytes) into dst.
+// Plans a copy of [src, src+bytes) into dst: the 16-byte aligned superset is
+// bulk-copied (clipped to `limit`, the end of the source allocation); the
+// few bytes past the last full chunk, if any, are copied here with plain
+// loads.  The row data then starts at dst + (src & 15).
 __device__ __forceinline__ StagePlan plan_stage(uint8_t* dst, const uint8_t* src, uint64_t bytes, const uint8_t* limit) {
     StagePlan sp;
     const uintptr_t s = reinterpret_cast<uintptr_t>(src);
@@ -360,305 +426,416 @@ __device__ __forceinline__ StagePlan plan_stage(uint8_t* dst, const uint8_t* src
     const uintptr_t lim = reinterpret_cast<uintptr_t>(limit);
     const uintptr_t hi_full = hi <= lim ? hi : (lim & ~static_cast<uintptr_t>(15));
     sp.lo = reinterpret_cast<const uint8_t*>(lo);
-    sp.skew = static_cast<uint32_t>(s - lo);
     sp.tx = hi_full > lo ? static_cast<uint32_t>(hi_full - lo) : 0u;
     for (uintptr_t a = (hi_full > lo ? hi_full : lo); a < s + bytes; ++a)
         dst[a - lo] = *reinterpret_cast<const uint8_t*>(a);
     return sp;
 }
 
-struct GateUpSmem {
-    uint64_t* full;
-    uint64_t* empty;
-    uint64_t* xbar;
-    Chunk* chunks;
-    int* misc;  // [0] nch, [1] ntask, [2] R0, [3] R1, [4] n_active
-    uint8_t* xs;
-    float* hbuf;
-    uint8_t* stages;
-};
+__device__ __forceinline__ void load_sched(int* s_sched, const DecodeParams& P) {
+    const int words = sched_words(P.T, P.k, P.E);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) s_sched[i] = __ldcg(P.sched + i);
+}
 
-__global__ void __launch_bounds__(XK_THREADS, 1)
-    k_gateup(DecodeParams P, int nst, int ch_rows, uint32_t half_bytes, int hbuf_rows) {
+// The same quantisation of one 32-block, written to global memory.
+__device__ __forceinline__ void xq_block32_global(float v, uint8_t* base, int K, int e0, int lane) {
+    const uint32_t ab = __reduce_max_sync(FULL, __float_as_uint(v) & 0x7FFFFFFFu);
+    float s16 = v;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) s16 += __shfl_xor_sync(FULL, s16, o);
+    const bool bad = ab >= 0x7F800000u;
+    const uint32_t eb = ab >> 23;
+    int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
+    sh = sh > 126 ? 126 : sh;
+    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
+    float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+    const int X = bad ? 0 : __float2int_rn(v * mul);
+    if (bad) scale = __uint_as_float(0x7FC00000u);
+    base[e0 + lane] = static_cast<uint8_t>(X & 255);
+    base[K + e0 + lane] = static_cast<uint8_t>((X >> 8) & 255);
+    base[2 * K + e0 + lane] = static_cast<uint8_t>((X >> 16) & 255);
+    if ((lane & 15) == 0) reinterpret_cast<float2*>(base + 3 * K)[(e0 >> 4) + (lane >> 4)] = make_float2(scale, s16);
+}
+
+// ---------------------------------------------------------------------------
+// Expert gate/up
+//
+// Work is cut into items of 32 consecutive rows of one source (the shared
+// expert's Fs/32 items first, then F/32 items per active expert): CTA c takes
+// items c, c + grid, ...  At T = 1 with Qwen3.5-35B shapes that is 16 + 128
+// items, one per SM.  An item's 32 results per token form one 32-block of
+// silu(g)*u, which the CTA quantises into the 24-bit planes the down kernel
+// reads -- each block exactly once.  All index arithmetic in the loops is
+// shifts and running counters (row, unit and item counts are powers of two).
+// ---------------------------------------------------------------------------
+constexpr int GU_NCW = 16;
+constexpr int GU_THREADS = (GU_NCW + 1) * 32;
+constexpr int ITEM_ROWS = 32;
+
+__device__ __forceinline__ int ilog2(int v) { return 31 - __clz(v); }
+
+template <int TR, int TS>
+__global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int nst, uint32_t half_bytes, int dn_rows) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int d = P.d, U = d / 64, RPS = 32 / U;
-    GateUpSmem S;
-    S.full = reinterpret_cast<uint64_t*>(smem);
-    S.empty = S.full + 32;
-    S.xbar = S.empty + 32;
-    S.misc = reinterpret_cast<int*>(smem + 528);
-    S.chunks = reinterpret_cast<Chunk*>(smem + 576);
-    S.xs = smem + 576 + MAXCH * sizeof(Chunk);
-    const size_t xs_bytes = P.xq_stride * P.T;
-    S.hbuf = reinterpret_cast<float*>(S.xs + xs_bytes);
-    S.stages = reinterpret_cast<uint8_t*>(S.hbuf) + align_up(static_cast<size_t>(hbuf_rows) * P.T * 4, 128);
+    const int d = P.d;
+    const int lgU = ilog2(d >> 6), U = 1 << lgU;   // units (64 elements) per row
+    const int lgR = 5 - lgU;                        // rows per warp step = 32 / U
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + 8;
+    uint64_t* xbar = empty + 8;
+    int* s_sched = reinterpret_cast<int*>(smem + 256);
+    uint8_t* xs = reinterpret_cast<uint8_t*>(s_sched) + align_up(SCHED_SMEM_WORDS * 4, 128);
+    const uint32_t xs_bytes = static_cast<uint32_t>(P.xq_stride) * static_cast<uint32_t>(P.T);
+    float* hb = reinterpret_cast<float*>(xs + align_up(xs_bytes, 128));
+    uint8_t* stages = reinterpret_cast<uint8_t*>(hb) + align_up(static_cast<size_t>(ITEM_ROWS) * P.T * 4, 128);
+    const uint64_t rbg = row_bytes(TR, d), rbs = row_bytes(TS, d);
+    const int nb_sh = P.has_shared ? P.Fs / ITEM_ROWS : 0;
+    const int lgF = ilog2(P.F / ITEM_ROWS);         // items per routed expert = 2^lgF
+    const int G = gridDim.x, c = blockIdx.x;
 
     if (threadIdx.x == 0) {
-        const int n_active = static_cast<int>(P.ctrl[CTRL_N_ACTIVE]);
-        const int rows_tot = n_active * P.F + (P.has_shared ? P.Fs : 0);
-        const int per = 32 * ((rows_tot + 32 * gridDim.x - 1) / (32 * gridDim.x));
-        const int R0 = blockIdx.x * per;
-        const int R1 = min(R0 + per, rows_tot);
-        int nch = 0, ntask = 0;
-        for (int r = R0; r < R1 && nch < MAXCH;) {
-            int s, rr, rows;
-            if (r < n_active * P.F) { s = r / P.F; rr = r % P.F; rows = P.F; }
-            else { s = n_active; rr = r - n_active * P.F; rows = P.Fs; }
-            const int n = min(min(ch_rows, R1 - r), rows - rr);
-            const SrcInfo si = src_info(P, s, n_active);
-            Chunk c;
-            c.src = s; c.r0 = rr; c.n = n; c.task0 = ntask; c.rflat = r;
-            c.ntok = si.ntok; c.steps = (n + RPS - 1) / RPS; c.pad = 0;
-            S.chunks[nch++] = c;
-            ntask += c.ntok * c.steps;
-            r += n;
-        }
-        S.misc[0] = nch; S.misc[1] = ntask; S.misc[2] = R0; S.misc[3] = R1; S.misc[4] = n_active;
-        for (int i = 0; i < nst; ++i) { mbar_init(S.full + i, 1); mbar_init(S.empty + i, NCW); }
-        mbar_init(S.xbar, 1);
+        QMOE_TRACE(P, 1, 0);
+        for (int i = 0; i < nst; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, GU_NCW); }
+        mbar_init(xbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
-    const int nch = S.misc[0], ntask = S.misc[1], R0 = S.misc[2], R1 = S.misc[3], n_active = S.misc[4];
-    if (R0 >= R1) return;
+    auto issue = [&](int slot, bool shared_src, int expert, int r0) {
+        const uint64_t rb = shared_src ? rbs : rbg;
+        const uint8_t* gsrc = shared_src ? P.sgate.p + r0 * rbs : P.gate.p + (static_cast<uint64_t>(expert) * P.F + r0) * rbg;
+        const uint8_t* usrc = shared_src ? P.sup.p + r0 * rbs : P.up.p + (static_cast<uint64_t>(expert) * P.F + r0) * rbg;
+        uint8_t* dg = stages + static_cast<size_t>(slot) * 2 * half_bytes;
+        uint8_t* du = dg + half_bytes;
+        const StagePlan pg = plan_stage(dg, gsrc, ITEM_ROWS * rb, shared_src ? P.sgate.end : P.gate.end);
+        const StagePlan pu = plan_stage(du, usrc, ITEM_ROWS * rb, shared_src ? P.sup.end : P.up.end);
+        mbar_arrive_expect_tx(full + slot, pg.tx + pu.tx);
+        if (pg.tx) bulk_g2s(dg, pg.lo, pg.tx, full + slot, P.ctrl);
+        if (pu.tx) bulk_g2s(du, pu.lo, pu.tx, full + slot, P.ctrl);
+    };
+    // prologue: a shared-expert item does not depend on the routing
+    if (warp == GU_NCW && lane == 0 && c < nb_sh) issue(0, true, -1, c * ITEM_ROWS);
+    pdl_wait();  // the router has finished: schedule and block input are valid
+    if (threadIdx.x == 0) QMOE_TRACE(P, 1, 1);
+    if (warp == GU_NCW && lane == 0) {
+        mbar_arrive_expect_tx(xbar, xs_bytes);
+        bulk_g2s(xs, P.xq, xs_bytes, xbar, P.ctrl);
+    }
+    load_sched(s_sched, P);
+    __syncthreads();
+    const int nact = s_sched[0];
+    const int* s_perm = s_sched + sched_perm_off(P.T, P.k, P.E);
+    const int* s_tok = s_sched + sched_tok_off(P.T, P.k, P.E);
+    const int nitems = nb_sh + (nact << lgF);
+    const int ni = c < nitems ? (nitems - 1 - c) / G + 1 : 0;
+    if (threadIdx.x == 0) QMOE_TRACE(P, 1, 2);
+    pdl_trigger();  // the down kernel may start its prologue (routing is final)
 
-    const uint64_t rbg = row_bytes(P.gate.type, d), rbs = row_bytes(P.sgate.type, d);
-
-    if (warp == NCW) {
+    if (warp == GU_NCW) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            mbar_arrive_expect_tx(S.xbar, static_cast<uint32_t>(xs_bytes));
-            bulk_g2s(S.xs, P.xq, static_cast<uint32_t>(xs_bytes), S.xbar);
-            for (int c = 0; c < nch; ++c) {
-                const int slot = c % nst;
-                if (c >= nst) mbar_wait(S.empty + slot, ((c / nst) - 1) & 1, P.ctrl);
-                const Chunk ck = S.chunks[c];
-                const uint8_t *gsrc, *usrc, *gend, *uend;
-                uint64_t rb;
-                if (ck.src < n_active) {
-                    const int e = P.active[ck.src];
-                    rb = rbg;
-                    gsrc = P.gate.p + (static_cast<uint64_t>(e) * P.F + ck.r0) * rbg;
-                    usrc = P.up.p + (static_cast<uint64_t>(e) * P.F + ck.r0) * rbg;
-                    gend = P.gate.end; uend = P.up.end;
-                } else {
-                    rb = rbs;
-                    gsrc = P.sgate.p + static_cast<uint64_t>(ck.r0) * rbs;
-                    usrc = P.sup.p + static_cast<uint64_t>(ck.r0) * rbs;
-                    gend = P.sgate.end; uend = P.sup.end;
+            // the down kernel's CTA c reads rows [c*dn_rows, ...) of every
+            // active expert's down matrix: warm L2 with them now
+            const int r0 = c * dn_rows, nr = min(dn_rows, P.d - r0);
+            if (nr > 0) {
+                const uint64_t rbd = row_bytes(P.down.type, P.F), rbsd = row_bytes(P.sdown.type, P.Fs);
+                for (int s2 = 0; s2 <= nact; ++s2) {
+                    const uint8_t* src = s2 < nact ? P.down.p + (static_cast<uint64_t>(s_sched[SCHED_HDR + 3 * s2]) * P.d + r0) * rbd
+                                                   : P.sdown.p + static_cast<uint64_t>(r0) * rbsd;
+                    if (s2 == nact && !P.has_shared) break;
+                    const uint64_t nb = s2 < nact ? nr * rbd : nr * rbsd;
+                    const uintptr_t lo = reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15);
+                    const uintptr_t hi = (reinterpret_cast<uintptr_t>(src) + nb) & ~static_cast<uintptr_t>(15);
+                    if (hi > lo) prefetch_l2(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
                 }
-                uint8_t* dg = S.stages + static_cast<size_t>(slot) * 2 * half_bytes;
-                uint8_t* du = dg + half_bytes;
-                const StagePlan pg = plan_stage(dg, gsrc, ck.n * rb, gend);
-                const StagePlan pu = plan_stage(du, usrc, ck.n * rb, uend);
-                mbar_arrive_expect_tx(S.full + slot, pg.tx + pu.tx);
-                if (pg.tx) bulk_g2s(dg, pg.lo, pg.tx, S.full + slot);
-                if (pu.tx) bulk_g2s(du, pu.lo, pu.tx, S.full + slot);
             }
+            int i = c, slot = 0, round = 0;
+            for (int kk = 0; kk < ni; ++kk, i += G) {
+                if (kk > 0 || i >= nb_sh) {  // item 0 of a shared-expert CTA was issued in the prologue
+                    if (round > 0) mbar_wait(empty + slot, (round - 1) & 1, P.ctrl);
+                    if (i < nb_sh) {
+                        issue(slot, true, -1, i * ITEM_ROWS);
+                    } else {
+                        const int j = i - nb_sh;
+                        issue(slot, false, s_sched[SCHED_HDR + 3 * (j >> lgF)], (j & ((1 << lgF) - 1)) * ITEM_ROWS);
+                    }
+                }
+                if (++slot == nst) { slot = 0; ++round; }
+            }
+            mbar_wait(xbar, 0, P.ctrl);
         }
         return;
     }
 
     // ---------------- consumers ----------------
-    mbar_wait(S.xbar, 0, P.ctrl);
-    const int t_lo = (warp * ntask) / NCW, t_hi = ((warp + 1) * ntask) / NCW;
-    const int u = lane % U, rsub = lane / U;
+    mbar_wait(xbar, 0, P.ctrl);
+    if (threadIdx.x == 0) QMOE_TRACE(P, 1, 3);
+    const int u = lane & (U - 1), rsub = lane >> lgU;
+    const int lgS = 5 - lgR;  // steps per item = 32 / rows-per-step
     XU xr;
     int cur_key = -1;
-    for (int c = 0; c < nch; ++c) {
-        const int slot = c % nst;
-        mbar_wait(S.full + slot, (c / nst) & 1, P.ctrl);
-        const Chunk ck = S.chunks[c];
-        const int c_lo = max(t_lo, ck.task0), c_hi = min(t_hi, ck.task0 + ck.ntok * ck.steps);
-        if (c_lo < c_hi) {
-            const bool routed = ck.src < n_active;
-            const int type = routed ? P.gate.type : P.sgate.type;
-            const uint64_t rb = routed ? rbg : rbs;
-            const SrcInfo si = src_info(P, ck.src, n_active);
-            const uint8_t* dg = S.stages + static_cast<size_t>(slot) * 2 * half_bytes;
-            const uint8_t* du = dg + half_bytes;
-            const uint32_t skg = static_cast<uint32_t>(
-                reinterpret_cast<uintptr_t>(routed ? P.gate.p + (static_cast<uint64_t>(si.expert) * P.F + ck.r0) * rbg
-                                                   : P.sgate.p + static_cast<uint64_t>(ck.r0) * rbs) & 15u);
-            const uint32_t sku = static_cast<uint32_t>(
-                reinterpret_cast<uintptr_t>(routed ? P.up.p + (static_cast<uint64_t>(si.expert) * P.F + ck.r0) * rbg
-                                                   : P.sup.p + static_cast<uint64_t>(ck.r0) * rbs) & 15u);
-            for (int tau = c_lo; tau < c_hi; ++tau) {
-                const int tl = tau - ck.task0;
-                const int ti = tl / ck.steps, st = tl % ck.steps;
-                const int tok = routed ? P.perm[si.pair0 + ti] / P.k : ti;
-                const int key = tok * 64 + type;
-                if (key != cur_key) {
-                    load_xu(xr, planes_view(S.xs + static_cast<size_t>(tok) * P.xq_stride, d), type, u);
-                    cur_key = key;
-                }
-                const int rl = st * RPS + rsub;  // row inside the chunk
-                const bool valid = rl < ck.n;
-                float g = 0.0f, up = 0.0f;
-                if (valid) {
-                    g = unit_dot(type, dg + skg + rl * rb, u, xr);
-                    up = unit_dot(type, du + sku + rl * rb, u, xr);
-                }
-                for (int o = U / 2; o; o >>= 1) {
-                    g += __shfl_xor_sync(FULL, g, o);
-                    up += __shfl_xor_sync(FULL, up, o);
-                }
-                if (valid && u == 0)
-                    S.hbuf[static_cast<size_t>(ck.rflat - R0 + rl) * P.T + ti] = silu_mul(g, up);
-            }
+    int i = c, slot = 0, round = 0;
+    for (int kk = 0; kk < ni; ++kk, i += G) {
+        const bool routed = i >= nb_sh;
+        int bb, expert = -1, pair0 = 0, ntok = P.T;
+        if (routed) {
+            const int j = i - nb_sh, s2 = j >> lgF;
+            bb = j & ((1 << lgF) - 1);
+            expert = s_sched[SCHED_HDR + 3 * s2];
+            pair0 = s_sched[SCHED_HDR + 3 * s2 + 1];
+            ntok = s_sched[SCHED_HDR + 3 * s2 + 2];
+        } else {
+            bb = i;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(S.empty + slot);
+        const int r0 = bb * ITEM_ROWS;
+        mbar_wait(full + slot, round & 1, P.ctrl);
+        if (threadIdx.x == 0 && kk == 0) QMOE_TRACE(P, 1, 4);
+        uint32_t dg = smem_u32(stages) + static_cast<uint32_t>(slot) * 2u * half_bytes;
+        uint32_t du = dg + half_bytes;
+        {
+            const uintptr_t gsrc = routed ? reinterpret_cast<uintptr_t>(P.gate.p) + (static_cast<uint64_t>(expert) * P.F + r0) * rbg
+                                          : reinterpret_cast<uintptr_t>(P.sgate.p) + static_cast<uint64_t>(r0) * rbs;
+            const uintptr_t usrc = routed ? reinterpret_cast<uintptr_t>(P.up.p) + (static_cast<uint64_t>(expert) * P.F + r0) * rbg
+                                          : reinterpret_cast<uintptr_t>(P.sup.p) + static_cast<uint64_t>(r0) * rbs;
+            dg += static_cast<uint32_t>(gsrc & 15u);
+            du += static_cast<uint32_t>(usrc & 15u);
+        }
+        const uint32_t rb = static_cast<uint32_t>(routed ? rbg : rbs);
+        const int ntask = ntok << lgS;
+        for (int tau = warp; tau < ntask; tau += GU_NCW) {
+            const int ti = tau >> lgS, st = tau & ((1 << lgS) - 1);
+            const int tok = routed ? s_tok[pair0 + ti] : ti;
+            const int key = (tok << 1) | (routed ? 1 : 0);
+            if (key != cur_key) {
+                const XPlanesView xv = planes_view(smem_u32(xs) + static_cast<uint32_t>(tok) * static_cast<uint32_t>(P.xq_stride), d);
+                if (routed) load_xu(xr, xv, TR, u); else load_xu(xr, xv, TS, u);
+                cur_key = key;
+            }
+            const int rl = (st << lgR) + rsub;
+            float g, up;
+            if (routed) {
+                g = unit_dot_t<TR>(dg + static_cast<uint32_t>(rl) * rb, u, xr);
+                up = unit_dot_t<TR>(du + static_cast<uint32_t>(rl) * rb, u, xr);
+            } else {
+                g = unit_dot_t<TS>(dg + static_cast<uint32_t>(rl) * rb, u, xr);
+                up = unit_dot_t<TS>(du + static_cast<uint32_t>(rl) * rb, u, xr);
+            }
+            for (int o = U >> 1; o; o >>= 1) {
+                g += __shfl_xor_sync(FULL, g, o);
+                up += __shfl_xor_sync(FULL, up, o);
+            }
+            if (u == 0) stsf(smem_u32(hb) + 4u * static_cast<uint32_t>(rl * P.T + ti), silu_mul(g, up));
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(GU_NCW * 32) : "memory");
+        if (threadIdx.x == 0 && kk == 0) QMOE_TRACE(P, 1, 5);
+        // the item's 32-blocks of silu(g)*u: F32 copy and 24-bit planes
+        for (int ti = warp; ti < ntok; ti += GU_NCW) {
+            const int vid = routed ? s_perm[pair0 + ti] : P.T * P.k + ti;
+            const float v = ldsf(smem_u32(hb) + 4u * static_cast<uint32_t>(lane * P.T + ti));
+            P.hidden[static_cast<size_t>(vid) * P.H + r0 + lane] = v;
+            xq_block32_global(v, P.hq + static_cast<size_t>(vid) * P.hq_stride, P.H, r0, lane);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(GU_NCW * 32) : "memory");
+        if (lane == 0) mbar_arrive(empty + slot);
+        if (++slot == nst) { slot = 0; ++round; }
     }
-    // all consumer warps done with hbuf
-    asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-
-    // planes of silu(g)*u per 32-row block, and the F32 values
-    const int nblk = (R1 - R0) / 32;
-    for (int task = warp; task < nblk * P.T; task += NCW) {
-        const int blk = task / P.T, ti = task % P.T;
-        const int rf = R0 + 32 * blk;
-        int s, rr;
-        if (rf < n_active * P.F) { s = rf / P.F; rr = rf % P.F; }
-        else { s = n_active; rr = rf - n_active * P.F; }
-        const SrcInfo si = src_info(P, s, n_active);
-        if (ti >= si.ntok) continue;
-        const int vid = s < n_active ? P.perm[si.pair0 + ti] : P.T * P.k + ti;
-        const float v = S.hbuf[static_cast<size_t>(32 * blk + lane) * P.T + ti];
-        P.hidden[static_cast<size_t>(vid) * P.H + rr + lane] = v;
-        uint8_t* base = P.hq + static_cast<size_t>(vid) * P.hq_stride;
-        xq_block32(v, base + rr + lane, base + P.H + rr + lane, base + 2 * P.H + rr + lane,
-                   reinterpret_cast<float2*>(base + 3 * P.H) + rr / 16, lane);
-    }
+    if (threadIdx.x == 0) QMOE_TRACE(P, 1, 6);
 }
 
 // ---------------------------------------------------------------------------
 // Expert down + combine
+//
+// CTA c owns output rows [c*Rd, c*Rd + Rd).  Its sources are the shared
+// expert (chunk 0) and the active experts (chunks 1..); all of them must fit
+// in shared memory at once (host plan).  The hidden vectors are visited in
+// source order -- shared vectors first, then the permuted pairs -- so a
+// contiguous range of (vector, row step) tasks per warp keeps one vector's
+// planes in registers.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(XK_THREADS, 1)
+template <int TR, int TS>
+__global__ void __launch_bounds__(XK_THREADS, 2)
     k_down(DecodeParams P, int nst, int Rd, uint32_t stage_bytes, int nvec) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + 64;
-    uint64_t* hbar = empty + 64;
-    int* misc = reinterpret_cast<int*>(smem + 1040);
-    uint8_t* hs = smem + 1088;
-    const size_t hs_bytes = P.hq_stride * static_cast<size_t>(nvec);
-    float* ybuf = reinterpret_cast<float*>(hs + hs_bytes);
-    uint8_t* stages = reinterpret_cast<uint8_t*>(ybuf) + align_up(static_cast<size_t>(nvec) * Rd * 4, 128);
+    uint64_t* hbar = full + 72;
+    int* s_sched = reinterpret_cast<int*>(smem + 1280);
+    uint8_t* hs = reinterpret_cast<uint8_t*>(s_sched) + align_up(SCHED_SMEM_WORDS * 4, 128);
+    const uint32_t hs_bytes = static_cast<uint32_t>(P.hq_stride) * static_cast<uint32_t>(nvec);
+    float* ybuf = reinterpret_cast<float*>(hs + align_up(hs_bytes, 128));
+    // every region starts 128-byte aligned (the stages are bulk-copy targets)
+    float* s_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ybuf) +
+                                          align_up(static_cast<size_t>(nvec) * Rd * 4, 128));  // [T*k] weights
+    float* s_sg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s_w) +
+                                           align_up(static_cast<size_t>(P.T) * P.k * 4, 128));  // [T] shared gate
+    float* s_res = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s_sg) +
+                                            align_up(static_cast<size_t>(P.T) * 4, 128));       // [T][Rd] residual
+    uint8_t* stages = reinterpret_cast<uint8_t*>(s_res) + align_up(static_cast<size_t>(P.T) * Rd * 4, 128);
+    const uint64_t rbd = row_bytes(TR, P.F), rbs = row_bytes(TS, P.Fs);
 
     const int r0 = blockIdx.x * Rd;
     const int nrow = min(Rd, P.d - r0);
     if (threadIdx.x == 0) {
-        misc[0] = static_cast<int>(P.ctrl[CTRL_N_ACTIVE]);
-        for (int i = 0; i < nst; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, NCW); }
-        mbar_init(hbar, 1);
+        QMOE_TRACE(P, 2, 0);
+        for (int i = 0; i <= nst; ++i) mbar_init(full + i, 1);  // full[nst] doubles as the planes barrier
         fence_mbar_init();
     }
     __syncthreads();
-    const int n_active = misc[0];
-    const int nsrc = n_active + (P.has_shared ? 1 : 0);
-    if (nrow <= 0) return;
-    const uint64_t rbd = row_bytes(P.down.type, P.F), rbs = row_bytes(P.sdown.type, P.Fs);
-
+    const int sh = P.has_shared ? 1 : 0;
+    // prologue 1: shared-expert down rows (chunk 0)
+    if (warp == NCW && lane == 0 && sh) {
+        const StagePlan sp = plan_stage(stages, P.sdown.p + static_cast<uint64_t>(r0) * rbs, nrow * rbs, P.sdown.end);
+        mbar_arrive_expect_tx(full, sp.tx);
+        if (sp.tx) bulk_g2s(stages, sp.lo, sp.tx, full, P.ctrl);
+    }
+    // prologue 2: the routing and the block's residual input are final (the
+    // gate/up kernel lets this kernel start only after the router completed)
+    load_sched(s_sched, P);
+    const int LS = P.E + 1;
+    for (int i = threadIdx.x; i < P.T * P.k; i += blockDim.x) s_w[i] = __ldcg(P.topk_w + i);
+    for (int t = threadIdx.x; t < P.T; t += blockDim.x)
+        s_sg[t] = sh ? 1.0f / (1.0f + expf(-__ldcg(P.logits + t * LS + P.E))) : 0.0f;
+    if (P.residual)
+        for (int t = 0; t < P.T; ++t)
+            for (int r = threadIdx.x; r < nrow; r += blockDim.x)
+                s_res[t * Rd + r] = __ldcg(P.residual + static_cast<size_t>(t) * P.d + r0 + r);
+    __syncthreads();
+    if (threadIdx.x == 0) QMOE_TRACE(P, 2, 1);
+    const int nact = s_sched[0];
+    const int npairs = s_sched[1];
+    const int* s_perm = s_sched + sched_perm_off(P.T, P.k, P.E);
+    const int nsrc = nact + sh;  // chunk 0 = shared (if any), then routed sources
+    // chunk cc occupies slot cc - round*nst during round cc / nst
+    auto issue = [&](int cc, int slot) {
+        const int e = s_sched[SCHED_HDR + 3 * (cc - sh)];
+        uint8_t* dst = stages + static_cast<size_t>(slot) * stage_bytes;
+        const StagePlan sp = plan_stage(dst, P.down.p + (static_cast<uint64_t>(e) * P.d + r0) * rbd, nrow * rbd,
+                                        P.down.end);
+        mbar_arrive_expect_tx(full + slot, sp.tx);
+        if (sp.tx) bulk_g2s(dst, sp.lo, sp.tx, full + slot, P.ctrl);
+    };
     if (warp == NCW) {
+        // ---------------- producer ----------------
+        if (lane == 0)
+            for (int cc = sh; cc < min(nsrc, nst); ++cc) issue(cc, cc);
+        pdl_wait();  // the planes of silu(g)*u are written
         if (lane == 0) {
-            mbar_arrive_expect_tx(hbar, static_cast<uint32_t>(hs_bytes));
-            bulk_g2s(hs, P.hq, static_cast<uint32_t>(hs_bytes), hbar);
-            for (int c = 0; c < nsrc; ++c) {
-                const int slot = c % nst;
-                if (c >= nst) mbar_wait(empty + slot, ((c / nst) - 1) & 1, P.ctrl);
-                const uint8_t *src, *end;
-                uint64_t rb;
-                if (c < n_active) {
-                    const int e = P.active[c];
-                    rb = rbd;
-                    src = P.down.p + (static_cast<uint64_t>(e) * P.d + r0) * rbd;
-                    end = P.down.end;
-                } else {
-                    rb = rbs;
-                    src = P.sdown.p + static_cast<uint64_t>(r0) * rbs;
-                    end = P.sdown.end;
-                }
-                uint8_t* dst = stages + static_cast<size_t>(slot) * stage_bytes;
-                const StagePlan sp = plan_stage(dst, src, nrow * rb, end);
-                mbar_arrive_expect_tx(full + slot, sp.tx);
-                if (sp.tx) bulk_g2s(dst, sp.lo, sp.tx, full + slot);
-            }
+            mbar_arrive_expect_tx(full + nst, hs_bytes);
+            bulk_g2s(hs, P.hq, hs_bytes, full + nst, P.ctrl);
         }
+        pdl_trigger();
+        for (int rb0 = nst; rb0 < nsrc; rb0 += nst) {
+            asm volatile("bar.sync 2, %0;" ::"r"((NCW + 1) * 32) : "memory");  // previous round consumed
+            if (lane == 0)
+                for (int cc = rb0; cc < min(nsrc, rb0 + nst); ++cc) issue(cc, cc - rb0);
+        }
+        if (lane == 0) mbar_wait(full + nst, 0, P.ctrl);
         return;
     }
+    pdl_wait();
+    pdl_trigger();  // the next block's router may start loading its weights
+    if (threadIdx.x == 0) QMOE_TRACE(P, 2, 2);
+    mbar_wait(full + nst, 0, P.ctrl);
+    if (threadIdx.x == 0) QMOE_TRACE(P, 2, 3);
 
-    mbar_wait(hbar, 0, P.ctrl);
-    // tasks: (source, token, step), enumerated source-major; contiguous per warp
-    int ntask = 0;
-    for (int c = 0; c < nsrc; ++c) {
-        const bool routed = c < n_active;
-        const int K = routed ? P.F : P.Fs;
-        const int rps = 32 / (K / 64);
-        const SrcInfo si = src_info(P, c, n_active);
-        ntask += si.ntok * ((nrow + rps - 1) / rps);
-    }
-    const int t_lo = (warp * ntask) / NCW, t_hi = ((warp + 1) * ntask) / NCW;
+    // Tasks are (vector, row step) in source order: the T shared vectors
+    // (ids T*k ..) of chunk 0 first, then the permuted pairs, whose chunk is
+    // their expert's source index + sh.  Round r covers chunks
+    // [r*nst, r*nst + nst) -- a contiguous task range, split evenly over the
+    // consumer warps so that each warp keeps one vector's planes in registers
+    // across consecutive tasks.
+    const int Ur = P.F >> 6, Us = P.Fs >> 6;
+    const int lgUr = ilog2(Ur), lgUs = ilog2(Us);
+    const int steps_r = (nrow + (32 >> lgUr) - 1) >> (5 - lgUr);
+    const int steps_s = (nrow + (32 >> lgUs) - 1) >> (5 - lgUs);
+    const int Tsh = sh ? P.T : 0;
+    const int nt_sh = Tsh * steps_s;
+    // first task of chunk cc (cc == nsrc gives the total)
+    auto chunk_task = [&](int cc) {
+        if (cc < sh) return 0;
+        const int q = cc - sh < nact ? s_sched[SCHED_HDR + 3 * (cc - sh) + 1] : npairs;
+        return nt_sh + q * steps_r;
+    };
     XU xr;
-    int cur_vid = -1;
-    int task0 = 0;
-    for (int c = 0; c < nsrc; ++c) {
-        const int slot = c % nst;
-        const bool routed = c < n_active;
-        const int K = routed ? P.F : P.Fs;
-        const int U = K / 64, rps = 32 / U;
-        const int steps = (nrow + rps - 1) / rps;
-        const SrcInfo si = src_info(P, c, n_active);
-        const int nt = si.ntok * steps;
-        mbar_wait(full + slot, (c / nst) & 1, P.ctrl);
-        const int c_lo = max(t_lo, task0), c_hi = min(t_hi, task0 + nt);
-        if (c_lo < c_hi) {
-            const int type = routed ? P.down.type : P.sdown.type;
-            const uint64_t rb = routed ? rbd : rbs;
-            const uint8_t* src = routed ? P.down.p + (static_cast<uint64_t>(si.expert) * P.d + r0) * rbd
-                                        : P.sdown.p + static_cast<uint64_t>(r0) * rbs;
-            const uint8_t* wbase = stages + static_cast<size_t>(slot) * stage_bytes +
-                                   (reinterpret_cast<uintptr_t>(src) & 15u);
-            const int u = lane % U, rsub = lane / U;
-            for (int tau = c_lo; tau < c_hi; ++tau) {
-                const int tl = tau - task0;
-                const int ti = tl / steps, st = tl % steps;
-                const int vid = routed ? P.perm[si.pair0 + ti] : P.T * P.k + ti;
-                if (vid != cur_vid) {
-                    load_xu(xr, planes_view(hs + static_cast<size_t>(vid) * P.hq_stride, P.H), type, u);
-                    cur_vid = vid;
+    for (int rb0 = 0, round = 0; rb0 < nsrc; rb0 += nst, ++round) {
+        const int rend = min(nsrc, rb0 + nst);
+        const int A = chunk_task(rb0), B = chunk_task(rend);
+        const int t_lo = A + ((warp * (B - A)) >> 3), t_hi = A + (((warp + 1) * (B - A)) >> 3);
+        static_assert(NCW == 8, "task split assumes 8 consumer warps");
+        if (t_lo < t_hi) {
+            // cursor of task t_lo: vector index vi (source order), row step st, chunk cc
+            int vi, st, cc;
+            if (t_lo < nt_sh) {
+                vi = t_lo / steps_s;
+                st = t_lo - vi * steps_s;
+                cc = 0;
+            } else {
+                const int q = t_lo - nt_sh;
+                const int pv = q / steps_r;
+                st = q - pv * steps_r;
+                vi = Tsh + pv;
+                cc = max(rb0, sh);
+                while (cc + 1 < rend && s_sched[SCHED_HDR + 3 * (cc + 1 - sh) + 1] <= pv) ++cc;
+            }
+            int cend = cc < sh ? Tsh : Tsh + s_sched[SCHED_HDR + 3 * (cc - sh) + 1] + s_sched[SCHED_HDR + 3 * (cc - sh) + 2];
+            int cur_cc = -1, cur_vi = -1;
+            uint32_t wbase = 0;
+            for (int tau = t_lo; tau < t_hi; ++tau) {
+                const bool shv = cc < sh;
+                if (cc != cur_cc) {
+                    const int slot = cc - rb0;
+                    mbar_wait(full + slot, round & 1, P.ctrl);
+                    const uint64_t srcaddr =
+                        shv ? reinterpret_cast<uintptr_t>(P.sdown.p) + static_cast<uint64_t>(r0) * rbs
+                            : reinterpret_cast<uintptr_t>(P.down.p) +
+                                  (static_cast<uint64_t>(s_sched[SCHED_HDR + 3 * (cc - sh)]) * P.d + r0) * rbd;
+                    wbase = smem_u32(stages) + static_cast<uint32_t>(slot) * stage_bytes + static_cast<uint32_t>(srcaddr & 15u);
+                    cur_cc = cc;
                 }
-                const int rl = st * rps + rsub;
+                const int vid = shv ? P.T * P.k + vi : s_perm[vi - Tsh];
+                const int lgU = shv ? lgUs : lgUr;
+                if (vi != cur_vi) {
+                    const XPlanesView hv =
+                        planes_view(smem_u32(hs) + static_cast<uint32_t>(vid) * static_cast<uint32_t>(P.hq_stride), P.H);
+                    if (shv) load_xu(xr, hv, TS, lane & (Us - 1)); else load_xu(xr, hv, TR, lane & (Ur - 1));
+                    cur_vi = vi;
+                }
+                const int u = lane & ((1 << lgU) - 1), rsub = lane >> lgU;
+                const int rl = (st << (5 - lgU)) + rsub;
                 const bool valid = rl < nrow;
-                float y = valid ? unit_dot(type, wbase + rl * rb, u, xr) : 0.0f;
-                for (int o = U / 2; o; o >>= 1) y += __shfl_xor_sync(FULL, y, o);
-                if (valid && u == 0) ybuf[static_cast<size_t>(vid) * Rd + rl] = y;
+                float y = 0.0f;
+                if (valid)
+                    y = shv ? unit_dot_t<TS>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbs), u, xr)
+                            : unit_dot_t<TR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbd), u, xr);
+                for (int o = (1 << lgU) >> 1; o; o >>= 1) y += __shfl_xor_sync(FULL, y, o);
+                if (valid && u == 0) stsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
+                // advance the cursor
+                if (++st == (shv ? steps_s : steps_r)) {
+                    st = 0;
+                    if (++vi == cend && cc + 1 < nsrc) {
+                        ++cc;
+                        cend = Tsh + s_sched[SCHED_HDR + 3 * (cc - sh) + 1] + s_sched[SCHED_HDR + 3 * (cc - sh) + 2];
+                    }
+                }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + slot);
-        task0 += nt;
+        if (rend < nsrc) asm volatile("bar.sync 2, %0;" ::"r"((NCW + 1) * 32) : "memory");  // slots may be refilled
     }
     asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+    if (threadIdx.x == 0) QMOE_TRACE(P, 2, 5);
 
     // combine (moe.cu:76-81 and :90-96, accumulation order of layer_moe.cpp:127-153)
-    const int LS = P.E + 1;
     for (int idx = threadIdx.x; idx < P.T * nrow; idx += NCW * 32) {
-        const int t = idx / nrow, r = idx % nrow;
+        const int t = idx / nrow, r = idx - (idx / nrow) * nrow;
         float acc = 0.0f;
-        const bool bad = P.topk_idx[t * P.k] < 0;
-        for (int j = 0; j < P.k; ++j) acc = fmaf(P.topk_w[t * P.k + j], ybuf[static_cast<size_t>(t * P.k + j) * Rd + r], acc);
-        if (P.has_shared) {
-            const float sg = 1.0f / (1.0f + expf(-P.logits[t * LS + P.E]));
-            acc = fmaf(ybuf[static_cast<size_t>(P.T * P.k + t) * Rd + r], sg, acc);
-        }
-        if (bad) acc = __uint_as_float(0x7FC00000u);
+        for (int j = 0; j < P.k; ++j)
+            acc = fmaf(s_w[t * P.k + j], ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((t * P.k + j) * Rd + r)), acc);
+        if (sh) acc = fmaf(ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((P.T * P.k + t) * Rd + r)), s_sg[t], acc);
+        if (!(s_w[t * P.k] == s_w[t * P.k])) acc = __uint_as_float(0x7FC00000u);  // routing error: NaN weights
         const size_t o = static_cast<size_t>(t) * P.d + r0 + r;
-        P.out[o] = P.residual ? P.residual[o] + acc : acc;
+        P.out[o] = P.residual ? s_res[t * Rd + r] + acc : acc;
     }
+    if (threadIdx.x == 0) QMOE_TRACE(P, 2, 6);
 }
 
 // ---------------------------------------------------------------------------
@@ -668,7 +845,7 @@ namespace {
 struct DevCache {
     int sms = 0;
     int smem_optin = 0;
-    bool attr_gu = false, attr_dn = false;
+    bool pdl = true;
 };
 DevCache g_dev[64];
 
@@ -679,8 +856,35 @@ DevCache& dev_cache() {
     if (!c.sms) {
         cudaDeviceGetAttribute(&c.sms, cudaDevAttrMultiProcessorCount, dev);
         cudaDeviceGetAttribute(&c.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        const char* e = getenv("QMOE_PDL");
+        c.pdl = !(e && e[0] == '0');
     }
     return c;
+}
+
+// Preferred shared-memory budget per expert-kernel CTA: small enough that a
+// gate/up CTA and a down CTA fit on one SM together (PDL overlap).
+constexpr size_t kCoResidentSmem = 110 * 1024;
+
+template <typename... Args>
+cudaError_t launch(void (*kern)(Args...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dev_cache().pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <typename K>
+cudaError_t set_smem(K kern, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
 }
 }  // namespace
 
@@ -690,38 +894,35 @@ cudaError_t launch_router(const DecodeParams& P, cudaStream_t s) {
     const int nrows = P.E + (P.has_shared ? 1 : 0);
     const int grid = (nrows + RT_WARPS - 1) / RT_WARPS;
     switch (P.d / 256) {
-        case 1: k_router<1><<<grid, RT_WARPS * 32, 0, s>>>(P); break;
-        case 2: k_router<2><<<grid, RT_WARPS * 32, 0, s>>>(P); break;
-        case 4: k_router<4><<<grid, RT_WARPS * 32, 0, s>>>(P); break;
-        case 8: k_router<8><<<grid, RT_WARPS * 32, 0, s>>>(P); break;
-        case 16: k_router<16><<<grid, RT_WARPS * 32, 0, s>>>(P); break;
+        case 1: return launch(k_router<1>, grid, RT_WARPS * 32, 0, s, P);
+        case 2: return launch(k_router<2>, grid, RT_WARPS * 32, 0, s, P);
+        case 4: return launch(k_router<4>, grid, RT_WARPS * 32, 0, s, P);
+        case 8: return launch(k_router<8>, grid, RT_WARPS * 32, 0, s, P);
+        case 16: return launch(k_router<16>, grid, RT_WARPS * 32, 0, s, P);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
-// Shared-memory plan of k_gateup for this launch.
-struct GuPlan { int grid, nst, ch_rows, hbuf_rows; uint32_t half_bytes; size_t smem; };
+struct GuPlan { int grid, nst, dn_rows; uint32_t half_bytes; size_t smem; };
 
 static bool plan_gateup(const DecodeParams& P, GuPlan& g) {
     DevCache& dc = dev_cache();
-    const int U = P.d / 64;
     g.grid = dc.sms;
-    g.ch_rows = (32 / U) * NCW;
+    g.dn_rows = (P.d + dc.sms - 1) / dc.sms;  // rows per down-kernel CTA (see plan_down)
+    if (P.F % ITEM_ROWS || P.Fs % ITEM_ROWS) return false;
     const uint64_t rb = std::max(row_bytes(P.gate.type, P.d), row_bytes(P.sgate.type, P.d));
-    g.half_bytes = static_cast<uint32_t>(align_up(g.ch_rows * rb + 32, 128));
-    const int umax = std::min(P.T * P.k, P.E);
-    const int rows_tot = umax * P.F + (P.has_shared ? P.Fs : 0);
-    g.hbuf_rows = 32 * ((rows_tot + 32 * g.grid - 1) / (32 * g.grid));
-    const int nch_max = g.hbuf_rows / g.ch_rows + 2 + g.hbuf_rows / std::min(P.F, P.has_shared ? P.Fs : P.F) + 2;
-    if (nch_max > MAXCH) return false;
-    const size_t fixed = 576 + MAXCH * sizeof(Chunk) + P.xq_stride * P.T +
-                         align_up(static_cast<size_t>(g.hbuf_rows) * P.T * 4, 128);
+    g.half_bytes = static_cast<uint32_t>(align_up(ITEM_ROWS * rb + 32, 128));
+    const int umax = sched_max_src(P.T, P.k, P.E);
+    const int items_max = (P.has_shared ? P.Fs / ITEM_ROWS : 0) + umax * (P.F / ITEM_ROWS);
+    const int per_cta = (items_max + g.grid - 1) / g.grid;
+    const size_t fixed = 256 + align_up(SCHED_SMEM_WORDS * 4, 128) + align_up(P.xq_stride * P.T, 128) +
+                         align_up(static_cast<size_t>(ITEM_ROWS) * P.T * 4, 128);
+    const size_t stage = 2 * static_cast<size_t>(g.half_bytes);
     const size_t budget = static_cast<size_t>(dc.smem_optin) - 1024;
-    if (fixed + 2 * 2 * g.half_bytes > budget) return false;
-    g.nst = static_cast<int>(std::min<size_t>(std::min<size_t>(nch_max, 32), (budget - fixed) / (2 * g.half_bytes)));
-    if (g.nst < 2) g.nst = 2;
-    g.smem = fixed + static_cast<size_t>(g.nst) * 2 * g.half_bytes;
+    if (fixed + stage > budget) return false;
+    g.nst = static_cast<int>(std::min<size_t>(std::min<size_t>(per_cta, 8), (budget - fixed) / stage));
+    g.nst = std::max(g.nst, 1);
+    g.smem = fixed + static_cast<size_t>(g.nst) * stage;
     return true;
 }
 
@@ -734,13 +935,18 @@ static bool plan_down(const DecodeParams& P, DnPlan& p) {
     p.nvec = P.T * P.k + P.T;
     const uint64_t rb = std::max(row_bytes(P.down.type, P.F), row_bytes(P.sdown.type, P.Fs));
     p.stage_bytes = static_cast<uint32_t>(align_up(p.Rd * rb + 32, 128));
-    const size_t fixed = 1088 + P.hq_stride * p.nvec + align_up(static_cast<size_t>(p.nvec) * p.Rd * 4, 128);
-    const size_t budget = static_cast<size_t>(dc.smem_optin) - 1024;
-    if (fixed + 2 * p.stage_bytes > budget) return false;
-    const int nsrc_max = std::min(P.T * P.k, P.E) + 1;
-    p.nst = static_cast<int>(std::min<size_t>(std::min<size_t>(nsrc_max, 64), (budget - fixed) / p.stage_bytes));
-    if (p.nst < 2) p.nst = 2;
+    const size_t fixed = 1280 + align_up(SCHED_SMEM_WORDS * 4, 128) + align_up(P.hq_stride * p.nvec, 128) +
+                         align_up(static_cast<size_t>(p.nvec) * p.Rd * 4, 128) +
+                         align_up(4 * static_cast<size_t>(P.T) * P.k, 128) + align_up(4 * static_cast<size_t>(P.T), 128) +
+                         align_up(static_cast<size_t>(P.T) * p.Rd * 4, 128);
+    const size_t optin = static_cast<size_t>(dc.smem_optin) - 1024;
+    // as many sources resident at once as fit (shared + one per active
+    // expert when possible); the rest follow in rounds
+    if (fixed + p.stage_bytes > optin) return false;
+    const int want = sched_max_src(P.T, P.k, P.E) + (P.has_shared ? 1 : 0);
+    p.nst = static_cast<int>(std::min<size_t>({static_cast<size_t>(want), 71, (optin - fixed) / p.stage_bytes}));
     p.smem = fixed + static_cast<size_t>(p.nst) * p.stage_bytes;
+    if (P.hq_stride * p.nvec >= (1u << 20)) return false;  // one bulk copy (transaction-count limit)
     return true;
 }
 
@@ -750,30 +956,56 @@ bool decode_supported(const DecodeParams& P) {
     return plan_gateup(P, g) && plan_down(P, dn);
 }
 
+// (routed type, shared type) -> kernel instantiation
+template <template <int, int> class KS>
+static typename KS<12, 12>::type pick(int tr, int ts) {  // NOLINT
+#define QMOE_TS(TRV)                                         \
+    switch (ts) {                                            \
+        case 12: return KS<TRV, 12>::get();                  \
+        case 13: return KS<TRV, 13>::get();                  \
+        case 14: return KS<TRV, 14>::get();                  \
+        case 8: return KS<TRV, 8>::get();                    \
+        default: return nullptr;                             \
+    }
+    switch (tr) {
+        case 12: QMOE_TS(12)
+        case 13: QMOE_TS(13)
+        case 14: QMOE_TS(14)
+        case 8: QMOE_TS(8)
+        default: return nullptr;
+    }
+#undef QMOE_TS
+}
+
+template <int A, int B>
+struct GuSel {
+    typedef void (*type)(DecodeParams, int, uint32_t, int);
+    static type get() { return k_gateup<A, B>; }
+};
+template <int A, int B>
+struct DnSel {
+    typedef void (*type)(DecodeParams, int, int, uint32_t, int);
+    static type get() { return k_down<A, B>; }
+};
+
 cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s) {
     GuPlan g;
     if (!plan_gateup(P, g)) return cudaErrorInvalidValue;
-    DevCache& dc = dev_cache();
-    if (!dc.attr_gu) {
-        cudaError_t e = cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, dc.smem_optin);
-        if (e != cudaSuccess) return e;
-        dc.attr_gu = true;
-    }
-    k_gateup<<<g.grid, XK_THREADS, g.smem, s>>>(P, g.nst, g.ch_rows, g.half_bytes, g.hbuf_rows);
-    return cudaGetLastError();
+    auto kern = pick<GuSel>(P.gate.type, P.sgate.type);
+    if (!kern) return cudaErrorInvalidValue;
+    cudaError_t e = set_smem(kern, g.smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, g.grid, GU_THREADS, g.smem, s, P, g.nst, g.half_bytes, g.dn_rows);
 }
 
 cudaError_t launch_down(const DecodeParams& P, cudaStream_t s) {
     DnPlan p;
     if (!plan_down(P, p)) return cudaErrorInvalidValue;
-    DevCache& dc = dev_cache();
-    if (!dc.attr_dn) {
-        cudaError_t e = cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, dc.smem_optin);
-        if (e != cudaSuccess) return e;
-        dc.attr_dn = true;
-    }
-    k_down<<<p.grid, XK_THREADS, p.smem, s>>>(P, p.nst, p.Rd, p.stage_bytes, p.nvec);
-    return cudaGetLastError();
+    auto kern = pick<DnSel>(P.down.type, P.sdown.type);
+    if (!kern) return cudaErrorInvalidValue;
+    cudaError_t e = set_smem(kern, p.smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, p.grid, XK_THREADS, p.smem, s, P, p.nst, p.Rd, p.stage_bytes, p.nvec);
 }
 
 }  // namespace qmoe

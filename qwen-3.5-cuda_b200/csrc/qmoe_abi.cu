@@ -92,6 +92,8 @@ WArg warg(const qmoe_tensor& t) {
     return a;
 }
 
+uint64_t* g_trace = nullptr;  // qmoe_trace_enable
+
 // DecodeParams for tokens [0, T) of x/out at the given workspace.
 DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out, const float* residual,
                          int T, void* ws) {
@@ -118,9 +120,15 @@ DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x
     P.perm = reinterpret_cast<int32_t*>(w + L.perm);
     P.inv_perm = reinterpret_cast<int32_t*>(w + L.inv_perm);
     P.active = reinterpret_cast<int32_t*>(w + L.active);
+    P.sched = reinterpret_cast<int32_t*>(w + L.sched);
+    P.xnorm = reinterpret_cast<float*>(w + L.xnorm);
+    P.norm_w = nullptr;
+    P.eps = 0.0f;
+    P.prenorm = 0;
     P.xq = w + L.xq; P.xq_stride = L.xq_stride;
     P.hidden = reinterpret_cast<float*>(w + L.hidden);
     P.hq = w + L.hq; P.hq_stride = L.hq_stride; P.H = L.H;
+    P.trace = g_trace;
     return P;
 }
 
@@ -202,6 +210,7 @@ void* qmoe_ws_view(void* ws, const qmoe_dims* D, int T, int which) {
         case QMOE_WS_INV_PERM: return w + L.inv_perm;
         case QMOE_WS_HIDDEN: return w + L.hidden;
         case QMOE_WS_ERROR: return w + L.ctrl + CTRL_ERROR * 4;
+        case QMOE_WS_INPUT: return w + L.xnorm;
         default: return nullptr;
     }
 }
@@ -252,17 +261,23 @@ int qmoe_down_combine(const qmoe_block* B, const qmoe_dims* D, int T, float* out
     return cuda_status(launch_down(P, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-int qmoe_block_forward(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out, const float* residual,
-                       int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out,
+                              const float* residual, const float* norm_w, float eps, int T, void* ws,
+                              size_t ws_bytes, qmoe_stream_t stream) {
     int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
     if (st) return st;
     if (!x || !out) return QMOE_ERR_ARG;
-    if (!aligned16(x)) return QMOE_ERR_ALIGN;
+    if (!aligned16(x) || (norm_w && !aligned16(norm_w))) return QMOE_ERR_ALIGN;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
         const int n = std::min(kDecodeMaxT, T - t0);
         const size_t o = static_cast<size_t>(t0) * D->d_model;
         DecodeParams P = make_params(B, D, x + o, out + o, residual ? residual + o : nullptr, n, ws);
+        if (norm_w) {
+            P.prenorm = 1;
+            P.norm_w = norm_w;
+            P.eps = eps;
+        }
         if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
         cudaError_t e = launch_router(P, s);
         if (e == cudaSuccess) e = launch_gateup(P, s);
@@ -271,6 +286,26 @@ int qmoe_block_forward(const qmoe_block* B, const qmoe_dims* D, const float* x, 
     }
     return QMOE_OK;
 }
+
+int qmoe_block_forward(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out, const float* residual,
+                       int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    return block_forward_impl(B, D, x, out, residual, nullptr, 0.0f, T, ws, ws_bytes, stream);
+}
+
+int qmoe_block_forward_prenorm(const qmoe_block* B, const qmoe_dims* D, const float* resid, const float* norm_weight,
+                               float eps, float* out, int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    if (!norm_weight) return QMOE_ERR_ARG;
+    if (!(eps > 0.0f)) return QMOE_ERR_ARG;
+    return block_forward_impl(B, D, resid, out, resid, norm_weight, eps, T, ws, ws_bytes, stream);
+}
+
+int qmoe_trace_enable(uint64_t* buf, size_t bytes) {
+    if (buf && bytes < qmoe_trace_bytes()) return QMOE_ERR_ARG;
+    g_trace = buf;
+    return QMOE_OK;
+}
+
+size_t qmoe_trace_bytes(void) { return sizeof(uint64_t) * kTraceKinds * kTraceCtas * kTraceEvents; }
 
 int qmoe_check_errors(void* ws, const qmoe_dims* D, uint32_t* err, qmoe_stream_t stream) {
     (void)D;
@@ -286,7 +321,7 @@ int qmoe_check_errors(void* ws, const qmoe_dims* D, uint32_t* err, qmoe_stream_t
     if (err) { err[0] = w[0]; err[1] = w[1]; }
     if (w[0] & EF_ROUTING) return QMOE_ERR_ROUTING;
     if (w[0] & EF_NOT_NORMALIZED) return QMOE_ERR_NOT_NORMALIZED;
-    if (w[0] & EF_TIMEOUT) return QMOE_ERR_TIMEOUT;
+    if (w[0] & (EF_TIMEOUT | EF_ALIGN)) return QMOE_ERR_TIMEOUT;
     return QMOE_OK;
 }
 

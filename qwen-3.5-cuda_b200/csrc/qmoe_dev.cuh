@@ -14,6 +14,7 @@ enum : uint32_t {
     EF_ROUTING = 1u,        // non-finite logits / invalid id or weight (layer_moe.cpp:116-118)
     EF_NOT_NORMALIZED = 2u, // |sum(w) - 1| > 1e-4 (layer_moe.cpp:122-124)
     EF_TIMEOUT = 4u,        // a bounded wait gave up
+    EF_ALIGN = 8u,          // a bulk copy with a misaligned address or size was skipped
 };
 
 // Control block at the start of every workspace (uint32 words).
@@ -79,18 +80,21 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: the warp sleeps in the barrier unit until
+// the phase completes (or ~100 us pass) instead of re-issuing the test.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls, records EF_TIMEOUT and returns false.
-constexpr uint32_t kWaitLimit = 1u << 24;
+// Bounded wait: gives up after kWaitLimit tries (each one suspends for up to
+// the hint above), records EF_TIMEOUT and returns false.
+constexpr uint32_t kWaitLimit = 1u << 14;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* ctrl) {
     for (uint32_t i = 0; i < kWaitLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
@@ -98,9 +102,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// L2 prefetch of a global range (no shared-memory destination).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // global -> shared bulk copy (16-byte aligned addresses, size multiple of 16),
-// completion signalled on `bar` as transaction bytes.
-__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+// completion signalled on `bar` as transaction bytes.  A misaligned request is
+// not issued: EF_ALIGN is recorded and the waiter times out instead of the
+// copy faulting.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                         uint32_t* ctrl) {
+    if (((smem_u32(smem_dst) | static_cast<uint32_t>(reinterpret_cast<uintptr_t>(gmem_src)) | bytes) & 15u) != 0) {
+        if (ctrl) atomicOr(ctrl + CTRL_ERROR, EF_ALIGN);
+        return;
+    }
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_u32(smem_dst)),
@@ -108,53 +124,73 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// Copies [src, src+bytes) of global memory into shared memory at `dst`, where
-// `src` may be unaligned: the 16-byte aligned superset [lo, hi) is bulk-copied
-// (hi clipped to `limit`, the end of the source allocation), any tail past the
-// last full 16-byte chunk is copied with plain loads by the calling thread.
-// Returns the transaction bytes that will arrive on `bar`, and sets *skew to
-// the offset of `src` inside the staged window.  `dst` must be 16-byte aligned
-// and have room for bytes + 32.  Called by ONE thread.
-__device__ __forceinline__ uint32_t stage_bytes(uint8_t* dst, const uint8_t* src, uint64_t bytes,
-                                                const uint8_t* limit, uint64_t* bar, uint32_t* skew) {
-    uintptr_t s = reinterpret_cast<uintptr_t>(src);
-    uintptr_t lo = s & ~static_cast<uintptr_t>(15);
-    uintptr_t hi = (s + bytes + 15) & ~static_cast<uintptr_t>(15);
-    uintptr_t lim = reinterpret_cast<uintptr_t>(limit);
-    uintptr_t hi_full = hi <= lim ? hi : (lim & ~static_cast<uintptr_t>(15));
-    *skew = static_cast<uint32_t>(s - lo);
-    uint32_t tx = 0;
-    if (hi_full > lo) {
-        tx = static_cast<uint32_t>(hi_full - lo);
-        bulk_g2s(dst, reinterpret_cast<const void*>(lo), tx, bar);
-    }
-    // tail (only when the window would run past the allocation end)
-    for (uintptr_t a = hi_full > lo ? hi_full : lo; a < s + bytes; ++a)
-        dst[a - lo] = *reinterpret_cast<const uint8_t*>(a);
-    return tx;
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
+// Programmatic dependent launch (PDL).  wait: block until the grids this
+// launch depends on have completed and their memory is visible (a no-op when
+// the launch has no programmatic dependency).  launch_dependents: allow the
+// next kernel in the stream to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
-// Shared-memory loads
+// Shared-memory accesses through 32-bit shared-window addresses (explicit
+// ld.shared / st.shared: the hot loops never go through generic addressing).
+// volatile keeps them ordered after the mbarrier waits that publish the data.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float2 ldsf2(uint32_t a) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts8(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u8 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void stsf(uint32_t a, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void stsf2(uint32_t a, float x, float y) {
+    asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
+}
 
 // 16 bytes from a shared address with any 2-byte alignment: two aligned
 // 16-byte loads and a byte funnel shift.
-__device__ __forceinline__ uint4 lds128_any(const uint8_t* p) {
-    uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    uint32_t off = static_cast<uint32_t>(a & 15u);
-    const uint8_t* base = p - off;
-    uint4 v0 = lds128(base);
+__device__ __forceinline__ uint4 lds128_any(uint32_t a) {
+    const uint32_t off = a & 15u;
+    const uint32_t base = a - off;
+    const uint4 v0 = lds128(base);
     if (off == 0) return v0;
-    uint4 v1 = lds128(base + 16);
-    uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t sh = (off & 3u) * 8u;
+    const uint4 v1 = lds128(base + 16);
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    const uint32_t sh = (off & 3u) * 8u;
     uint32_t s[7];
 #pragma unroll
     for (int i = 0; i < 7; ++i) s[i] = __funnelshift_r(w[i], w[i + 1], sh);
-    uint32_t q = off >> 2;  // 0..3
+    const uint32_t q = off >> 2;  // 0..3
     uint4 r;
     r.x = q == 0 ? s[0] : q == 1 ? s[1] : q == 2 ? s[2] : s[3];
     r.y = q == 0 ? s[1] : q == 1 ? s[2] : q == 2 ? s[3] : s[4];
@@ -164,13 +200,11 @@ __device__ __forceinline__ uint4 lds128_any(const uint8_t* p) {
 }
 
 // 4 bytes from a shared address with 2-byte alignment.
-__device__ __forceinline__ uint32_t lds32_any(const uint8_t* p) {
-    uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    uint32_t off = static_cast<uint32_t>(a & 3u);
-    const uint8_t* base = p - off;
-    uint32_t w0 = lds32(base);
+__device__ __forceinline__ uint32_t lds32_any(uint32_t a) {
+    const uint32_t off = a & 3u;
+    const uint32_t w0 = lds32(a - off);
     if (off == 0) return w0;
-    uint32_t w1 = lds32(base + 4);
+    const uint32_t w1 = lds32(a - off + 4);
     return __funnelshift_r(w0, w1, off * 8u);
 }
 
@@ -187,68 +221,33 @@ __device__ __forceinline__ uint32_t lds32_any(const uint8_t* p) {
 // |v|max * 2^-23 per element, i.e. F32-level accuracy.
 // ---------------------------------------------------------------------------
 struct XPlanesView {
-    const uint8_t* p0;
-    const uint8_t* p1;
-    const uint8_t* p2;
-    const float2* meta;  // [K/16]
+    uint32_t p0, p1, p2;  // shared addresses of the three planes
+    uint32_t meta;        // shared address of float2 meta[K/16]
 };
 
 // Quantises one 32-element block held one element per lane (all 32 lanes
 // participate).  Writes the lane's three plane bytes and, from lanes 0 and 16,
-// the meta of the two 16-element halves.
-__device__ __forceinline__ void xq_block32(float v, uint8_t* p0, uint8_t* p1, uint8_t* p2, float2* meta16,
+// the meta of the two 16-element halves.  The largest magnitude comes from one
+// redux over the IEEE bits (non-negative floats order like unsigned ints;
+// anything >= 0x7F800000 is inf/NaN).
+__device__ __forceinline__ void xq_block32(float v, uint32_t p0, uint32_t p1, uint32_t p2, uint32_t meta16,
                                            int lane) {
-    float a = fabsf(v);
-    float amax = a;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    // fmaxf drops NaN: detect non-finite separately
-    bool bad = !isfinite(v);
-    bad = __any_sync(0xffffffffu, bad);
+    const uint32_t ab = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
     float s16 = v;
 #pragma unroll
     for (int o = 8; o; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-    uint32_t eb = __float_as_uint(amax) >> 23;  // biased exponent (sign is 0)
+    const bool bad = ab >= 0x7F800000u;
+    const uint32_t eb = ab >> 23;  // biased exponent of the largest magnitude
     int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
     sh = sh > 126 ? 126 : sh;
-    float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
+    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
     float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-    int X = bad ? 0 : __float2int_rn(v * mul);
+    const int X = bad ? 0 : __float2int_rn(v * mul);
     if (bad) scale = __uint_as_float(0x7FC00000u);
-    *p0 = static_cast<uint8_t>(X & 255);
-    *p1 = static_cast<uint8_t>((X >> 8) & 255);
-    *p2 = static_cast<uint8_t>((X >> 16) & 255);
-    if ((lane & 15) == 0) meta16[lane >> 4] = make_float2(scale, s16);
-}
-
-// 64 consecutive elements (one "unit") of a plane view, as 16 words per plane.
-struct XUnit64 {
-    uint32_t x0[16], x1[16], x2[16];
-};
-
-__device__ __forceinline__ void load_xunit64(XUnit64& u, const XPlanesView& xv, int e0) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 a = lds128(xv.p0 + e0 + 16 * q);
-        uint4 b = lds128(xv.p1 + e0 + 16 * q);
-        uint4 c = lds128(xv.p2 + e0 + 16 * q);
-        u.x0[4 * q] = a.x; u.x0[4 * q + 1] = a.y; u.x0[4 * q + 2] = a.z; u.x0[4 * q + 3] = a.w;
-        u.x1[4 * q] = b.x; u.x1[4 * q + 1] = b.y; u.x1[4 * q + 2] = b.z; u.x1[4 * q + 3] = b.w;
-        u.x2[4 * q] = c.x; u.x2[4 * q + 1] = c.y; u.x2[4 * q + 2] = c.z; u.x2[4 * q + 3] = c.w;
-    }
-}
-
-// Four 16-element runs starting at e[0..3] (Q6_K units).
-__device__ __forceinline__ void load_xunit_runs(XUnit64& u, const XPlanesView& xv, const int e[4]) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 a = lds128(xv.p0 + e[q]);
-        uint4 b = lds128(xv.p1 + e[q]);
-        uint4 c = lds128(xv.p2 + e[q]);
-        u.x0[4 * q] = a.x; u.x0[4 * q + 1] = a.y; u.x0[4 * q + 2] = a.z; u.x0[4 * q + 3] = a.w;
-        u.x1[4 * q] = b.x; u.x1[4 * q + 1] = b.y; u.x1[4 * q + 2] = b.z; u.x1[4 * q + 3] = b.w;
-        u.x2[4 * q] = c.x; u.x2[4 * q + 1] = c.y; u.x2[4 * q + 2] = c.z; u.x2[4 * q + 3] = c.w;
-    }
+    sts8(p0, static_cast<uint32_t>(X) & 255u);
+    sts8(p1, (static_cast<uint32_t>(X) >> 8) & 255u);
+    sts8(p2, (static_cast<uint32_t>(X) >> 16) & 255u);
+    if ((lane & 15) == 0) stsf2(meta16 + 8u * static_cast<uint32_t>(lane >> 4), scale, s16);
 }
 
 // Combines the three plane partial sums into sum(q * X) (one rounding).

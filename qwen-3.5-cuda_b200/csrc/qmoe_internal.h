@@ -40,9 +40,20 @@ __host__ __device__ inline uint64_t row_bytes(int t, int K) {
     return be ? static_cast<uint64_t>(K / be) * static_cast<uint64_t>(blk_bytes(t)) : 0;
 }
 
+// Packed routing schedule written by the router's last CTA and read once by
+// the expert kernels: [0] n_active, [1] n_pairs, [2..3] spare, then per
+// active expert s: {expert, first permuted position, pair count}, then the
+// permutation (pair ids in (expert, token, slot) order), then the token of
+// each permuted pair.
+constexpr int SCHED_HDR = 4;
+__host__ __device__ inline int sched_max_src(int T, int k, int E) { return T * k < E ? T * k : E; }
+__host__ __device__ inline int sched_perm_off(int T, int k, int E) { return SCHED_HDR + 3 * sched_max_src(T, k, E); }
+__host__ __device__ inline int sched_tok_off(int T, int k, int E) { return sched_perm_off(T, k, E) + T * k; }
+__host__ __device__ inline int sched_words(int T, int k, int E) { return sched_tok_off(T, k, E) + T * k; }
+
 // Workspace layout for a call with T tokens (all offsets 256-byte aligned).
 struct WsLayout {
-    size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, xq, hidden, hq, total;
+    size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, sched, xnorm, xq, hidden, hq, total;
     size_t xq_stride;  // bytes per token of x planes: 3*d + (d/16)*8
     size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
     int H;             // max(F, Fs)
@@ -64,6 +75,8 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     L.perm = take(sizeof(int32_t) * P);
     L.inv_perm = take(sizeof(int32_t) * P);
     L.active = take(sizeof(int32_t) * (P < E ? P : E));
+    L.sched = take(sizeof(int32_t) * sched_words(T, k, E));
+    L.xnorm = take(sizeof(float) * static_cast<size_t>(T) * d);
     L.xq_stride = align_up(3 * static_cast<size_t>(d) + static_cast<size_t>(d / 16) * 8, 16);
     L.xq = take(L.xq_stride * T);
     L.H = H;
@@ -73,6 +86,9 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     L.total = o;
     return L;
 }
+
+// Phase tracer: kernel kinds x CTAs x events of %globaltimer (ns).
+constexpr int kTraceKinds = 3, kTraceCtas = 160, kTraceEvents = 8;
 
 // One weight tensor as seen by the kernels.
 struct WArg {
@@ -97,6 +113,7 @@ struct DecodeParams {
     const float* x;  // [T][d]
     float* out;      // [T][d]
     const float* residual;
+    uint64_t* trace;   // optional phase timestamps (qmoe_trace_enable), else null
     int32_t* out_idx;  // optional copies of the routing result
     float* out_w;
     // workspace
@@ -108,10 +125,15 @@ struct DecodeParams {
     int32_t* perm;
     int32_t* inv_perm;
     int32_t* active;
-    uint8_t* xq;
+    int32_t* sched;
+    float* xnorm;       // [T][d] the block's input after the optional fused RMSNorm
+    const float* norm_w;  // optional fused pre-MoE RMSNorm weight [d] (prenorm != 0)
+    float eps;
+    int prenorm;
+    uint8_t* xq;        // [T] 24-bit planes of the block input (written by the router)
     size_t xq_stride;
     float* hidden;
-    uint8_t* hq;
+    uint8_t* hq;        // [T*k + T] 24-bit planes of silu(g)*u (written by the gate/up kernel)
     size_t hq_stride;
     int H;
 };

@@ -39,13 +39,13 @@ __device__ __forceinline__ void load_xu(XU& x, const XPlanesView& xv, int type, 
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         int e = unit_run_start(type, u, q);
-        uint4 a = lds128(xv.p0 + e);
-        uint4 b = lds128(xv.p1 + e);
-        uint4 c = lds128(xv.p2 + e);
+        const uint4 a = lds128(xv.p0 + e);
+        const uint4 b = lds128(xv.p1 + e);
+        const uint4 c = lds128(xv.p2 + e);
         x.x0[4 * q] = a.x; x.x0[4 * q + 1] = a.y; x.x0[4 * q + 2] = a.z; x.x0[4 * q + 3] = a.w;
         x.x1[4 * q] = b.x; x.x1[4 * q + 1] = b.y; x.x1[4 * q + 2] = b.z; x.x1[4 * q + 3] = b.w;
         x.x2[4 * q] = c.x; x.x2[4 * q + 1] = c.y; x.x2[4 * q + 2] = c.z; x.x2[4 * q + 3] = c.w;
-        float2 m = xv.meta[e >> 4];
+        const float2 m = ldsf2(xv.meta + 8u * static_cast<uint32_t>(e >> 4));
         x.sc[q] = m.x;
         x.sum[q] = m.y;
     }
@@ -65,10 +65,10 @@ __device__ __forceinline__ void kscale(uint32_t W0, uint32_t W1, uint32_t W2, in
 
 // Q4_K / Q5_K unit dot.  `row` is the row start in shared memory (16-byte aligned).
 template <bool Q5>
-__device__ __forceinline__ float dot_qk45(const uint8_t* row, int u, const XU& x) {
+__device__ __forceinline__ float dot_qk45(uint32_t row, int u, const XU& x) {
     constexpr int BB = Q5 ? 176 : 144;
     constexpr int QS = Q5 ? 48 : 16;
-    const uint8_t* blk = row + (u >> 2) * BB;
+    const uint32_t blk = row + static_cast<uint32_t>((u >> 2) * BB);
     const int g = u & 3;
     uint4 hd = lds128(blk);
     uint4 qa = lds128(blk + QS + 32 * g);
@@ -109,8 +109,8 @@ __device__ __forceinline__ float dot_qk45(const uint8_t* row, int u, const XU& x
 }
 
 // Q8_0 unit dot (two 34-byte blocks at byte 68*u of the row; 4-byte aligned).
-__device__ __forceinline__ float dot_q8_0(const uint8_t* row, int u, const XU& x) {
-    const uint8_t* b = row + 68 * u;
+__device__ __forceinline__ float dot_q8_0(uint32_t row, int u, const XU& x) {
+    const uint32_t b = row + 68u * static_cast<uint32_t>(u);
     uint32_t w0 = lds32(b);        // d0 | q0[0..1]
     uint32_t w8 = lds32(b + 32);   // q0[30..31] | d1
     const float d0 = h2f_bits(w0), d1 = h2f_bits(w8 >> 16);
@@ -132,14 +132,14 @@ __device__ __forceinline__ float dot_q8_0(const uint8_t* row, int u, const XU& x
 }
 
 // Q6_K unit dot (210-byte blocks: 2-byte aligned in general).
-__device__ __forceinline__ float dot_q6_k(const uint8_t* row, int u, const XU& x) {
-    const uint8_t* blk = row + 210 * (u >> 2);
+__device__ __forceinline__ float dot_q6_k(uint32_t row, int u, const XU& x) {
+    const uint32_t blk = row + 210u * static_cast<uint32_t>(u >> 2);
     const int h = (u >> 1) & 1, a = u & 1;
     uint4 l0 = lds128_any(blk + 64 * h + 16 * a);
     uint4 l1 = lds128_any(blk + 64 * h + 32 + 16 * a);
     uint4 qh = lds128_any(blk + 128 + 32 * h + 16 * a);
     uint32_t s0 = lds32_any(blk + 192 + 8 * h), s1 = lds32_any(blk + 196 + 8 * h);
-    const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(blk + 208));
+    const float d = h2f_bits(lds16(blk + 208));
     // scales[8h + 2q + a], q = 0..3 -> bytes a, a+2 of s0 and a, a+2 of s1
     const uint32_t sa = 8u * static_cast<uint32_t>(a);
     const float sc[4] = {static_cast<float>(static_cast<int8_t>((s0 >> sa) & 255u)),
@@ -174,7 +174,7 @@ __device__ __forceinline__ float dot_q6_k(const uint8_t* row, int u, const XU& x
     return r;
 }
 
-__device__ __forceinline__ float unit_dot(int type, const uint8_t* row, int u, const XU& x) {
+__device__ __forceinline__ float unit_dot(int type, uint32_t row, int u, const XU& x) {
     switch (type) {
         case T_Q4_K: return dot_qk45<false>(row, u, x);
         case T_Q5_K: return dot_qk45<true>(row, u, x);

@@ -24,7 +24,7 @@ QMOE_ERR_ROUTING = 10
 QMOE_ERR_NOT_NORMALIZED = 11
 QMOE_ERR_TIMEOUT = 12
 
-WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR = range(8)
+WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR, WS_INPUT = range(9)
 
 
 class QmoeTensor(ctypes.Structure):
@@ -61,7 +61,11 @@ SIGNATURES = [
                                   c_size_t, c_void_p]),
     ("qmoe_block_forward", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_void_p, c_int,
                                    c_void_p, c_size_t, c_void_p]),
+    ("qmoe_block_forward_prenorm", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_float,
+                                           c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     ("qmoe_check_errors", c_int, [c_void_p, POINTER(QmoeDims), POINTER(c_uint32), c_void_p]),
+    ("qmoe_trace_enable", c_int, [c_void_p, c_size_t]),
+    ("qmoe_trace_bytes", c_size_t, []),
     ("qmoe_workspace_init", c_int, [c_void_p, c_size_t, c_void_p]),
     ("qmoe_synth_fill", c_int, [c_void_p, c_uint32, c_uint64, c_uint64, c_uint64, c_float, c_void_p]),
     ("qmoe_synth_fill_host", c_int, [c_void_p, c_uint32, c_uint64, c_uint64, c_uint64, c_float]),
