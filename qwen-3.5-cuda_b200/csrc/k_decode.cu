@@ -160,9 +160,10 @@ __device__ __forceinline__ void write_planes4(float4 v, uint8_t* base, int K, in
     const uint32_t w0 = (X0 & 255u) | ((X1 & 255u) << 8) | ((X2 & 255u) << 16) | ((X3 & 255u) << 24);
     const uint32_t w1 = ((X0 >> 8) & 255u) | (((X1 >> 8) & 255u) << 8) | (((X2 >> 8) & 255u) << 16) | (((X3 >> 8) & 255u) << 24);
     const uint32_t w2 = ((X0 >> 16) & 255u) | (((X1 >> 16) & 255u) << 8) | (((X2 >> 16) & 255u) << 16) | (((X3 >> 16) & 255u) << 24);
-    *reinterpret_cast<uint32_t*>(base + e0) = w0;
-    *reinterpret_cast<uint32_t*>(base + K + e0) = w1;
-    *reinterpret_cast<uint32_t*>(base + 2 * K + e0) = w2;
+    const uint32_t o = pswz(static_cast<uint32_t>(e0));
+    *reinterpret_cast<uint32_t*>(base + o) = w0;
+    *reinterpret_cast<uint32_t*>(base + K + o) = w1;
+    *reinterpret_cast<uint32_t*>(base + 2 * K + o) = w2;
     if ((lane & 3) == 0) reinterpret_cast<float2*>(base + 3 * K)[e0 >> 4] = make_float2(scale, s16);
 }
 
@@ -172,65 +173,105 @@ __device__ __forceinline__ uint32_t fkey(float v) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+__device__ __forceinline__ float fkey_inv(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+// 64-bit sort key of a lane's candidate i: logit key, then lower i first
+__device__ __forceinline__ uint64_t cand_key(uint32_t key, int i) {
+    return (static_cast<uint64_t>(key) << 8) | static_cast<uint32_t>(7 - i);
+}
+__device__ __forceinline__ void cex(uint64_t& a, uint64_t& b) {  // a <- max, b <- min
+    const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
+    a = hi;
+    b = lo;
+}
+
 // Top-k + softmax + validation for every token, then the permutation and the
 // packed schedule.  Runs in the single CTA that finished the router last.
 //
-// Selection (moe.cu:19-36): k rounds of "largest remaining logit, lowest index
-// on ties": each lane offers its best unused logit (ascending scan with a
-// strict >, so its lowest index among equals), one redux picks the largest
-// key, a second the lowest expert id among lanes holding that key.
+// Selection (moe.cu:19-36): k rounds of "largest remaining logit, lowest
+// index on ties".  Each lane holds the logits of experts lane + 32 i, sorted
+// once (descending key, ascending i) by an 8-input Batcher network; a round is
+// then one redux for the largest head key and one for the lowest expert id
+// among the lanes whose head holds it, after which the winning lane pops its
+// head.
+//
+// Dispatch: a token picks an expert at most once, so each expert's pairs are
+// described by a token bitmask (T <= 32).  One block-wide exclusive scan of
+// (pair count, active flag) per expert gives the expert offsets and the
+// source index of every active expert; a pair's permuted position is its
+// expert's offset plus the number of earlier tokens in the mask -- the stable
+// (expert, pair) order of a counting sort.
 __device__ void topk_and_schedule(const DecodeParams& P) {
     constexpr int MP = kDecodeMaxT * kMaxTopK;
+    static_assert(kDecodeMaxT <= 32, "token masks are 32-bit");
+    static_assert(RT_WARPS * 32 * 2 >= kMaxExperts, "two experts per thread in the scan");
+    __shared__ uint32_t s_mask[kMaxExperts];
+    __shared__ int s_off[kMaxExperts];
     __shared__ int s_idx[MP];
-    __shared__ int s_rank[MP];
-    __shared__ int s_perm[MP];
-    __shared__ int s_first[MP + 1];
-    __shared__ int s_nact;
+    __shared__ uint32_t s_wsum[RT_WARPS];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int E = P.E, k = P.k, LS = E + 1;
     const int NP = P.T * k;
+    for (int e = threadIdx.x; e < kMaxExperts; e += blockDim.x) s_mask[e] = 0u;
+    __syncthreads();
 
     for (int t = warp; t < P.T; t += RT_WARPS) {
-        float v[8];
-        uint32_t key[8];
+        uint64_t c[8];
         uint32_t amax = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane + 32 * i;
-            v[i] = e < E ? __ldcg(P.logits + t * LS + e) : 0.0f;
-            key[i] = e < E ? fkey(v[i]) : 0u;
-            amax = max(amax, e < E ? (__float_as_uint(v[i]) & 0x7FFFFFFFu) : 0u);
+            const float v = e < E ? __ldcg(P.logits + t * LS + e) : 0.0f;
+            c[i] = cand_key(e < E ? fkey(v) : 0u, i);
+            amax = max(amax, e < E ? (__float_as_uint(v) & 0x7FFFFFFFu) : 0u);
         }
         const bool finite = __reduce_max_sync(FULL, amax) < 0x7F800000u;
-        uint32_t used = 0;
+        // Batcher odd-even merge sort of 8 (19 comparators)
+        cex(c[0], c[1]); cex(c[2], c[3]); cex(c[4], c[5]); cex(c[6], c[7]);
+        cex(c[0], c[2]); cex(c[1], c[3]); cex(c[4], c[6]); cex(c[5], c[7]);
+        cex(c[1], c[2]); cex(c[5], c[6]);
+        cex(c[0], c[4]); cex(c[1], c[5]); cex(c[2], c[6]); cex(c[3], c[7]);
+        cex(c[2], c[4]); cex(c[3], c[5]);
+        cex(c[1], c[2]); cex(c[3], c[4]); cex(c[5], c[6]);
         int my_idx = -1;
         float my_v = 0.0f;
         if (finite) {
             for (int j = 0; j < k; ++j) {
-                uint32_t bk = 0;
-                int bi = 0x7fffffff;
-                float bv = 0.0f;
+                const uint32_t hk = static_cast<uint32_t>(c[0] >> 8);
+                const int he = lane + 32 * (7 - static_cast<int>(c[0] & 7u));
+                const uint32_t mk = __reduce_max_sync(FULL, hk);
+                const int win = static_cast<int>(__reduce_min_sync(FULL, hk == mk ? static_cast<uint32_t>(he) : 0xFFFFFFFFu));
+                if (he == win) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    if (!((used >> i) & 1u) && key[i] > bk) { bk = key[i]; bi = lane + 32 * i; bv = v[i]; }
-                const uint32_t mk = __reduce_max_sync(FULL, bk);
-                const int win = static_cast<int>(__reduce_min_sync(FULL, bk == mk ? static_cast<uint32_t>(bi) : 0xFFFFFFFFu));
-                if (bi == win) used |= 1u << (win >> 5);
-                const float wv = __shfl_sync(FULL, bv, win & 31);
-                if (lane == j) { my_idx = win; my_v = wv; }
+                    for (int i = 0; i < 7; ++i) c[i] = c[i + 1];
+                    c[7] = 0;
+                }
+                if (lane == j) { my_idx = win; my_v = fkey_inv(mk); }
             }
         }
         // softmax over the selected logits (moe.cu:41-51): max, sequential
         // sum j = 0..k-1, division
-        float mx = __shfl_sync(FULL, my_v, 0);
-        for (int j = 1; j < k; ++j) mx = fmaxf(mx, __shfl_sync(FULL, my_v, j));
+        float sel[kMaxTopK];
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, my_v, j);
+        float mx = sel[0];
+#pragma unroll
+        for (int j = 1; j < kMaxTopK; ++j) if (j < k) mx = fmaxf(mx, sel[j]);
         const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, ex, j);
         float sum = 0.0f;
-        for (int j = 0; j < k; ++j) sum += __shfl_sync(FULL, ex, j);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) if (j < k) sum += sel[j];
         const float wj = ex / sum;
         // host-side checks of layer_moe.cpp:114-124, on the device
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, wj, j);
         float rs = 0.0f;
-        for (int j = 0; j < k; ++j) rs += __shfl_sync(FULL, wj, j);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK; ++j) if (j < k) rs += sel[j];
         const bool lane_ok = lane >= k || (my_idx >= 0 && my_idx < E && isfinite(wj) && wj >= 0.0f);
         const bool ok = finite && __all_sync(FULL, lane_ok);
         uint32_t flag = 0;
@@ -244,6 +285,7 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
             const int oi = flag ? -1 : my_idx;
             const float ow = flag ? __uint_as_float(0x7FC00000u) : wj;
             s_idx[t * k + lane] = oi;
+            if (oi >= 0) atomicOr(s_mask + oi, 1u << t);
             P.topk_idx[t * k + lane] = oi;
             P.topk_w[t * k + lane] = ow;
             if (P.out_idx) P.out_idx[t * k + lane] = oi;
@@ -252,62 +294,63 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
     }
     __syncthreads();
 
-    // stable permutation by (expert, pair): rank of pair p = #pairs with a
-    // smaller expert + #earlier pairs with the same expert
+    // exclusive scan over experts of (pairs << 16 | active), two experts per thread
+    const int e0 = 2 * threadIdx.x;
+    const uint32_t m0 = e0 < E ? s_mask[e0] : 0u, m1 = e0 + 1 < E ? s_mask[e0 + 1] : 0u;
+    const uint32_t v0 = (static_cast<uint32_t>(__popc(m0)) << 16) | (m0 ? 1u : 0u);
+    const uint32_t v1 = (static_cast<uint32_t>(__popc(m1)) << 16) | (m1 ? 1u : 0u);
+    uint32_t inc = v0 + v1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) s_wsum[warp] = inc;
+    __syncthreads();
+    uint32_t base = 0, total = 0;
+    for (int w = 0; w < RT_WARPS; ++w) {
+        const uint32_t ws = s_wsum[w];
+        base += w < warp ? ws : 0u;
+        total += ws;
+    }
+    const uint32_t ex0 = base + inc - v0 - v1, ex1 = ex0 + v0;
+    const int npairs = static_cast<int>(total >> 16), nact = static_cast<int>(total & 0xFFFFu);
+    const int poff = sched_perm_off(P.T, k, E), toff = sched_tok_off(P.T, k, E);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int e = e0 + h;
+        const uint32_t ex = h ? ex1 : ex0, m = h ? m1 : m0;
+        if (e < E) {
+            s_off[e] = static_cast<int>(ex >> 16);
+            P.offsets[e] = static_cast<int>(ex >> 16);
+            if (m) {
+                const int s2 = static_cast<int>(ex & 0xFFFFu);
+                P.active[s2] = e;
+                P.sched[SCHED_HDR + 3 * s2] = e;
+                P.sched[SCHED_HDR + 3 * s2 + 1] = static_cast<int>(ex >> 16);
+                P.sched[SCHED_HDR + 3 * s2 + 2] = __popc(m);
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        P.offsets[E] = npairs;
+        P.sched[0] = nact;
+        P.sched[1] = npairs;
+        P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(nact);
+        P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(npairs);
+    }
+    __syncthreads();
     for (int p = threadIdx.x; p < NP; p += blockDim.x) {
         const int e = s_idx[p];
         int rank = -1;
-        if (e >= 0 && e < E) {
-            rank = 0;
-            for (int q = 0; q < NP; ++q) {
-                const int f = s_idx[q];
-                rank += (f >= 0 && (f < e || (f == e && q < p))) ? 1 : 0;
-            }
-            s_perm[rank] = p;
+        if (e >= 0) {
+            const int t = p / k;
+            rank = s_off[e] + __popc(s_mask[e] & ((1u << t) - 1u));
+            P.perm[rank] = p;
+            P.sched[poff + rank] = p;
+            P.sched[toff + rank] = t;
         }
-        s_rank[p] = rank;
         P.inv_perm[p] = rank;
-    }
-    __syncthreads();
-    int npairs = 0;
-    for (int q = 0; q < NP; ++q) npairs += s_rank[q] >= 0 ? 1 : 0;
-    for (int i = threadIdx.x; i < npairs; i += blockDim.x)
-        s_first[i] = (i == 0 || s_idx[s_perm[i]] != s_idx[s_perm[i - 1]]) ? 1 : 0;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int i = 0; i < npairs; ++i) n += s_first[i];
-        s_nact = n;
-    }
-    // offsets[e] = number of valid pairs routed to experts < e
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
-        int c = 0;
-        for (int q = 0; q < NP; ++q) c += (s_idx[q] >= 0 && s_idx[q] < e) ? 1 : 0;
-        P.offsets[e] = c;
-    }
-    const int maxs = sched_max_src(P.T, k, E);
-    const int poff = sched_perm_off(P.T, k, E), toff = sched_tok_off(P.T, k, E);
-    for (int i = threadIdx.x; i < npairs; i += blockDim.x) {
-        P.perm[i] = s_perm[i];
-        P.sched[poff + i] = s_perm[i];
-        P.sched[toff + i] = s_perm[i] / k;
-        if (s_first[i]) {
-            int s = 0, c = 1;
-            for (int q = 0; q < i; ++q) s += s_first[q];
-            while (i + c < npairs && !s_first[i + c]) ++c;
-            const int e = s_idx[s_perm[i]];
-            P.active[s] = e;
-            P.sched[SCHED_HDR + 3 * s] = e;
-            P.sched[SCHED_HDR + 3 * s + 1] = i;
-            P.sched[SCHED_HDR + 3 * s + 2] = c;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        P.sched[0] = s_nact;
-        P.sched[1] = npairs;
-        P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(s_nact);
-        P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(npairs);
     }
 }
 
@@ -451,9 +494,10 @@ __device__ __forceinline__ void xq_block32_global(float v, uint8_t* base, int K,
     float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
     const int X = bad ? 0 : __float2int_rn(v * mul);
     if (bad) scale = __uint_as_float(0x7FC00000u);
-    base[e0 + lane] = static_cast<uint8_t>(X & 255);
-    base[K + e0 + lane] = static_cast<uint8_t>((X >> 8) & 255);
-    base[2 * K + e0 + lane] = static_cast<uint8_t>((X >> 16) & 255);
+    const uint32_t o = pswz(static_cast<uint32_t>(e0 + lane));
+    base[o] = static_cast<uint8_t>(X & 255);
+    base[K + o] = static_cast<uint8_t>((X >> 8) & 255);
+    base[2 * K + o] = static_cast<uint8_t>((X >> 16) & 255);
     if ((lane & 15) == 0) reinterpret_cast<float2*>(base + 3 * K)[(e0 >> 4) + (lane >> 4)] = make_float2(scale, s16);
 }
 
@@ -570,7 +614,8 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
     // ---------------- consumers ----------------
     mbar_wait(xbar, 0, P.ctrl);
     if (threadIdx.x == 0) QMOE_TRACE(P, 1, 3);
-    const int u = lane & (U - 1), rsub = lane >> lgU;
+    const int ul = lane & (U - 1), rsub = lane >> lgU;
+    const int u_r = unit_of_lane<TR>(ul, lgU), u_s = unit_of_lane<TS>(ul, lgU);
     const int lgS = 5 - lgR;  // steps per item = 32 / rows-per-step
     XU xr;
     int cur_key = -1;
@@ -608,23 +653,23 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
             const int key = (tok << 1) | (routed ? 1 : 0);
             if (key != cur_key) {
                 const XPlanesView xv = planes_view(smem_u32(xs) + static_cast<uint32_t>(tok) * static_cast<uint32_t>(P.xq_stride), d);
-                if (routed) load_xu(xr, xv, TR, u); else load_xu(xr, xv, TS, u);
+                if (routed) load_xu<TR>(xr, xv, u_r); else load_xu<TS>(xr, xv, u_s);
                 cur_key = key;
             }
             const int rl = (st << lgR) + rsub;
             float g, up;
             if (routed) {
-                g = unit_dot_t<TR>(dg + static_cast<uint32_t>(rl) * rb, u, xr);
-                up = unit_dot_t<TR>(du + static_cast<uint32_t>(rl) * rb, u, xr);
+                g = unit_dot_t<TR>(dg + static_cast<uint32_t>(rl) * rb, u_r, xr);
+                up = unit_dot_t<TR>(du + static_cast<uint32_t>(rl) * rb, u_r, xr);
             } else {
-                g = unit_dot_t<TS>(dg + static_cast<uint32_t>(rl) * rb, u, xr);
-                up = unit_dot_t<TS>(du + static_cast<uint32_t>(rl) * rb, u, xr);
+                g = unit_dot_t<TS>(dg + static_cast<uint32_t>(rl) * rb, u_s, xr);
+                up = unit_dot_t<TS>(du + static_cast<uint32_t>(rl) * rb, u_s, xr);
             }
             for (int o = U >> 1; o; o >>= 1) {
                 g += __shfl_xor_sync(FULL, g, o);
                 up += __shfl_xor_sync(FULL, up, o);
             }
-            if (u == 0) stsf(smem_u32(hb) + 4u * static_cast<uint32_t>(rl * P.T + ti), silu_mul(g, up));
+            if (ul == 0) stsf(smem_u32(hb) + 4u * static_cast<uint32_t>(rl * P.T + ti), silu_mul(g, up));
         }
         asm volatile("bar.sync 1, %0;" ::"r"(GU_NCW * 32) : "memory");
         if (threadIdx.x == 0 && kk == 0) QMOE_TRACE(P, 1, 5);
@@ -797,18 +842,21 @@ __global__ void __launch_bounds__(XK_THREADS, 2)
                 if (vi != cur_vi) {
                     const XPlanesView hv =
                         planes_view(smem_u32(hs) + static_cast<uint32_t>(vid) * static_cast<uint32_t>(P.hq_stride), P.H);
-                    if (shv) load_xu(xr, hv, TS, lane & (Us - 1)); else load_xu(xr, hv, TR, lane & (Ur - 1));
+                    if (shv) load_xu<TS>(xr, hv, unit_of_lane<TS>(lane & (Us - 1), lgUs));
+                    else load_xu<TR>(xr, hv, unit_of_lane<TR>(lane & (Ur - 1), lgUr));
                     cur_vi = vi;
                 }
-                const int u = lane & ((1 << lgU) - 1), rsub = lane >> lgU;
+                const int ul = lane & ((1 << lgU) - 1), rsub = lane >> lgU;
                 const int rl = (st << (5 - lgU)) + rsub;
                 const bool valid = rl < nrow;
                 float y = 0.0f;
                 if (valid)
-                    y = shv ? unit_dot_t<TS>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbs), u, xr)
-                            : unit_dot_t<TR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbd), u, xr);
+                    y = shv ? unit_dot_t<TS>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbs),
+                                             unit_of_lane<TS>(ul, lgUs), xr)
+                            : unit_dot_t<TR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbd),
+                                             unit_of_lane<TR>(ul, lgUr), xr);
                 for (int o = (1 << lgU) >> 1; o; o >>= 1) y += __shfl_xor_sync(FULL, y, o);
-                if (valid && u == 0) stsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
+                if (valid && ul == 0) stsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
                 // advance the cursor
                 if (++st == (shv ? steps_s : steps_r)) {
                     st = 0;

@@ -230,24 +230,13 @@ struct XPlanesView {
 // the meta of the two 16-element halves.  The largest magnitude comes from one
 // redux over the IEEE bits (non-negative floats order like unsigned ints;
 // anything >= 0x7F800000 is inf/NaN).
-__device__ __forceinline__ void xq_block32(float v, uint32_t p0, uint32_t p1, uint32_t p2, uint32_t meta16,
-                                           int lane) {
-    const uint32_t ab = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
-    float s16 = v;
-#pragma unroll
-    for (int o = 8; o; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-    const bool bad = ab >= 0x7F800000u;
-    const uint32_t eb = ab >> 23;  // biased exponent of the largest magnitude
-    int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
-    sh = sh > 126 ? 126 : sh;
-    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
-    float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-    const int X = bad ? 0 : __float2int_rn(v * mul);
-    if (bad) scale = __uint_as_float(0x7FC00000u);
-    sts8(p0, static_cast<uint32_t>(X) & 255u);
-    sts8(p1, (static_cast<uint32_t>(X) >> 8) & 255u);
-    sts8(p2, (static_cast<uint32_t>(X) >> 16) & 255u);
-    if ((lane & 15) == 0) stsf2(meta16 + 8u * static_cast<uint32_t>(lane >> 4), scale, s16);
+// Byte position of element e inside one activation plane.  The 16-byte
+// chunk c = e/16 is stored at chunk c ^ ((c/8) % 8): the eight lanes of a
+// quarter-warp that read the four 16-element runs of eight consecutive
+// 64-element units then hit eight different 16-byte bank groups.
+__device__ __forceinline__ uint32_t pswz(uint32_t e) {
+    const uint32_t c = e >> 4;
+    return ((c ^ ((c >> 3) & 7u)) << 4) | (e & 15u);
 }
 
 // Combines the three plane partial sums into sum(q * X) (one rounding).

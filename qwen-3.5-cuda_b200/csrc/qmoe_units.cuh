@@ -2,6 +2,9 @@
 // shared memory, read in place -- no repacking) against the 24-bit activation
 // planes of qmoe_dev.cuh.
 //
+// Activation planes are stored with the chunk swizzle pswz() of
+// qmoe_dev.cuh; weight rows are read as they are.
+//
 // Block layouts are the GGML ones the reference decodes per element in
 // src/cuda/matmul_q4.cu:30-129; here a lane decodes a whole unit at once:
 //   Q4_K (144 B / 256): unit u -> super-block u/4, 32 qs bytes at 16+32*(u%4);
@@ -35,19 +38,43 @@ __device__ __forceinline__ int unit_run_start(int type, int u, int q) {
     return 64 * u + 16 * q;
 }
 
-__device__ __forceinline__ void load_xu(XU& x, const XPlanesView& xv, int type, int u) {
+// Unit handled by lane index i (0..U-1, U = 2^lgU units per row).  Identity
+// except for Q6_K rows of at least 16 units, where the runs of unit u start
+// at chunk 8(u/2) + 2q + u%2 of the plane: lanes are spread so that every
+// quarter-warp reads eight distinct bank groups of the swizzled planes.
+template <int TYPE>
+__device__ __forceinline__ int unit_of_lane(int i, int lgU) {
+    if (TYPE != T_Q6_K || lgU < 4) return i;
+    const int m = 2 * ((i >> 1) & 3) + ((i >> 3) & 1) + 8 * (i >> 4);
+    return 2 * m + (i & 1);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void load_xu(XU& x, const XPlanesView& xv, int u) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        int e = unit_run_start(type, u, q);
-        const uint4 a = lds128(xv.p0 + e);
-        const uint4 b = lds128(xv.p1 + e);
-        const uint4 c = lds128(xv.p2 + e);
+        const uint32_t o = pswz(static_cast<uint32_t>(unit_run_start(TYPE, u, q)));
+        const uint4 a = lds128(xv.p0 + o);
+        const uint4 b = lds128(xv.p1 + o);
+        const uint4 c = lds128(xv.p2 + o);
         x.x0[4 * q] = a.x; x.x0[4 * q + 1] = a.y; x.x0[4 * q + 2] = a.z; x.x0[4 * q + 3] = a.w;
         x.x1[4 * q] = b.x; x.x1[4 * q + 1] = b.y; x.x1[4 * q + 2] = b.z; x.x1[4 * q + 3] = b.w;
         x.x2[4 * q] = c.x; x.x2[4 * q + 1] = c.y; x.x2[4 * q + 2] = c.z; x.x2[4 * q + 3] = c.w;
-        const float2 m = ldsf2(xv.meta + 8u * static_cast<uint32_t>(e >> 4));
-        x.sc[q] = m.x;
-        x.sum[q] = m.y;
+    }
+    if (TYPE == T_Q6_K) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 m = ldsf2(xv.meta + 8u * static_cast<uint32_t>(unit_run_start(TYPE, u, q) >> 4));
+            x.sc[q] = m.x;
+            x.sum[q] = m.y;
+        }
+    } else {  // the four runs' meta entries are contiguous: 32 bytes at 32u
+        const uint4 m0 = lds128(xv.meta + 32u * static_cast<uint32_t>(u));
+        const uint4 m1 = lds128(xv.meta + 32u * static_cast<uint32_t>(u) + 16u);
+        x.sc[0] = __uint_as_float(m0.x); x.sum[0] = __uint_as_float(m0.y);
+        x.sc[1] = __uint_as_float(m0.z); x.sum[1] = __uint_as_float(m0.w);
+        x.sc[2] = __uint_as_float(m1.x); x.sum[2] = __uint_as_float(m1.y);
+        x.sc[3] = __uint_as_float(m1.z); x.sum[3] = __uint_as_float(m1.w);
     }
 }
 
