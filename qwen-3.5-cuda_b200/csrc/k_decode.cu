@@ -112,7 +112,8 @@ __device__ __forceinline__ float reg_dot(const float4 (&w)[CH][2], const float4 
 // (ops.cu:33-64) (x * rsqrt(mean(x^2) + eps)) * weight -- the sum of squares
 // has exactly the GEMV's thread/shuffle structure, so reg_dot(x, x) is it.
 template <int CH>
-__device__ __forceinline__ void load_input(float4 (&xr)[CH][2], const DecodeParams& P, const float* x, int lane) {
+__device__ __forceinline__ void load_input(float4 (&xr)[CH][2], const DecodeParams& P, const float* x,
+                                           const float* s_nw, int lane) {
 #pragma unroll
     for (int i = 0; i < CH; ++i)
 #pragma unroll
@@ -124,7 +125,7 @@ __device__ __forceinline__ void load_input(float4 (&xr)[CH][2], const DecodePara
         for (int i = 0; i < CH; ++i)
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const float4 nv = __ldg(reinterpret_cast<const float4*>(P.norm_w + 256 * i + 128 * hh + 4 * lane));
+                const float4 nv = *reinterpret_cast<const float4*>(s_nw + 256 * i + 128 * hh + 4 * lane);
                 xr[i][hh].x = __fmul_rn(__fmul_rn(xr[i][hh].x, sc), nv.x);
                 xr[i][hh].y = __fmul_rn(__fmul_rn(xr[i][hh].y, sc), nv.y);
                 xr[i][hh].z = __fmul_rn(__fmul_rn(xr[i][hh].z, sc), nv.z);
@@ -185,6 +186,33 @@ __device__ __forceinline__ void cex(uint64_t& a, uint64_t& b) {  // a <- max, b 
     const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
     a = hi;
     b = lo;
+}
+
+// Softmax over the k selected logits held by lanes 0..k-1 (moe.cu:41-51):
+// max, then exp(v - max) summed sequentially over j = 0..k-1, then one
+// division per weight.  `rs` is the sequential sum of the weights, checked by
+// the caller as layer_moe.cpp:114-124 does on the host.  KM >= k bounds the
+// unrolled chains.
+template <int KM>
+__device__ __forceinline__ void softmax_selected(float my_v, int k, int lane, float& wj, float& rs) {
+    float sel[KM];
+#pragma unroll
+    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, my_v, j);
+    float mx = sel[0];
+#pragma unroll
+    for (int j = 1; j < KM; ++j) if (j < k) mx = fmaxf(mx, sel[j]);
+    const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, ex, j);
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) if (j < k) sum += sel[j];
+    wj = ex / sum;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, wj, j);
+    rs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < KM; ++j) if (j < k) rs += sel[j];
 }
 
 // Top-k + softmax + validation for every token, then the permutation and the
@@ -251,27 +279,10 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
                 if (lane == j) { my_idx = win; my_v = fkey_inv(mk); }
             }
         }
-        // softmax over the selected logits (moe.cu:41-51): max, sequential
-        // sum j = 0..k-1, division
-        float sel[kMaxTopK];
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, my_v, j);
-        float mx = sel[0];
-#pragma unroll
-        for (int j = 1; j < kMaxTopK; ++j) if (j < k) mx = fmaxf(mx, sel[j]);
-        const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, ex, j);
-        float sum = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) if (j < k) sum += sel[j];
-        const float wj = ex / sum;
-        // host-side checks of layer_moe.cpp:114-124, on the device
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) sel[j] = __shfl_sync(FULL, wj, j);
-        float rs = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxTopK; ++j) if (j < k) rs += sel[j];
+        // softmax over the selected logits (moe.cu:41-51)
+        float wj, rs;
+        if (k <= 8) softmax_selected<8>(my_v, k, lane, wj, rs);
+        else softmax_selected<kMaxTopK>(my_v, k, lane, wj, rs);
         const bool lane_ok = lane >= k || (my_idx >= 0 && my_idx < E && isfinite(wj) && wj >= 0.0f);
         const bool ok = finite && __all_sync(FULL, lane_ok);
         uint32_t flag = 0;
@@ -371,18 +382,25 @@ __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
         const uint8_t* row = gw < P.E ? P.router + static_cast<size_t>(gw) * P.d * router_esize(type) : P.sgate_inp;
         load_router_row<CH>(w, row, type, lane);
     }
+    // the norm weights (shared memory) and this row's bias are weights too
+    __shared__ __align__(16) float s_nw[kMaxNormDim];
+    if (P.prenorm)
+        for (int i = threadIdx.x; i < P.d / 4; i += blockDim.x)
+            reinterpret_cast<float4*>(s_nw)[i] = __ldg(reinterpret_cast<const float4*>(P.norm_w) + i);
+    const float bias_v = (has_row && gw < P.E && P.bias) ? __ldg(P.bias + gw) : 0.0f;
     pdl_trigger();
-    pdl_wait();
+    if (threadIdx.x == 0) pdl_wait();  // one waiter; the CTA barrier releases the rest
+    __syncthreads();
     if (threadIdx.x == 0) QMOE_TRACE(P, 0, 1);
 
     if (has_row || writer) {
         for (int t = 0; t < P.T; ++t) {
             float4 xr[CH][2];
-            load_input<CH>(xr, P, P.x + static_cast<size_t>(t) * P.d, lane);
+            load_input<CH>(xr, P, P.x + static_cast<size_t>(t) * P.d, s_nw, lane);
             if (has_row) {
                 float v = reg_dot<CH>(w, xr);
                 if (lane == 0) {
-                    if (gw < P.E && P.bias) v = __fadd_rn(v, __ldg(P.bias + gw));
+                    if (gw < P.E && P.bias) v = __fadd_rn(v, bias_v);
                     P.logits[t * LS + gw] = v;
                 }
             }
@@ -395,7 +413,6 @@ __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
                         for (int hh = 0; hh < 2; ++hh) {
                             const int e0 = 256 * ii + 128 * hh + 4 * lane;
                             *reinterpret_cast<float4*>(P.xnorm + static_cast<size_t>(t) * P.d + e0) = xr[ii][hh];
-                            write_planes4(xr[ii][hh], P.xq + static_cast<size_t>(t) * P.xq_stride, P.d, e0, lane);
                         }
             }
         }
@@ -501,6 +518,40 @@ __device__ __forceinline__ void xq_block32_global(float v, uint8_t* base, int K,
     if ((lane & 15) == 0) reinterpret_cast<float2*>(base + 3 * K)[(e0 >> 4) + (lane >> 4)] = make_float2(scale, s16);
 }
 
+__device__ __forceinline__ int ilog2(int v) { return 31 - __clz(v); }
+
+// Block input x_in (F32, written by the router) of every token -> 24-bit
+// planes in shared memory (token stride xq_stride).  Each warp quantises
+// 128-element chunks (lanes 8m..8m+7 hold one 32-block); every load is issued
+// before the first plane is written.  NTHREADS is a multiple of 32 and
+// T * d / 4 a multiple of 32, so each chunk test is warp-uniform.
+template <int NTHREADS>
+__device__ __forceinline__ void x_planes_smem(uint8_t* xs, const DecodeParams& P, int tid) {
+    const int lq = ilog2(P.d) - 2;  // float4s per token = 2^lq
+    const int nv = P.T << lq;
+    const int lane = tid & 31;
+    constexpr int J = 8;
+    float4 v[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int g = tid + j * NTHREADS;
+        if (g < nv) v[j] = __ldcg(reinterpret_cast<const float4*>(P.xnorm) + g);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int g = tid + j * NTHREADS;
+        if (g < nv) {
+            const int t = g >> lq;
+            write_planes4(v[j], xs + static_cast<size_t>(t) * P.xq_stride, P.d, (g - (t << lq)) * 4, lane);
+        }
+    }
+    for (int g = tid + J * NTHREADS; g < nv; g += NTHREADS) {
+        const int t = g >> lq;
+        write_planes4(__ldcg(reinterpret_cast<const float4*>(P.xnorm) + g), xs + static_cast<size_t>(t) * P.xq_stride,
+                      P.d, (g - (t << lq)) * 4, lane);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Expert gate/up
 //
@@ -516,7 +567,6 @@ constexpr int GU_NCW = 16;
 constexpr int GU_THREADS = (GU_NCW + 1) * 32;
 constexpr int ITEM_ROWS = 32;
 
-__device__ __forceinline__ int ilog2(int v) { return 31 - __clz(v); }
 
 template <int TR, int TS>
 __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int nst, uint32_t half_bytes, int dn_rows) {
@@ -527,7 +577,6 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
     const int lgR = 5 - lgU;                        // rows per warp step = 32 / U
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + 8;
-    uint64_t* xbar = empty + 8;
     int* s_sched = reinterpret_cast<int*>(smem + 256);
     uint8_t* xs = reinterpret_cast<uint8_t*>(s_sched) + align_up(SCHED_SMEM_WORDS * 4, 128);
     const uint32_t xs_bytes = static_cast<uint32_t>(P.xq_stride) * static_cast<uint32_t>(P.T);
@@ -541,7 +590,6 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
     if (threadIdx.x == 0) {
         QMOE_TRACE(P, 1, 0);
         for (int i = 0; i < nst; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, GU_NCW); }
-        mbar_init(xbar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -559,13 +607,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
     };
     // prologue: a shared-expert item does not depend on the routing
     if (warp == GU_NCW && lane == 0 && c < nb_sh) issue(0, true, -1, c * ITEM_ROWS);
-    pdl_wait();  // the router has finished: schedule and block input are valid
+    if (threadIdx.x == 0) pdl_wait();  // the router has finished: schedule and block input are valid
+    __syncthreads();
     if (threadIdx.x == 0) QMOE_TRACE(P, 1, 1);
-    if (warp == GU_NCW && lane == 0) {
-        mbar_arrive_expect_tx(xbar, xs_bytes);
-        bulk_g2s(xs, P.xq, xs_bytes, xbar, P.ctrl);
-    }
     load_sched(s_sched, P);
+    x_planes_smem<GU_THREADS>(xs, P, threadIdx.x);
     __syncthreads();
     const int nact = s_sched[0];
     const int* s_perm = s_sched + sched_perm_off(P.T, P.k, P.E);
@@ -606,13 +652,11 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gateup(DecodeParams P, int ns
                 }
                 if (++slot == nst) { slot = 0; ++round; }
             }
-            mbar_wait(xbar, 0, P.ctrl);
         }
         return;
     }
 
     // ---------------- consumers ----------------
-    mbar_wait(xbar, 0, P.ctrl);
     if (threadIdx.x == 0) QMOE_TRACE(P, 1, 3);
     const int ul = lane & (U - 1), rsub = lane >> lgU;
     const int u_r = unit_of_lane<TR>(ul, lgU), u_s = unit_of_lane<TS>(ul, lgU);
@@ -763,8 +807,8 @@ __global__ void __launch_bounds__(XK_THREADS, 2)
         // ---------------- producer ----------------
         if (lane == 0)
             for (int cc = sh; cc < min(nsrc, nst); ++cc) issue(cc, cc);
-        pdl_wait();  // the planes of silu(g)*u are written
         if (lane == 0) {
+            pdl_wait();  // the planes of silu(g)*u are written
             mbar_arrive_expect_tx(full + nst, hs_bytes);
             bulk_g2s(hs, P.hq, hs_bytes, full + nst, P.ctrl);
         }
@@ -777,10 +821,11 @@ __global__ void __launch_bounds__(XK_THREADS, 2)
         if (lane == 0) mbar_wait(full + nst, 0, P.ctrl);
         return;
     }
-    pdl_wait();
+    // the consumers read the planes only through the producer's copy, which
+    // it issues after its own dependency wait
+    mbar_wait(full + nst, 0, P.ctrl);
     pdl_trigger();  // the next block's router may start loading its weights
     if (threadIdx.x == 0) QMOE_TRACE(P, 2, 2);
-    mbar_wait(full + nst, 0, P.ctrl);
     if (threadIdx.x == 0) QMOE_TRACE(P, 2, 3);
 
     // Tasks are (vector, row step) in source order: the T shared vectors
@@ -884,6 +929,418 @@ __global__ void __launch_bounds__(XK_THREADS, 2)
         P.out[o] = P.residual ? s_res[t * Rd + r] + acc : acc;
     }
     if (threadIdx.x == 0) QMOE_TRACE(P, 2, 6);
+}
+
+// ---------------------------------------------------------------------------
+// Fused expert kernel: gate/up items, one grid-wide barrier, down + combine
+//
+// One CTA per SM.  Before the barrier a CTA does what k_gateup does for its
+// items and, at the same time, pulls its own down rows (rows [c*Rd, c*Rd+Rd)
+// of the shared expert and of every active expert) into shared memory; after
+// the barrier it reads the planes of every hidden vector and does what
+// k_down does.  The down rows therefore stream from HBM while the gate/up
+// items are still being computed, and no kernel boundary separates the two
+// halves.
+//
+// The barrier is a 64-bit arrival count in the workspace control words that
+// only grows: every CTA adds one (acq_rel) and waits (acquire polls) until
+// the count reaches the next multiple of the grid size.  A CTA that waits
+// longer than kGridWaitNs raises EF_TIMEOUT and goes on; the results of that
+// call are then invalid, and the count is no longer a multiple of the grid
+// size, so the workspace must be initialised again (qmoe_workspace_init).  All CTAs must be resident at
+// once: the grid is one CTA per SM and the launch asks for the whole SM's
+// worth of shared memory at most; the dependent launch is released only
+// after the barrier, so a later kernel cannot take an SM that a CTA of this
+// grid still needs.
+// ---------------------------------------------------------------------------
+constexpr int FX_NCW = 16;
+constexpr int FX_THREADS = (FX_NCW + 1) * 32;
+constexpr uint64_t kGridWaitNs = 200ull * 1000ull * 1000ull;
+
+struct FxLayout {
+    int gnst, gsub, dnst, Rd, nvec;
+    uint32_t half_bytes, dstage;
+    uint32_t off_sched, off_xs, off_hb, off_w, off_sg, off_res, off_yb, off_gu, off_dn;
+};
+
+__device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// n bytes (a multiple of 16; both ends 16-byte aligned) global -> shared with
+// plain L2 loads, threads [0, nth) taking 16 bytes each per pass
+__device__ __forceinline__ void copy_g2s16(uint8_t* dst, const uint8_t* src, uint32_t n, int tid, int nth) {
+    for (uint32_t o = 16u * static_cast<uint32_t>(tid); o < n; o += 16u * static_cast<uint32_t>(nth))
+        *reinterpret_cast<uint4*>(dst + o) = __ldcg(reinterpret_cast<const uint4*>(src + o));
+}
+
+template <int TR, int TS, int DR, int DS>
+__global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLayout L) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t* gfull = reinterpret_cast<uint64_t*>(smem);  // [8 slots][4 sub-chunks]
+    uint64_t* gempty = gfull + 32;
+    uint64_t* dfull = gempty + 8;  // [72]
+    int* s_sched = reinterpret_cast<int*>(smem + L.off_sched);
+    uint8_t* xs = smem + L.off_xs;
+    float* hb = reinterpret_cast<float*>(smem + L.off_hb);
+    float* s_w = reinterpret_cast<float*>(smem + L.off_w);
+    float* s_sg = reinterpret_cast<float*>(smem + L.off_sg);
+    float* s_res = reinterpret_cast<float*>(smem + L.off_res);
+    float* ybuf = reinterpret_cast<float*>(smem + L.off_yb);
+    uint8_t* gst = smem + L.off_gu;
+    uint8_t* hs = smem + L.off_gu;  // the gate/up stages are free once every item is done
+    uint8_t* dst = smem + L.off_dn;
+
+    const int d = P.d, G = gridDim.x, c = blockIdx.x;
+    const int lgU = ilog2(d >> 6), U = 1 << lgU, lgR = 5 - lgU;
+    const uint64_t rbg = row_bytes(TR, d), rbs = row_bytes(TS, d);
+    const uint64_t rbd = row_bytes(DR, P.F), rbsd = row_bytes(DS, P.Fs);
+    const int sh = P.has_shared ? 1 : 0;
+    const int nb_sh = sh ? P.Fs / ITEM_ROWS : 0;
+    const int lgF = ilog2(P.F / ITEM_ROWS);
+    const int Rd = L.Rd, r0d = c * Rd;
+    const int nrow = max(0, min(Rd, d - r0d));
+    const uint32_t half_bytes = L.half_bytes;
+
+    if (tid == 0) {
+        QMOE_TRACE(P, 1, 0);
+        for (int i = 0; i < L.gnst; ++i) {
+            for (int j = 0; j < L.gsub; ++j) mbar_init(gfull + 4 * i + j, 1);
+            mbar_init(gempty + i, FX_NCW);
+        }
+        for (int i = 0; i < L.dnst; ++i) mbar_init(dfull + i, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto issue_gu = [&](int slot, bool shared_src, int expert, int r0) {
+        const uint64_t rb = shared_src ? rbs : rbg;
+        const uint8_t* gsrc = shared_src ? P.sgate.p + r0 * rbs : P.gate.p + (static_cast<uint64_t>(expert) * P.F + r0) * rbg;
+        const uint8_t* usrc = shared_src ? P.sup.p + r0 * rbs : P.up.p + (static_cast<uint64_t>(expert) * P.F + r0) * rbg;
+        uint8_t* dg = gst + static_cast<size_t>(slot) * 2 * half_bytes;
+        uint8_t* du = dg + half_bytes;
+        // gsub sub-chunks of 32/gsub rows, each with its own barrier, so the
+        // consumers start on the first rows while the rest stream in (the host
+        // picks gsub > 1 only when every sub-chunk starts 16-byte aligned)
+        const uint64_t cb = (ITEM_ROWS / L.gsub) * rb;
+        for (int j = 0; j < L.gsub; ++j) {
+            const StagePlan pg = plan_stage(dg + j * cb, gsrc + j * cb, cb, shared_src ? P.sgate.end : P.gate.end);
+            const StagePlan pu = plan_stage(du + j * cb, usrc + j * cb, cb, shared_src ? P.sup.end : P.up.end);
+            uint64_t* bar = gfull + 4 * slot + j;
+            mbar_arrive_expect_tx(bar, pg.tx + pu.tx);
+            if (pg.tx) bulk_g2s(dg + j * cb, pg.lo, pg.tx, bar, P.ctrl);
+            if (pu.tx) bulk_g2s(du + j * cb, pu.lo, pu.tx, bar, P.ctrl);
+        }
+    };
+    // chunk cc = 0: shared expert (when present); cc >= sh: routed source cc - sh
+    auto dn_src = [&](int cc) -> const uint8_t* {
+        return cc < sh ? P.sdown.p + static_cast<uint64_t>(r0d) * rbsd
+                       : P.down.p + (static_cast<uint64_t>(s_sched[SCHED_HDR + 3 * (cc - sh)]) * d + r0d) * rbd;
+    };
+    auto issue_dn = [&](int cc, int slot) {
+        uint8_t* dd = dst + static_cast<size_t>(slot) * L.dstage;
+        const bool shc = cc < sh;
+        const StagePlan sp = plan_stage(dd, dn_src(cc), nrow * (shc ? rbsd : rbd), shc ? P.sdown.end : P.down.end);
+        mbar_arrive_expect_tx(dfull + slot, sp.tx);
+        if (sp.tx) bulk_g2s(dd, sp.lo, sp.tx, dfull + slot, P.ctrl);
+    };
+
+    // prologue: loads that do not depend on the routing
+    if (warp == FX_NCW && lane == 0) {
+        if (c < nb_sh) issue_gu(0, true, -1, c * ITEM_ROWS);
+        if (sh && nrow > 0) issue_dn(0, 0);
+    }
+    if (tid == 0) pdl_wait();  // the router has finished: schedule and block input are valid
+    __syncthreads();
+    if (tid == 0) QMOE_TRACE(P, 1, 1);
+    {
+        // One round trip for the schedule, the input planes, the routing
+        // weights, the shared-expert gate logit and the residual rows: every
+        // thread issues all of its loads before it stores any of them.
+        const int words = sched_words(P.T, P.k, P.E);
+        const int nw = P.T * P.k;
+        const int nres = (P.residual && nrow > 0) ? P.T * nrow : 0;
+        const int n32 = words + nw + P.T + nres;
+        const int LS = P.E + 1;
+        auto load32 = [&](int q) -> uint32_t {
+            if (q < words) return static_cast<uint32_t>(__ldcg(P.sched + q));
+            q -= words;
+            if (q < nw) return __float_as_uint(__ldcg(P.topk_w + q));
+            q -= nw;
+            if (q < P.T) return __float_as_uint(__ldcg(P.logits + q * LS + P.E));
+            q -= P.T;
+            const int t = q / nrow, r = q - t * nrow;
+            return __float_as_uint(__ldcg(P.residual + static_cast<size_t>(t) * d + r0d + r));
+        };
+        auto store32 = [&](int q, uint32_t v) {
+            if (q < words) { s_sched[q] = static_cast<int>(v); return; }
+            q -= words;
+            if (q < nw) { s_w[q] = __uint_as_float(v); return; }
+            q -= nw;
+            if (q < P.T) { s_sg[q] = sh ? 1.0f / (1.0f + expf(-__uint_as_float(v))) : 0.0f; return; }
+            q -= P.T;
+            const int t = q / nrow, r = q - t * nrow;
+            s_res[t * Rd + r] = __uint_as_float(v);
+        };
+        constexpr int J32 = 2;
+        uint32_t v32[J32];
+#pragma unroll
+        for (int j = 0; j < J32; ++j) {
+            const int q = tid + j * FX_THREADS;
+            if (q < n32) v32[j] = load32(q);
+        }
+        x_planes_smem<FX_THREADS>(xs, P, tid);  // its loads go out before these stores
+#pragma unroll
+        for (int j = 0; j < J32; ++j) {
+            const int q = tid + j * FX_THREADS;
+            if (q < n32) store32(q, v32[j]);
+        }
+        // whatever did not fit the unrolled passes (large T * k)
+        for (int q = tid + J32 * FX_THREADS; q < n32; q += FX_THREADS) store32(q, load32(q));
+    }
+    __syncthreads();
+    if (tid == 0) QMOE_TRACE(P, 1, 2);
+    const int nact = s_sched[0];
+    const int npairs = s_sched[1];
+    const int* s_perm = s_sched + sched_perm_off(P.T, P.k, P.E);
+    const int* s_tok = s_sched + sched_tok_off(P.T, P.k, P.E);
+    const int nitems = nb_sh + (nact << lgF);
+    const int ni = c < nitems ? (nitems - 1 - c) / G + 1 : 0;
+    const int nsrc = nact + sh;
+    const int dnst = L.dnst;
+
+    if (warp == FX_NCW) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            auto issue_item = [&](int slot, int i) {
+                if (i < nb_sh) {
+                    issue_gu(slot, true, -1, i * ITEM_ROWS);
+                } else {
+                    const int j = i - nb_sh;
+                    issue_gu(slot, false, s_sched[SCHED_HDR + 3 * (j >> lgF)], (j & ((1 << lgF) - 1)) * ITEM_ROWS);
+                }
+            };
+            int kk = 0, i = c, slot = 0, round = 0;
+            for (; kk < ni && kk < L.gnst; ++kk, i += G) {  // first fill of the ring
+                if (kk > 0 || i >= nb_sh) issue_item(slot, i);  // a shared item 0 went out in the prologue
+                if (++slot == L.gnst) { slot = 0; ++round; }
+            }
+            if (nrow > 0)  // this CTA's down rows of the routed sources (first round)
+                for (int cc = sh; cc < min(nsrc, dnst); ++cc) issue_dn(cc, cc);
+            for (; kk < ni; ++kk, i += G) {
+                mbar_wait(gempty + slot, (round - 1) & 1, P.ctrl);
+                issue_item(slot, i);
+                if (++slot == L.gnst) { slot = 0; ++round; }
+            }
+        }
+        for (int rb0 = dnst; rb0 < nsrc; rb0 += dnst) {  // later down rounds, if the sources do not all fit
+            asm volatile("bar.sync 2, %0;" ::"r"((FX_NCW + 1) * 32) : "memory");
+            if (lane == 0 && nrow > 0)
+                for (int cc = rb0; cc < min(nsrc, rb0 + dnst); ++cc) issue_dn(cc, cc - rb0);
+        }
+        return;
+    }
+
+    // ---------------- consumers: gate/up items ----------------
+    {
+        const int ul = lane & (U - 1), rsub = lane >> lgU;
+        const int u_r = unit_of_lane<TR>(ul, lgU), u_s = unit_of_lane<TS>(ul, lgU);
+        const int lgS = lgU;  // steps per item = 32 / rows per step
+        XU xr;
+        int cur_key = -1;
+        int i = c, slot = 0, round = 0;
+        for (int kk = 0; kk < ni; ++kk, i += G) {
+            const bool routed = i >= nb_sh;
+            int bb, expert = -1, pair0 = 0, ntok = P.T;
+            if (routed) {
+                const int j = i - nb_sh, s2 = j >> lgF;
+                bb = j & ((1 << lgF) - 1);
+                expert = s_sched[SCHED_HDR + 3 * s2];
+                pair0 = s_sched[SCHED_HDR + 3 * s2 + 1];
+                ntok = s_sched[SCHED_HDR + 3 * s2 + 2];
+            } else {
+                bb = i;
+            }
+            const int r0 = bb * ITEM_ROWS;
+            uint32_t waited = 0;  // sub-chunks of this item this warp has waited for
+            uint32_t dg = smem_u32(gst) + static_cast<uint32_t>(slot) * 2u * half_bytes;
+            uint32_t du = dg + half_bytes;
+            {
+                const uintptr_t gsrc = routed ? reinterpret_cast<uintptr_t>(P.gate.p) + (static_cast<uint64_t>(expert) * P.F + r0) * rbg
+                                              : reinterpret_cast<uintptr_t>(P.sgate.p) + static_cast<uint64_t>(r0) * rbs;
+                const uintptr_t usrc = routed ? reinterpret_cast<uintptr_t>(P.up.p) + (static_cast<uint64_t>(expert) * P.F + r0) * rbg
+                                              : reinterpret_cast<uintptr_t>(P.sup.p) + static_cast<uint64_t>(r0) * rbs;
+                dg += static_cast<uint32_t>(gsrc & 15u);
+                du += static_cast<uint32_t>(usrc & 15u);
+            }
+            const uint32_t rb = static_cast<uint32_t>(routed ? rbg : rbs);
+            const int ntask = ntok << lgS;
+            for (int tau = warp; tau < ntask; tau += FX_NCW) {
+                const int ti = tau >> lgS, st = tau & ((1 << lgS) - 1);
+                const int tok = routed ? s_tok[pair0 + ti] : ti;
+                const int key = (tok << 1) | (routed ? 1 : 0);
+                if (key != cur_key) {
+                    const XPlanesView xv = planes_view(smem_u32(xs) + static_cast<uint32_t>(tok) * static_cast<uint32_t>(P.xq_stride), d);
+                    if (routed) load_xu<TR>(xr, xv, u_r); else load_xu<TS>(xr, xv, u_s);
+                    cur_key = key;
+                }
+                const int rl = (st << lgR) + rsub;
+                const int sub = (rl * L.gsub) >> 5;  // the warp's rows lie in one sub-chunk
+                if (!((waited >> sub) & 1u)) {
+                    mbar_wait(gfull + 4 * slot + sub, round & 1, P.ctrl);
+                    waited |= 1u << sub;
+                    if (tid == 0 && kk == 0) QMOE_TRACE(P, 1, 3);
+                }
+                float g, up;
+                if (routed) {
+                    g = unit_dot_t<TR>(dg + static_cast<uint32_t>(rl) * rb, u_r, xr);
+                    up = unit_dot_t<TR>(du + static_cast<uint32_t>(rl) * rb, u_r, xr);
+                } else {
+                    g = unit_dot_t<TS>(dg + static_cast<uint32_t>(rl) * rb, u_s, xr);
+                    up = unit_dot_t<TS>(du + static_cast<uint32_t>(rl) * rb, u_s, xr);
+                }
+                for (int o = U >> 1; o; o >>= 1) {
+                    g += __shfl_xor_sync(FULL, g, o);
+                    up += __shfl_xor_sync(FULL, up, o);
+                }
+                if (ul == 0) stsf(smem_u32(hb) + 4u * static_cast<uint32_t>(rl * P.T + ti), silu_mul(g, up));
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+            // the item's 32-blocks of silu(g)*u: F32 copy and 24-bit planes
+            for (int ti = warp; ti < ntok; ti += FX_NCW) {
+                const int vid = routed ? s_perm[pair0 + ti] : P.T * P.k + ti;
+                const float v = ldsf(smem_u32(hb) + 4u * static_cast<uint32_t>(lane * P.T + ti));
+                P.hidden[static_cast<size_t>(vid) * P.H + r0 + lane] = v;
+                xq_block32_global(v, P.hq + static_cast<size_t>(vid) * P.hq_stride, P.H, r0, lane);
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+            if (lane == 0) mbar_arrive(gempty + slot);
+            if (++slot == L.gnst) { slot = 0; ++round; }
+        }
+    }
+
+    // ---------------- grid-wide barrier: every hidden vector is written ----------------
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+    if (tid == 0) {
+        QMOE_TRACE(P, 1, 4);
+        // the CTA barrier above orders every consumer's stores before this
+        // release (cumulativity); the acquire polls make all CTAs' stores
+        // visible to this CTA's threads after the CTA barrier below
+        unsigned long long* ctr = reinterpret_cast<unsigned long long*>(P.ctrl + CTRL_GRID_CTR);
+        uint64_t old;
+        asm volatile("atom.add.acq_rel.gpu.u64 %0, [%1], %2;" : "=l"(old) : "l"(ctr), "l"(1ull) : "memory");
+        const uint64_t target = (old / static_cast<uint64_t>(G) + 1u) * static_cast<uint64_t>(G);
+        if (old + 1u != target) {
+            const uint64_t t0 = gtimer();
+            while (ld_acquire_u64(ctr) < target) {
+                if (gtimer() - t0 > kGridWaitNs) {
+                    atomicOr(P.ctrl + CTRL_ERROR, EF_TIMEOUT);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        QMOE_TRACE(P, 1, 5);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+    pdl_trigger();  // the next block's router may start loading its weights
+
+    // ---------------- consumers: down + combine ----------------
+    copy_g2s16(hs, P.hq, static_cast<uint32_t>(P.hq_stride) * static_cast<uint32_t>(L.nvec), tid, FX_NCW * 32);
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+    if (tid == 0) QMOE_TRACE(P, 2, 3);
+    const int Ur = P.F >> 6, Us = P.Fs >> 6;
+    const int lgUr = ilog2(Ur), lgUs = ilog2(Us);
+    const int steps_r = (nrow + (32 >> lgUr) - 1) >> (5 - lgUr);
+    const int steps_s = (nrow + (32 >> lgUs) - 1) >> (5 - lgUs);
+    const int Tsh = sh ? P.T : 0;
+    const int nt_sh = Tsh * steps_s;
+    auto chunk_task = [&](int cc) {
+        if (cc < sh) return 0;
+        const int q = cc - sh < nact ? s_sched[SCHED_HDR + 3 * (cc - sh) + 1] : npairs;
+        return nt_sh + q * steps_r;
+    };
+    XU xr;
+    static_assert(FX_NCW == 16, "task split assumes 16 consumer warps");
+    for (int rb0 = 0, round = 0; rb0 < nsrc; rb0 += dnst, ++round) {
+        const int rend = min(nsrc, rb0 + dnst);
+        const int A = chunk_task(rb0), B = chunk_task(rend);
+        const int t_lo = A + ((warp * (B - A)) >> 4), t_hi = A + (((warp + 1) * (B - A)) >> 4);
+        if (t_lo < t_hi) {
+            int vi, st, cc;
+            if (t_lo < nt_sh) {
+                vi = t_lo / steps_s;
+                st = t_lo - vi * steps_s;
+                cc = 0;
+            } else {
+                const int q = t_lo - nt_sh;
+                const int pv = q / steps_r;
+                st = q - pv * steps_r;
+                vi = Tsh + pv;
+                cc = max(rb0, sh);
+                while (cc + 1 < rend && s_sched[SCHED_HDR + 3 * (cc + 1 - sh) + 1] <= pv) ++cc;
+            }
+            int cend = cc < sh ? Tsh : Tsh + s_sched[SCHED_HDR + 3 * (cc - sh) + 1] + s_sched[SCHED_HDR + 3 * (cc - sh) + 2];
+            int cur_cc = -1, cur_vi = -1;
+            uint32_t wbase = 0;
+            for (int tau = t_lo; tau < t_hi; ++tau) {
+                const bool shv = cc < sh;
+                if (cc != cur_cc) {
+                    const int slot = cc - rb0;
+                    mbar_wait(dfull + slot, round & 1, P.ctrl);
+                    wbase = smem_u32(dst) + static_cast<uint32_t>(slot) * L.dstage +
+                            static_cast<uint32_t>(reinterpret_cast<uintptr_t>(dn_src(cc)) & 15u);
+                    cur_cc = cc;
+                }
+                const int vid = shv ? P.T * P.k + vi : s_perm[vi - Tsh];
+                const int lgUv = shv ? lgUs : lgUr;
+                if (vi != cur_vi) {
+                    const XPlanesView hv =
+                        planes_view(smem_u32(hs) + static_cast<uint32_t>(vid) * static_cast<uint32_t>(P.hq_stride), P.H);
+                    if (shv) load_xu<DS>(xr, hv, unit_of_lane<DS>(lane & (Us - 1), lgUs));
+                    else load_xu<DR>(xr, hv, unit_of_lane<DR>(lane & (Ur - 1), lgUr));
+                    cur_vi = vi;
+                }
+                const int ul = lane & ((1 << lgUv) - 1), rsub = lane >> lgUv;
+                const int rl = (st << (5 - lgUv)) + rsub;
+                const bool valid = rl < nrow;
+                float y = 0.0f;
+                if (valid)
+                    y = shv ? unit_dot_t<DS>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbsd),
+                                             unit_of_lane<DS>(ul, lgUs), xr)
+                            : unit_dot_t<DR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbd),
+                                             unit_of_lane<DR>(ul, lgUr), xr);
+                for (int o = (1 << lgUv) >> 1; o; o >>= 1) y += __shfl_xor_sync(FULL, y, o);
+                if (valid && ul == 0) stsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
+                if (++st == (shv ? steps_s : steps_r)) {
+                    st = 0;
+                    if (++vi == cend && cc + 1 < nsrc) {
+                        ++cc;
+                        cend = Tsh + s_sched[SCHED_HDR + 3 * (cc - sh) + 1] + s_sched[SCHED_HDR + 3 * (cc - sh) + 2];
+                    }
+                }
+            }
+        }
+        if (rend < nsrc) asm volatile("bar.sync 2, %0;" ::"r"((FX_NCW + 1) * 32) : "memory");  // slots may be refilled
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
+    if (tid == 0) QMOE_TRACE(P, 2, 5);
+
+    // combine (moe.cu:76-81 and :90-96, accumulation order of layer_moe.cpp:127-153)
+    for (int idx = tid; idx < P.T * nrow; idx += FX_NCW * 32) {
+        const int t = idx / nrow, r = idx - t * nrow;
+        float acc = 0.0f;
+        for (int j = 0; j < P.k; ++j)
+            acc = fmaf(s_w[t * P.k + j], ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((t * P.k + j) * Rd + r)), acc);
+        if (sh) acc = fmaf(ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((P.T * P.k + t) * Rd + r)), s_sg[t], acc);
+        if (!(s_w[t * P.k] == s_w[t * P.k])) acc = __uint_as_float(0x7FC00000u);  // routing error: NaN weights
+        const size_t o = static_cast<size_t>(t) * d + r0d + r;
+        P.out[o] = P.residual ? s_res[t * Rd + r] + acc : acc;
+    }
+    if (tid == 0) QMOE_TRACE(P, 2, 6);
 }
 
 // ---------------------------------------------------------------------------
@@ -1044,6 +1501,92 @@ cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s) {
     cudaError_t e = set_smem(kern, g.smem);
     if (e != cudaSuccess) return e;
     return launch(kern, g.grid, GU_THREADS, g.smem, s, P, g.nst, g.half_bytes, g.dn_rows);
+}
+
+// ---- fused expert kernel ----
+static bool plan_fused(const DecodeParams& P, FxLayout& L, size_t& smem, int& grid) {
+    DevCache& dc = dev_cache();
+    if (P.F % ITEM_ROWS || P.Fs % ITEM_ROWS) return false;
+    grid = dc.sms;
+    L.Rd = (P.d + grid - 1) / grid;
+    L.nvec = P.T * P.k + P.T;
+    const uint64_t rbg = std::max(row_bytes(P.gate.type, P.d), row_bytes(P.sgate.type, P.d));
+    const uint64_t rbd = std::max(row_bytes(P.down.type, P.F), row_bytes(P.sdown.type, P.Fs));
+    L.half_bytes = static_cast<uint32_t>(align_up(ITEM_ROWS * rbg + 32, 128));
+    // four 8-row sub-chunks per item when 8 rows of every gate/up type are a
+    // whole number of 16-byte chunks (item starts are then 16-byte aligned)
+    L.gsub = ((8 * row_bytes(P.gate.type, P.d)) % 16 == 0 && (8 * row_bytes(P.sgate.type, P.d)) % 16 == 0) ? 4 : 1;
+    L.dstage = static_cast<uint32_t>(align_up(L.Rd * rbd + 32, 128));
+    size_t off = 1024;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += align_up(bytes, 128);
+        return static_cast<uint32_t>(o);
+    };
+    L.off_sched = take(SCHED_SMEM_WORDS * 4);
+    L.off_xs = take(static_cast<size_t>(P.xq_stride) * P.T);
+    L.off_hb = take(static_cast<size_t>(ITEM_ROWS) * P.T * 4);
+    L.off_w = take(static_cast<size_t>(P.T) * P.k * 4);
+    L.off_sg = take(static_cast<size_t>(P.T) * 4);
+    L.off_res = take(static_cast<size_t>(P.T) * L.Rd * 4);
+    L.off_yb = take(static_cast<size_t>(L.nvec) * L.Rd * 4);
+    const size_t fixed = off;
+    const size_t hs_bytes = static_cast<size_t>(P.hq_stride) * L.nvec;
+    const size_t budget = static_cast<size_t>(dc.smem_optin) - 1024;
+    const int nb_sh = P.has_shared ? P.Fs / ITEM_ROWS : 0;
+    const int srcs = sched_max_src(P.T, P.k, P.E);
+    const int per_cta = (nb_sh + srcs * (P.F / ITEM_ROWS) + grid - 1) / grid;
+    const int want_d = srcs + (P.has_shared ? 1 : 0);
+    auto gu_region = [&](int g) { return std::max(static_cast<size_t>(g) * 2 * L.half_bytes, hs_bytes); };
+    L.gnst = 1;
+    if (fixed + gu_region(1) + L.dstage > budget) return false;
+    L.dnst = static_cast<int>(std::min<size_t>({static_cast<size_t>(want_d), 71,
+                                                (budget - fixed - gu_region(1)) / L.dstage}));
+    while (L.gnst < std::min(per_cta, 8) &&
+           fixed + gu_region(L.gnst + 1) + static_cast<size_t>(L.dnst) * L.dstage <= budget)
+        ++L.gnst;
+    L.off_gu = static_cast<uint32_t>(fixed);
+    L.off_dn = static_cast<uint32_t>(fixed + align_up(gu_region(L.gnst), 128));
+    smem = L.off_dn + static_cast<size_t>(L.dnst) * L.dstage;
+    return smem <= budget;
+}
+
+typedef void (*FxKern)(DecodeParams, FxLayout);
+
+// (gate/up, shared gate/up, down, shared down) type combinations with a fused
+// instance; other combinations run the two-kernel path
+static FxKern pick_fused(int tr, int ts, int dr, int ds) {
+#define QMOE_FX(A, B, C, D) \
+    if (tr == A && ts == B && dr == C && ds == D) return k_experts<A, B, C, D>;
+    QMOE_FX(12, 12, 12, 12)
+    QMOE_FX(13, 13, 13, 13)
+    QMOE_FX(14, 14, 14, 14)
+    QMOE_FX(8, 8, 8, 8)
+    QMOE_FX(12, 8, 14, 8)
+    QMOE_FX(12, 8, 12, 8)
+    QMOE_FX(13, 8, 14, 8)
+    QMOE_FX(12, 12, 14, 14)
+    QMOE_FX(12, 12, 14, 12)
+#undef QMOE_FX
+    return nullptr;
+}
+
+bool fused_supported(const DecodeParams& P) {
+    FxLayout L;
+    size_t smem;
+    int grid;
+    return pick_fused(P.gate.type, P.sgate.type, P.down.type, P.sdown.type) && plan_fused(P, L, smem, grid);
+}
+
+cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s) {
+    FxLayout L;
+    size_t smem;
+    int grid;
+    FxKern kern = pick_fused(P.gate.type, P.sgate.type, P.down.type, P.sdown.type);
+    if (!kern || !plan_fused(P, L, smem, grid)) return cudaErrorInvalidValue;
+    cudaError_t e = set_smem(kern, smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, grid, FX_THREADS, smem, s, P, L);
 }
 
 cudaError_t launch_down(const DecodeParams& P, cudaStream_t s) {

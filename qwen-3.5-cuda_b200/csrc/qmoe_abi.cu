@@ -10,6 +10,8 @@ cudaError_t launch_router(const DecodeParams& P, cudaStream_t s);
 cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s);
 cudaError_t launch_down(const DecodeParams& P, cudaStream_t s);
 bool decode_supported(const DecodeParams& P);
+bool fused_supported(const DecodeParams& P);
+cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
 int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
                         cudaStream_t s);
@@ -280,8 +282,12 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
         }
         if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
         cudaError_t e = launch_router(P, s);
-        if (e == cudaSuccess) e = launch_gateup(P, s);
-        if (e == cudaSuccess) e = launch_down(P, s);
+        if (fused_supported(P)) {
+            if (e == cudaSuccess) e = launch_experts(P, s);
+        } else {
+            if (e == cudaSuccess) e = launch_gateup(P, s);
+            if (e == cudaSuccess) e = launch_down(P, s);
+        }
         if (e != cudaSuccess) return QMOE_ERR_CUDA;
     }
     return QMOE_OK;

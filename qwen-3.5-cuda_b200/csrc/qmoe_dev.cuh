@@ -24,6 +24,7 @@ enum : int {
     CTRL_ERR_TOKEN = 2,  // first failing token (atomicMin), 0xFFFFFFFF = none
     CTRL_N_ACTIVE = 3,   // number of experts with >= 1 routed pair
     CTRL_N_PAIRS = 4,    // number of valid pairs
+    CTRL_GRID_CTR = 6,   // words 6-7: 64-bit arrival count of the fused expert kernel's grid barrier
     CTRL_WORDS = 64
 };
 

@@ -8,6 +8,7 @@
 namespace qmoe {
 
 constexpr int kDecodeMaxT = 8;   // tokens per decode-path launch (larger T is sliced)
+constexpr int kMaxNormDim = 2048;  // largest d_model (the argument checks enforce it)
 constexpr int kMaxExperts = 256; // experts supported by the routing kernels
 constexpr int kMaxTopK = 32;
 

@@ -42,6 +42,23 @@ class Run:
         torch.cuda.synchronize()
         return out
 
+    def staged(self, x, residual=None):
+        """The same block through the three stage entry points (router_topk,
+        expert_gateup, down_combine): the two-kernel expert path."""
+        import torch
+        T = x.shape[0]
+        out = torch.full_like(x, float("nan"))
+        c = self.blk.c()
+        L = _lib.lib()
+        ws, wb, dp = self.ws.data_ptr(), self.ws_bytes, ctypes.byref(self.dims)
+        _lib.check(L.qmoe_router_topk(ctypes.byref(c), dp, x.data_ptr(), T, None, None, ws, wb, None), "router_topk")
+        _lib.check(L.qmoe_expert_gateup(ctypes.byref(c), dp, x.data_ptr(), T, ws, wb, None), "expert_gateup")
+        _lib.check(L.qmoe_down_combine(ctypes.byref(c), dp, T, out.data_ptr(),
+                                       None if residual is None else residual.data_ptr(), ws, wb, None),
+                   "down_combine")
+        torch.cuda.synchronize()
+        return out
+
     def view(self, which, T, count, dtype):
         import torch
         p = _lib.lib().qmoe_ws_view(self.ws.data_ptr(), ctypes.byref(self.dims), T, which)

@@ -199,6 +199,29 @@ def test_block_forward_vs_oracle(name, dims, types, bias, T):
     assert st == 0 and flags == 0
 
 
+@pytest.mark.parametrize("name,dims,types,bias,T", [CASES[1], CASES[3], CASES[5]], ids=[CASES[i][0] for i in (1, 3, 5)])
+def test_stage_entry_points_vs_block_forward(name, dims, types, bias, T):
+    """router_topk -> expert_gateup -> down_combine (two expert kernels) and
+    block_forward (fused expert kernel where an instance exists) agree with
+    the oracle and with each other."""
+    blk = synth.Block(dims, types, seed=zlib.crc32(name.encode()) & 0xFFFF, device="cuda", bias=bias)
+    r = Run(blk)
+    x = synth.inputs(T, dims.d_model, seed=78, tag=T)
+    res = synth.inputs(T, dims.d_model, seed=79, tag=T)
+    want = oracle_run(blk, x.cpu().numpy())
+    a = r.staged(x, res).cpu().numpy()
+    ida = r.view(_lib.WS_TOPK_IDX, T, T * dims.top_k, np.int32).copy()
+    b = r.forward(x, res).cpu().numpy()
+    idb = r.view(_lib.WS_TOPK_IDX, T, T * dims.top_k, np.int32).copy()
+    assert np.array_equal(ida, idb) and np.array_equal(ida.reshape(T, -1), want["idx"])
+    base = want["out"] + res.cpu().numpy()
+    assert_close(a, base, f"{name} staged")
+    assert_close(b, base, f"{name} block_forward")
+    assert_close(a, b, f"{name} staged vs block_forward")
+    st, flags, _ = r.check_errors()
+    assert st == 0 and flags == 0
+
+
 def test_block_forward_vs_reference_cuda_path():
     """Config 1 through the reference's own MoeLayer::forward (oracle/_ref):
     pins the oracle to the reference and the product to both."""
