@@ -231,7 +231,12 @@ __device__ __forceinline__ void softmax_selected(float my_v, int k, int lane, fl
 // source index of every active expert; a pair's permuted position is its
 // expert's offset plus the number of earlier tokens in the mask -- the stable
 // (expert, pair) order of a counting sort.
-__device__ void topk_and_schedule(const DecodeParams& P) {
+// Threads 0 .. 32*RT_WARPS-1 of the calling CTA take part; `bar_id` names the
+// barrier they use among themselves.  The schedule goes to `sched` (global
+// workspace or shared memory), the routing weights also to `w_out` when given.
+// With `publish`, the workspace outputs (top-k ids and weights, offsets,
+// permutation, active list, counters) and the error flags are written too.
+__device__ void topk_and_schedule(const DecodeParams& P, int* sched, float* w_out, bool publish, int bar_id) {
     constexpr int MP = kDecodeMaxT * kMaxTopK;
     static_assert(kDecodeMaxT <= 32, "token masks are 32-bit");
     static_assert(RT_WARPS * 32 * 2 >= kMaxExperts, "two experts per thread in the scan");
@@ -242,8 +247,9 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int E = P.E, k = P.k, LS = E + 1;
     const int NP = P.T * k;
-    for (int e = threadIdx.x; e < kMaxExperts; e += blockDim.x) s_mask[e] = 0u;
-    __syncthreads();
+    auto bar = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(RT_WARPS * 32) : "memory"); };
+    for (int e = threadIdx.x; e < kMaxExperts; e += RT_WARPS * 32) s_mask[e] = 0u;
+    bar();
 
     for (int t = warp; t < P.T; t += RT_WARPS) {
         uint64_t c[8];
@@ -288,7 +294,7 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
         uint32_t flag = 0;
         if (!ok) flag = EF_ROUTING;
         else if (!isfinite(rs) || fabsf(rs - 1.0f) > 1e-4f) flag = EF_NOT_NORMALIZED;
-        if (flag && lane == 0) {
+        if (publish && flag && lane == 0) {
             atomicOr(P.ctrl + CTRL_ERROR, flag);
             atomicMin(P.ctrl + CTRL_ERR_TOKEN, static_cast<uint32_t>(t));
         }
@@ -297,13 +303,16 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
             const float ow = flag ? __uint_as_float(0x7FC00000u) : wj;
             s_idx[t * k + lane] = oi;
             if (oi >= 0) atomicOr(s_mask + oi, 1u << t);
-            P.topk_idx[t * k + lane] = oi;
-            P.topk_w[t * k + lane] = ow;
-            if (P.out_idx) P.out_idx[t * k + lane] = oi;
-            if (P.out_w) P.out_w[t * k + lane] = ow;
+            if (w_out) w_out[t * k + lane] = ow;
+            if (publish) {
+                P.topk_idx[t * k + lane] = oi;
+                P.topk_w[t * k + lane] = ow;
+                if (P.out_idx) P.out_idx[t * k + lane] = oi;
+                if (P.out_w) P.out_w[t * k + lane] = ow;
+            }
         }
     }
-    __syncthreads();
+    bar();
 
     // exclusive scan over experts of (pairs << 16 | active), two experts per thread
     const int e0 = 2 * threadIdx.x;
@@ -317,7 +326,7 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
         if (lane >= o) inc += y;
     }
     if (lane == 31) s_wsum[warp] = inc;
-    __syncthreads();
+    bar();
     uint32_t base = 0, total = 0;
     for (int w = 0; w < RT_WARPS; ++w) {
         const uint32_t ws = s_wsum[w];
@@ -333,35 +342,37 @@ __device__ void topk_and_schedule(const DecodeParams& P) {
         const uint32_t ex = h ? ex1 : ex0, m = h ? m1 : m0;
         if (e < E) {
             s_off[e] = static_cast<int>(ex >> 16);
-            P.offsets[e] = static_cast<int>(ex >> 16);
+            if (publish) P.offsets[e] = static_cast<int>(ex >> 16);
             if (m) {
                 const int s2 = static_cast<int>(ex & 0xFFFFu);
-                P.active[s2] = e;
-                P.sched[SCHED_HDR + 3 * s2] = e;
-                P.sched[SCHED_HDR + 3 * s2 + 1] = static_cast<int>(ex >> 16);
-                P.sched[SCHED_HDR + 3 * s2 + 2] = __popc(m);
+                if (publish) P.active[s2] = e;
+                sched[SCHED_HDR + 3 * s2] = e;
+                sched[SCHED_HDR + 3 * s2 + 1] = static_cast<int>(ex >> 16);
+                sched[SCHED_HDR + 3 * s2 + 2] = __popc(m);
             }
         }
     }
     if (threadIdx.x == 0) {
-        P.offsets[E] = npairs;
-        P.sched[0] = nact;
-        P.sched[1] = npairs;
-        P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(nact);
-        P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(npairs);
+        sched[0] = nact;
+        sched[1] = npairs;
+        if (publish) {
+            P.offsets[E] = npairs;
+            P.ctrl[CTRL_N_ACTIVE] = static_cast<uint32_t>(nact);
+            P.ctrl[CTRL_N_PAIRS] = static_cast<uint32_t>(npairs);
+        }
     }
-    __syncthreads();
-    for (int p = threadIdx.x; p < NP; p += blockDim.x) {
+    bar();
+    for (int p = threadIdx.x; p < NP; p += RT_WARPS * 32) {
         const int e = s_idx[p];
         int rank = -1;
         if (e >= 0) {
             const int t = p / k;
             rank = s_off[e] + __popc(s_mask[e] & ((1u << t) - 1u));
-            P.perm[rank] = p;
-            P.sched[poff + rank] = p;
-            P.sched[toff + rank] = t;
+            if (publish) P.perm[rank] = p;
+            sched[poff + rank] = p;
+            sched[toff + rank] = t;
         }
-        P.inv_perm[p] = rank;
+        if (publish) P.inv_perm[p] = rank;
     }
 }
 
@@ -418,6 +429,10 @@ __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
         }
     }
 
+    if (!P.route_in_router) {  // the fused expert kernel selects the experts itself
+        if (threadIdx.x == 0) QMOE_TRACE(P, 0, 2);
+        return;
+    }
     // last CTA to arrive selects the experts.  The CTA barrier orders every
     // thread's logit writes before thread 0's release; the acquire side of the
     // same atomic makes all CTAs' logits visible to the last one.
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
     }
     __syncthreads();
     if (!s_last) return;
-    topk_and_schedule(P);
+    topk_and_schedule(P, P.sched, nullptr, true, 0);
     if (threadIdx.x == 0) {
         P.ctrl[CTRL_ARRIVE] = 0;
         QMOE_TRACE(P, 0, 4);
@@ -1056,50 +1071,34 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
     if (tid == 0) pdl_wait();  // the router has finished: schedule and block input are valid
     __syncthreads();
     if (tid == 0) QMOE_TRACE(P, 1, 1);
-    {
-        // One round trip for the schedule, the input planes, the routing
-        // weights, the shared-expert gate logit and the residual rows: every
-        // thread issues all of its loads before it stores any of them.
-        const int words = sched_words(P.T, P.k, P.E);
-        const int nw = P.T * P.k;
+    if (warp < RT_WARPS) {
+        // every CTA selects the experts itself from the router logits (CTA 0
+        // also publishes the routing to the workspace): no cross-CTA step
+        // between the router's logits and this CTA's weight loads
+        topk_and_schedule(P, s_sched, s_w, c == 0, 3);
+    } else {
+        // the other warps: input planes, shared-expert gate, residual rows
+        constexpr int NTH = FX_THREADS - RT_WARPS * 32;
+        const int t2 = tid - RT_WARPS * 32;
         const int nres = (P.residual && nrow > 0) ? P.T * nrow : 0;
-        const int n32 = words + nw + P.T + nres;
+        const int n32 = P.T + nres;
         const int LS = P.E + 1;
-        auto load32 = [&](int q) -> uint32_t {
-            if (q < words) return static_cast<uint32_t>(__ldcg(P.sched + q));
-            q -= words;
-            if (q < nw) return __float_as_uint(__ldcg(P.topk_w + q));
-            q -= nw;
-            if (q < P.T) return __float_as_uint(__ldcg(P.logits + q * LS + P.E));
+        auto load32 = [&](int q) -> float {
+            if (q < P.T) return __ldcg(P.logits + q * LS + P.E);
             q -= P.T;
             const int t = q / nrow, r = q - t * nrow;
-            return __float_as_uint(__ldcg(P.residual + static_cast<size_t>(t) * d + r0d + r));
+            return __ldcg(P.residual + static_cast<size_t>(t) * d + r0d + r);
         };
-        auto store32 = [&](int q, uint32_t v) {
-            if (q < words) { s_sched[q] = static_cast<int>(v); return; }
-            q -= words;
-            if (q < nw) { s_w[q] = __uint_as_float(v); return; }
-            q -= nw;
-            if (q < P.T) { s_sg[q] = sh ? 1.0f / (1.0f + expf(-__uint_as_float(v))) : 0.0f; return; }
+        auto store32 = [&](int q, float v) {
+            if (q < P.T) { s_sg[q] = sh ? 1.0f / (1.0f + expf(-v)) : 0.0f; return; }
             q -= P.T;
             const int t = q / nrow, r = q - t * nrow;
-            s_res[t * Rd + r] = __uint_as_float(v);
+            s_res[t * Rd + r] = v;
         };
-        constexpr int J32 = 2;
-        uint32_t v32[J32];
-#pragma unroll
-        for (int j = 0; j < J32; ++j) {
-            const int q = tid + j * FX_THREADS;
-            if (q < n32) v32[j] = load32(q);
-        }
-        x_planes_smem<FX_THREADS>(xs, P, tid);  // its loads go out before these stores
-#pragma unroll
-        for (int j = 0; j < J32; ++j) {
-            const int q = tid + j * FX_THREADS;
-            if (q < n32) store32(q, v32[j]);
-        }
-        // whatever did not fit the unrolled passes (large T * k)
-        for (int q = tid + J32 * FX_THREADS; q < n32; q += FX_THREADS) store32(q, load32(q));
+        const float v0 = t2 < n32 ? load32(t2) : 0.0f;
+        x_planes_smem<NTH>(xs, P, t2);  // its loads go out before the store below
+        if (t2 < n32) store32(t2, v0);
+        for (int q = t2 + NTH; q < n32; q += NTH) store32(q, load32(q));
     }
     __syncthreads();
     if (tid == 0) QMOE_TRACE(P, 1, 2);
@@ -1532,7 +1531,7 @@ static bool plan_fused(const DecodeParams& P, FxLayout& L, size_t& smem, int& gr
     L.off_yb = take(static_cast<size_t>(L.nvec) * L.Rd * 4);
     const size_t fixed = off;
     const size_t hs_bytes = static_cast<size_t>(P.hq_stride) * L.nvec;
-    const size_t budget = static_cast<size_t>(dc.smem_optin) - 1024;
+    const size_t budget = static_cast<size_t>(dc.smem_optin) - 5120;  // static shared memory of the routing step
     const int nb_sh = P.has_shared ? P.Fs / ITEM_ROWS : 0;
     const int srcs = sched_max_src(P.T, P.k, P.E);
     const int per_cta = (nb_sh + srcs * (P.F / ITEM_ROWS) + grid - 1) / grid;

@@ -127,6 +127,7 @@ DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x
     P.norm_w = nullptr;
     P.eps = 0.0f;
     P.prenorm = 0;
+    P.route_in_router = 1;
     P.xq = w + L.xq; P.xq_stride = L.xq_stride;
     P.hidden = reinterpret_cast<float*>(w + L.hidden);
     P.hq = w + L.hq; P.hq_stride = L.hq_stride; P.H = L.H;
@@ -281,8 +282,10 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
             P.eps = eps;
         }
         if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
+        const bool fused = fused_supported(P);
+        P.route_in_router = fused ? 0 : 1;
         cudaError_t e = launch_router(P, s);
-        if (fused_supported(P)) {
+        if (fused) {
             if (e == cudaSuccess) e = launch_experts(P, s);
         } else {
             if (e == cudaSuccess) e = launch_gateup(P, s);

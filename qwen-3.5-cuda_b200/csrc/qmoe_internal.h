@@ -131,6 +131,7 @@ struct DecodeParams {
     const float* norm_w;  // optional fused pre-MoE RMSNorm weight [d] (prenorm != 0)
     float eps;
     int prenorm;
+    int route_in_router;  // 1: the router's last CTA selects experts; 0: the fused expert kernel does
     uint8_t* xq;        // [T] 24-bit planes of the block input (written by the router)
     size_t xq_stride;
     float* hidden;
