@@ -128,7 +128,7 @@ DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x
     P.eps = 0.0f;
     P.prenorm = 0;
     P.route_in_router = 1;
-    P.xq = w + L.xq; P.xq_stride = L.xq_stride;
+    P.xq_stride = L.xq_stride;
     P.hidden = reinterpret_cast<float*>(w + L.hidden);
     P.hq = w + L.hq; P.hq_stride = L.hq_stride; P.H = L.H;
     P.trace = g_trace;
@@ -248,7 +248,7 @@ int qmoe_expert_gateup(const qmoe_block* B, const qmoe_dims* D, const float* x, 
                        qmoe_stream_t stream) {
     int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
     if (st) return st;
-    (void)x;  // the activation planes of x were written by qmoe_router_topk
+    (void)x;  // the block input x_in (workspace) was written by qmoe_router_topk
     DecodeParams P = make_params(B, D, x, nullptr, nullptr, T, ws);
     if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
     return cuda_status(launch_gateup(P, reinterpret_cast<cudaStream_t>(stream)));

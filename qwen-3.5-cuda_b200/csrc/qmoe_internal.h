@@ -54,8 +54,8 @@ __host__ __device__ inline int sched_words(int T, int k, int E) { return sched_t
 
 // Workspace layout for a call with T tokens (all offsets 256-byte aligned).
 struct WsLayout {
-    size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, sched, xnorm, xq, hidden, hq, total;
-    size_t xq_stride;  // bytes per token of x planes: 3*d + (d/16)*8
+    size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, sched, xnorm, hidden, hq, total;
+    size_t xq_stride;  // bytes per token of x planes in shared memory: 3*d + (d/16)*8
     size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
     int H;             // max(F, Fs)
 };
@@ -79,7 +79,6 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     L.sched = take(sizeof(int32_t) * sched_words(T, k, E));
     L.xnorm = take(sizeof(float) * static_cast<size_t>(T) * d);
     L.xq_stride = align_up(3 * static_cast<size_t>(d) + static_cast<size_t>(d / 16) * 8, 16);
-    L.xq = take(L.xq_stride * T);
     L.H = H;
     L.hidden = take(sizeof(float) * static_cast<size_t>(nvec) * H);
     L.hq_stride = align_up(3 * static_cast<size_t>(H) + static_cast<size_t>(H / 16) * 8, 16);
@@ -132,7 +131,6 @@ struct DecodeParams {
     float eps;
     int prenorm;
     int route_in_router;  // 1: the router's last CTA selects experts; 0: the fused expert kernel does
-    uint8_t* xq;        // [T] 24-bit planes of the block input (written by the router)
     size_t xq_stride;
     float* hidden;
     uint8_t* hq;        // [T*k + T] 24-bit planes of silu(g)*u (written by the gate/up kernel)
