@@ -143,6 +143,23 @@ QMOE_API int qmoe_dispatch(const int32_t* topk_idx, int T, int k, int E,
                   int32_t* offsets, int32_t* perm, int32_t* inv_perm,
                   void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 
+/* The permutation of qmoe_dispatch with nothing to allocate and no workspace
+ * argument.  No counterpart in the reference.  It is meant for callers that
+ * cannot hand the library device memory: a serving engine that reserves all
+ * of its device memory in pools at start-up and allows no allocation on the
+ * token path, or a binding layer (ctypes, cgo, JNI) with no place to keep a
+ * device buffer between calls.
+ * Its scratch is a fixed array inside the library, 32 KiB per device, which
+ * limits it to num_experts <= 256; larger E returns QMOE_ERR_UNSUPPORTED.
+ * Nothing has to start at zero: every call clears the scratch it uses.
+ * The first call on a device looks up the scratch's address with that device
+ * current (cudaGetSymbolAddress); make that first call before capturing a
+ * stream.  All calls on a device share the scratch, so two calls that
+ * overlap in time race: order them on one stream, or synchronise between
+ * streams. */
+QMOE_API int qmoe_dispatch_noalloc(const int32_t* topk_idx, int T, int k, int E,
+                          int32_t* offsets, int32_t* perm, int32_t* inv_perm, qmoe_stream_t stream);
+
 /* Gate/up products of every routed (token, expert) pair and of the shared
  * expert, fused with silu(gate)*up, for the routing in the workspace. */
 QMOE_API int qmoe_expert_gateup(const qmoe_block* blk, const qmoe_dims* dims, const float* x, int T,

@@ -79,6 +79,15 @@ __global__ void __launch_bounds__(DW * 32) k_dispatch(const int32_t* __restrict_
 
 size_t dispatch_scratch_bytes(int E) { return sizeof(int32_t) * static_cast<size_t>(E) * DW; }
 
+// Scratch of qmoe_dispatch_noalloc: a fixed per-device array of E * DW
+// counters for E <= kNoAllocMaxExperts (32 KiB).  k_dispatch clears the part
+// it uses at the start of every launch, so it needs no initialisation.
+static __device__ __align__(256) int32_t g_dispatch_scratch[kNoAllocMaxExperts * DW];
+
+cudaError_t dispatch_noalloc_scratch(int32_t** p) {
+    return cudaGetSymbolAddress(reinterpret_cast<void**>(p), g_dispatch_scratch);
+}
+
 cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
                             int32_t* table, cudaStream_t s) {
     k_dispatch<<<1, DW * 32, 0, s>>>(idx, NP, E, offsets, perm, inv_perm, table);

@@ -1,6 +1,7 @@
 // extern "C" entry points of include/qmoe.h: argument checks (the reference's
 // host-side exceptions become status codes), workspace layout, launches.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include "qmoe_dev.cuh"
 #include "qmoe_internal.h"
@@ -21,6 +22,7 @@ cudaError_t launch_synth(void* dst, int type, uint64_t nblocks, uint64_t seed, u
 cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
                             int32_t* table, cudaStream_t s);
 size_t dispatch_scratch_bytes(int E);
+cudaError_t dispatch_noalloc_scratch(int32_t** p);
 
 __global__ void k_ws_init(uint32_t* ctrl) {
     const int i = threadIdx.x;
@@ -241,6 +243,26 @@ int qmoe_dispatch(const int32_t* idx, int T, int k, int E, int32_t* offsets, int
     if (static_cast<int64_t>(T) * k > (1ll << 30)) return QMOE_ERR_UNSUPPORTED;
     if (!ws || ws_bytes < dispatch_scratch_bytes(E)) return QMOE_ERR_WORKSPACE;
     return cuda_status(launch_dispatch(idx, T * k, E, offsets, perm, inv_perm, static_cast<int32_t*>(ws),
+                                       reinterpret_cast<cudaStream_t>(stream)));
+}
+
+// Address of the fixed dispatch scratch on each device, looked up on the
+// first call made with that device current.
+static std::atomic<int32_t*> g_noalloc_scratch[64];
+
+int qmoe_dispatch_noalloc(const int32_t* idx, int T, int k, int E, int32_t* offsets, int32_t* perm,
+                          int32_t* inv_perm, qmoe_stream_t stream) {
+    if (!idx || !offsets || !perm || T <= 0 || k <= 0 || E <= 0) return QMOE_ERR_ARG;
+    if (E > kNoAllocMaxExperts) return QMOE_ERR_UNSUPPORTED;  // the fixed scratch holds E <= 256
+    if (static_cast<int64_t>(T) * k > (1ll << 30)) return QMOE_ERR_UNSUPPORTED;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QMOE_ERR_CUDA;
+    int32_t* table = g_noalloc_scratch[dev].load(std::memory_order_acquire);
+    if (!table) {
+        if (dispatch_noalloc_scratch(&table) != cudaSuccess || !table) return QMOE_ERR_CUDA;
+        g_noalloc_scratch[dev].store(table, std::memory_order_release);
+    }
+    return cuda_status(launch_dispatch(idx, T * k, E, offsets, perm, inv_perm, table,
                                        reinterpret_cast<cudaStream_t>(stream)));
 }
 

@@ -11,6 +11,7 @@ constexpr int kDecodeMaxT = 8;   // tokens per decode-path launch (larger T is s
 constexpr int kMaxNormDim = 2048;  // largest d_model (the argument checks enforce it)
 constexpr int kMaxExperts = 256; // experts supported by the routing kernels
 constexpr int kMaxTopK = 32;
+constexpr int kNoAllocMaxExperts = 256;  // largest E of qmoe_dispatch_noalloc (fixed scratch)
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -55,6 +55,7 @@ SIGNATURES = [
                                  c_void_p, c_size_t, c_void_p]),
     ("qmoe_dispatch", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                               c_void_p]),
+    ("qmoe_dispatch_noalloc", c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("qmoe_expert_gateup", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_int, c_void_p, c_size_t,
                                    c_void_p]),
     ("qmoe_down_combine", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int, c_void_p, c_void_p, c_void_p,
