@@ -19,6 +19,7 @@
  *   qmoe_dispatch         no counterpart (the reference is single-token)
  *   qmoe_expert_gateup    src/layer_moe.cpp:131-135, 147-149 (gate/up GEMVs,
  *                         moe_silu_mul) for all routed pairs + shared expert
+ *   qmoe_expert_block     src/layer_moe.cpp:127-154 (all expert work after routing)
  *   qmoe_down_combine     src/layer_moe.cpp:138-141, 150-154 (down GEMVs,
  *                         moe_add, moe_shared_add, final copy)
  *   qmoe_block_forward    src/layer_moe.cpp:82-155   MoeLayer::forward, for
@@ -171,6 +172,18 @@ QMOE_API int qmoe_expert_gateup(const qmoe_block* blk, const qmoe_dims* dims, co
 QMOE_API int qmoe_down_combine(const qmoe_block* blk, const qmoe_dims* dims, int T,
                       float* out, const float* residual,
                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* expert_gateup + down_combine in one step for the routing the workspace holds
+ * (after qmoe_router_topk, T <= 8): a single fused launch -- gate/up items,
+ * a device-wide barrier, down rows, combine -- where the weight types have a
+ * fused instance, else the two kernels.  Same result as the two calls. */
+QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int T,
+                      float* out, const float* residual,
+                      void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Number of kernels one qmoe_block_forward call with these arguments launches
+ * (for profiling and launch accounting); negative status on bad arguments. */
+QMOE_API int qmoe_block_kernel_count(const qmoe_block* blk, const qmoe_dims* dims, int T);
 
 /* The whole MoE block for T tokens: router_topk, expert_gateup, down_combine.
  * x, out: device F32 [T][d_model]; residual optional (NULL). */

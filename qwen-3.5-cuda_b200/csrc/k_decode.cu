@@ -1411,6 +1411,7 @@ struct GuPlan { int grid, nst, dn_rows; uint32_t half_bytes; size_t smem; };
 
 static bool plan_gateup(const DecodeParams& P, GuPlan& g) {
     DevCache& dc = dev_cache();
+    if (dc.sms <= 0 || dc.smem_optin <= 0) return false;  // no usable device
     g.grid = dc.sms;
     g.dn_rows = (P.d + dc.sms - 1) / dc.sms;  // rows per down-kernel CTA (see plan_down)
     if (P.F % ITEM_ROWS || P.Fs % ITEM_ROWS) return false;
@@ -1434,6 +1435,7 @@ struct DnPlan { int grid, nst, Rd, nvec; uint32_t stage_bytes; size_t smem; };
 
 static bool plan_down(const DecodeParams& P, DnPlan& p) {
     DevCache& dc = dev_cache();
+    if (dc.sms <= 0 || dc.smem_optin <= 0) return false;  // no usable device
     p.Rd = (P.d + dc.sms - 1) / dc.sms;
     p.grid = (P.d + p.Rd - 1) / p.Rd;
     p.nvec = P.T * P.k + P.T;
@@ -1505,6 +1507,7 @@ cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s) {
 // ---- fused expert kernel ----
 static bool plan_fused(const DecodeParams& P, FxLayout& L, size_t& smem, int& grid) {
     DevCache& dc = dev_cache();
+    if (dc.sms <= 0 || dc.smem_optin <= 0) return false;  // no usable device
     if (P.F % ITEM_ROWS || P.Fs % ITEM_ROWS) return false;
     grid = dc.sms;
     L.Rd = (P.d + grid - 1) / grid;

@@ -286,6 +286,33 @@ int qmoe_down_combine(const qmoe_block* B, const qmoe_dims* D, int T, float* out
     return cuda_status(launch_down(P, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int qmoe_expert_block(const qmoe_block* B, const qmoe_dims* D, int T, float* out, const float* residual, void* ws,
+                      size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
+    if (st) return st;
+    if (!out) return QMOE_ERR_ARG;
+    DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
+    if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (fused_supported(P)) return cuda_status(launch_experts(P, s));
+    cudaError_t e = launch_gateup(P, s);
+    if (e == cudaSuccess) e = launch_down(P, s);
+    return cuda_status(e);
+}
+
+int qmoe_block_kernel_count(const qmoe_block* B, const qmoe_dims* D, int T) {
+    int st;
+    if (T <= 0) return -QMOE_ERR_ARG;
+    if ((st = check_dims(D)) || (st = check_block(B, D))) return -st;
+    int n = 0;
+    for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
+        const int nt = std::min(kDecodeMaxT, T - t0);
+        DecodeParams P = make_params(B, D, nullptr, nullptr, nullptr, nt, nullptr);
+        n += fused_supported(P) ? 2 : 3;
+    }
+    return n;
+}
+
 static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const float* x, float* out,
                               const float* residual, const float* norm_w, float eps, int T, void* ws,
                               size_t ws_bytes, qmoe_stream_t stream) {

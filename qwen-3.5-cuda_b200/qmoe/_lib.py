@@ -60,6 +60,9 @@ SIGNATURES = [
                                    c_void_p]),
     ("qmoe_down_combine", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int, c_void_p, c_void_p, c_void_p,
                                   c_size_t, c_void_p]),
+    ("qmoe_expert_block", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int, c_void_p, c_void_p, c_void_p,
+                                  c_size_t, c_void_p]),
+    ("qmoe_block_kernel_count", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int]),
     ("qmoe_block_forward", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_void_p, c_int,
                                    c_void_p, c_size_t, c_void_p]),
     ("qmoe_block_forward_prenorm", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_float,

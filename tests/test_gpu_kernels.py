@@ -215,6 +215,18 @@ def test_stage_entry_points_vs_block_forward(name, dims, types, bias, T):
     idb = r.view(_lib.WS_TOPK_IDX, T, T * dims.top_k, np.int32).copy()
     assert np.array_equal(ida, idb) and np.array_equal(ida.reshape(T, -1), want["idx"])
     base = want["out"] + res.cpu().numpy()
+    # router_topk followed by the one-step expert entry point
+    import torch
+    c = blk.c()
+    L = _lib.lib()
+    out3 = torch.full_like(x, float("nan"))
+    _lib.check(L.qmoe_router_topk(ctypes.byref(c), ctypes.byref(r.dims), x.data_ptr(), T, None, None,
+                                  r.ws.data_ptr(), r.ws_bytes, None))
+    _lib.check(L.qmoe_expert_block(ctypes.byref(c), ctypes.byref(r.dims), T, out3.data_ptr(), res.data_ptr(),
+                                   r.ws.data_ptr(), r.ws_bytes, None))
+    torch.cuda.synchronize()
+    assert_close(out3.cpu().numpy(), base, f"{name} expert_block")
+    assert L.qmoe_block_kernel_count(ctypes.byref(c), ctypes.byref(r.dims), T) in (2, 3)
     assert_close(a, base, f"{name} staged")
     assert_close(b, base, f"{name} block_forward")
     assert_close(a, b, f"{name} staged vs block_forward")
