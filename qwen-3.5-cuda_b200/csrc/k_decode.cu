@@ -24,6 +24,7 @@
 #include <algorithm>
 #include "qmoe_dev.cuh"
 #include "qmoe_units.cuh"
+#include "qmoe_route.cuh"
 #include "qmoe_internal.h"
 
 namespace qmoe {
@@ -168,62 +169,9 @@ __device__ __forceinline__ void write_planes4(float4 v, uint8_t* base, int K, in
     if ((lane & 3) == 0) reinterpret_cast<float2*>(base + 3 * K)[e0 >> 4] = make_float2(scale, s16);
 }
 
-// Order-preserving key of a finite float (-0 and +0 map to the same key).
-__device__ __forceinline__ uint32_t fkey(float v) {
-    const uint32_t u = __float_as_uint(v + 0.0f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-__device__ __forceinline__ float fkey_inv(uint32_t key) {
-    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
-}
-
-// 64-bit sort key of a lane's candidate i: logit key, then lower i first
-__device__ __forceinline__ uint64_t cand_key(uint32_t key, int i) {
-    return (static_cast<uint64_t>(key) << 8) | static_cast<uint32_t>(7 - i);
-}
-__device__ __forceinline__ void cex(uint64_t& a, uint64_t& b) {  // a <- max, b <- min
-    const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
-    a = hi;
-    b = lo;
-}
-
-// Softmax over the k selected logits held by lanes 0..k-1 (moe.cu:41-51):
-// max, then exp(v - max) summed sequentially over j = 0..k-1, then one
-// division per weight.  `rs` is the sequential sum of the weights, checked by
-// the caller as layer_moe.cpp:114-124 does on the host.  KM >= k bounds the
-// unrolled chains.
-template <int KM>
-__device__ __forceinline__ void softmax_selected(float my_v, int k, int lane, float& wj, float& rs) {
-    float sel[KM];
-#pragma unroll
-    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, my_v, j);
-    float mx = sel[0];
-#pragma unroll
-    for (int j = 1; j < KM; ++j) if (j < k) mx = fmaxf(mx, sel[j]);
-    const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
-#pragma unroll
-    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, ex, j);
-    float sum = 0.0f;
-#pragma unroll
-    for (int j = 0; j < KM; ++j) if (j < k) sum += sel[j];
-    wj = ex / sum;
-#pragma unroll
-    for (int j = 0; j < KM; ++j) sel[j] = __shfl_sync(FULL, wj, j);
-    rs = 0.0f;
-#pragma unroll
-    for (int j = 0; j < KM; ++j) if (j < k) rs += sel[j];
-}
-
-// Top-k + softmax + validation for every token, then the permutation and the
-// packed schedule.  Runs in the single CTA that finished the router last.
-//
-// Selection (moe.cu:19-36): k rounds of "largest remaining logit, lowest
-// index on ties".  Each lane holds the logits of experts lane + 32 i, sorted
-// once (descending key, ascending i) by an 8-input Batcher network; a round is
-// then one redux for the largest head key and one for the lowest expert id
-// among the lanes whose head holds it, after which the winning lane pops its
-// head.
+// Top-k + softmax + validation for every token (select_token, one warp per
+// token), then the permutation and the packed schedule.  Runs in the router's
+// last CTA, or in every CTA of the fused expert kernel.
 //
 // Dispatch: a token picks an expert at most once, so each expert's pairs are
 // described by a token bitmask (T <= 32).  One block-wide exclusive scan of
@@ -231,6 +179,7 @@ __device__ __forceinline__ void softmax_selected(float my_v, int k, int lane, fl
 // source index of every active expert; a pair's permuted position is its
 // expert's offset plus the number of earlier tokens in the mask -- the stable
 // (expert, pair) order of a counting sort.
+//
 // Threads 0 .. 32*RT_WARPS-1 of the calling CTA take part; `bar_id` names the
 // barrier they use among themselves.  The schedule goes to `sched` (global
 // workspace or shared memory), the routing weights also to `w_out` when given.
@@ -252,48 +201,10 @@ __device__ void topk_and_schedule(const DecodeParams& P, int* sched, float* w_ou
     bar();
 
     for (int t = warp; t < P.T; t += RT_WARPS) {
-        uint64_t c[8];
-        uint32_t amax = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = lane + 32 * i;
-            const float v = e < E ? __ldcg(P.logits + t * LS + e) : 0.0f;
-            c[i] = cand_key(e < E ? fkey(v) : 0u, i);
-            amax = max(amax, e < E ? (__float_as_uint(v) & 0x7FFFFFFFu) : 0u);
-        }
-        const bool finite = __reduce_max_sync(FULL, amax) < 0x7F800000u;
-        // Batcher odd-even merge sort of 8 (19 comparators)
-        cex(c[0], c[1]); cex(c[2], c[3]); cex(c[4], c[5]); cex(c[6], c[7]);
-        cex(c[0], c[2]); cex(c[1], c[3]); cex(c[4], c[6]); cex(c[5], c[7]);
-        cex(c[1], c[2]); cex(c[5], c[6]);
-        cex(c[0], c[4]); cex(c[1], c[5]); cex(c[2], c[6]); cex(c[3], c[7]);
-        cex(c[2], c[4]); cex(c[3], c[5]);
-        cex(c[1], c[2]); cex(c[3], c[4]); cex(c[5], c[6]);
-        int my_idx = -1;
-        float my_v = 0.0f;
-        if (finite) {
-            for (int j = 0; j < k; ++j) {
-                const uint32_t hk = static_cast<uint32_t>(c[0] >> 8);
-                const int he = lane + 32 * (7 - static_cast<int>(c[0] & 7u));
-                const uint32_t mk = __reduce_max_sync(FULL, hk);
-                const int win = static_cast<int>(__reduce_min_sync(FULL, hk == mk ? static_cast<uint32_t>(he) : 0xFFFFFFFFu));
-                if (he == win) {
-#pragma unroll
-                    for (int i = 0; i < 7; ++i) c[i] = c[i + 1];
-                    c[7] = 0;
-                }
-                if (lane == j) { my_idx = win; my_v = fkey_inv(mk); }
-            }
-        }
-        // softmax over the selected logits (moe.cu:41-51)
-        float wj, rs;
-        if (k <= 8) softmax_selected<8>(my_v, k, lane, wj, rs);
-        else softmax_selected<kMaxTopK>(my_v, k, lane, wj, rs);
-        const bool lane_ok = lane >= k || (my_idx >= 0 && my_idx < E && isfinite(wj) && wj >= 0.0f);
-        const bool ok = finite && __all_sync(FULL, lane_ok);
-        uint32_t flag = 0;
-        if (!ok) flag = EF_ROUTING;
-        else if (!isfinite(rs) || fabsf(rs - 1.0f) > 1e-4f) flag = EF_NOT_NORMALIZED;
+        int my_idx;
+        float wj;
+        uint32_t flag;
+        select_token(P.logits + t * LS, E, k, lane, my_idx, wj, flag);
         if (publish && flag && lane == 0) {
             atomicOr(P.ctrl + CTRL_ERROR, flag);
             atomicMin(P.ctrl + CTRL_ERR_TOKEN, static_cast<uint32_t>(t));

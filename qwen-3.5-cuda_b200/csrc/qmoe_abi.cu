@@ -12,6 +12,8 @@ cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s);
 cudaError_t launch_down(const DecodeParams& P, cudaStream_t s);
 bool decode_supported(const DecodeParams& P);
 bool fused_supported(const DecodeParams& P);
+bool prefill_supported(const DecodeParams& P);
+cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
 int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
@@ -199,12 +201,13 @@ size_t qmoe_workspace_size(const qmoe_dims* D, int max_tokens) {
     if (check_dims(D) || max_tokens <= 0) return 0;
     const size_t a = ws_layout(*D, std::min(max_tokens, kDecodeMaxT)).total;
     const size_t b = dispatch_scratch_bytes(D->num_experts) + 256;
-    return std::max(a, b);
+    const size_t c = max_tokens > kDecodeMaxT ? ws_layout(*D, max_tokens).total : 0;  // prefill path
+    return std::max(std::max(a, b), c);
 }
 
 void* qmoe_ws_view(void* ws, const qmoe_dims* D, int T, int which) {
     if (!ws || check_dims(D) || T <= 0) return nullptr;
-    const WsLayout L = ws_layout(*D, std::min(T, kDecodeMaxT));
+    const WsLayout L = ws_layout(*D, T);
     uint8_t* w = static_cast<uint8_t*>(ws);
     switch (which) {
         case QMOE_WS_LOGITS: return w + L.logits;
@@ -321,6 +324,30 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
     if (!x || !out) return QMOE_ERR_ARG;
     if (!aligned16(x) || (norm_w && !aligned16(norm_w))) return QMOE_ERR_ALIGN;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (T > kDecodeMaxT && ws_layout(*D, T).total <= ws_bytes) {
+        // prefill: one pass over all tokens, expert products on the tensor cores
+        DecodeParams P = make_params(B, D, x, out, residual, T, ws);
+        if (norm_w) {
+            P.prenorm = 1;
+            P.norm_w = norm_w;
+            P.eps = eps;
+        }
+        if (prefill_supported(P)) {
+            const WsLayout L = ws_layout(*D, T);
+            uint8_t* w = static_cast<uint8_t*>(ws);
+            PrefillBufs pb;
+            pb.tok_of_pos = reinterpret_cast<int32_t*>(w + L.tok_of_pos);
+            pb.tile_start = reinterpret_cast<int32_t*>(w + L.tile_start);
+            pb.sh_grp = reinterpret_cast<int32_t*>(w + L.sh_grp);
+            pb.sh_tiles = pb.sh_grp + 2;
+            pb.disp = reinterpret_cast<int32_t*>(w + L.disp);
+            pb.H = reinterpret_cast<__half*>(w + L.Hpf);
+            pb.Hs = reinterpret_cast<__half*>(w + L.Hs);
+            pb.Y = reinterpret_cast<__half*>(w + L.Y);
+            pb.Ys = reinterpret_cast<__half*>(w + L.Ys);
+            return cuda_status(launch_prefill(P, pb, s));
+        }
+    }
     for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
         const int n = std::min(kDecodeMaxT, T - t0);
         const size_t o = static_cast<size_t>(t0) * D->d_model;

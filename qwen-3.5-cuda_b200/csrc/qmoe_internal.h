@@ -2,6 +2,7 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include "../../include/qmoe.h"
 
@@ -56,17 +57,26 @@ __host__ __device__ inline int sched_words(int T, int k, int E) { return sched_t
 // Workspace layout for a call with T tokens (all offsets 256-byte aligned).
 struct WsLayout {
     size_t ctrl, logits, topk_idx, topk_w, offsets, perm, inv_perm, active, sched, xnorm, hidden, hq, total;
+    // prefill regions (T > kDecodeMaxT): source token per permuted pair, tile
+    // prefix per expert, the shared expert's group, dispatch scratch, fp16
+    // hidden vectors and expert outputs
+    size_t tok_of_pos, tile_start, sh_grp, disp, Hpf, Hs, Y, Ys;
     size_t xq_stride;  // bytes per token of x planes in shared memory: 3*d + (d/16)*8
     size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
     int H;             // max(F, Fs)
 };
 
+// Workspace layout for a call with T tokens.  Regions used only by the
+// decode kernels (schedule, F32 hidden vectors and their planes) are sized
+// for at most kDecodeMaxT tokens; for T > kDecodeMaxT the prefill regions
+// follow.
 inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     WsLayout L{};
     const int E = D.num_experts, k = D.top_k, d = D.d_model;
     const int H = D.expert_dim > D.shared_dim ? D.expert_dim : D.shared_dim;
     const int P = T * k;
-    const int nvec = P + T;
+    const int Td = T < kDecodeMaxT ? T : kDecodeMaxT;
+    const int nvec = Td * k + Td;
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 256); return r; };
     L.ctrl = take(64 * 4);
@@ -76,17 +86,41 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     L.offsets = take(sizeof(int32_t) * (E + 1));
     L.perm = take(sizeof(int32_t) * P);
     L.inv_perm = take(sizeof(int32_t) * P);
-    L.active = take(sizeof(int32_t) * (P < E ? P : E));
-    L.sched = take(sizeof(int32_t) * sched_words(T, k, E));
+    L.active = take(sizeof(int32_t) * (Td * k < E ? Td * k : E));
+    L.sched = take(sizeof(int32_t) * sched_words(Td, k, E));
     L.xnorm = take(sizeof(float) * static_cast<size_t>(T) * d);
     L.xq_stride = align_up(3 * static_cast<size_t>(d) + static_cast<size_t>(d / 16) * 8, 16);
     L.H = H;
     L.hidden = take(sizeof(float) * static_cast<size_t>(nvec) * H);
     L.hq_stride = align_up(3 * static_cast<size_t>(H) + static_cast<size_t>(H / 16) * 8, 16);
     L.hq = take(L.hq_stride * nvec);
+    if (T > kDecodeMaxT) {
+        const int F = D.expert_dim, Fs = D.shared_dim;
+        L.tok_of_pos = take(sizeof(int32_t) * P);
+        L.tile_start = take(sizeof(int32_t) * (E + 1));
+        L.sh_grp = take(sizeof(int32_t) * 4);  // {0, T} and the shared expert's tile prefix {0, tiles}
+        L.disp = take(sizeof(int32_t) * static_cast<size_t>(E) * 32);
+        L.Hpf = take(2 * static_cast<size_t>(P) * F);
+        L.Hs = take(2 * static_cast<size_t>(T) * Fs);
+        L.Y = take(2 * static_cast<size_t>(P) * d);
+        L.Ys = take(2 * static_cast<size_t>(T) * d);
+    }
     L.total = o;
     return L;
 }
+
+// Prefill buffers of a workspace (fp16 data as raw 16-bit words).
+struct PrefillBufs {
+    int32_t* tok_of_pos;
+    int32_t* tile_start;
+    int32_t* sh_grp;    // [2] {0, T}
+    int32_t* sh_tiles;  // [2] {0, ceil(T / 128)}
+    int32_t* disp;
+    __half* H;
+    __half* Hs;
+    __half* Y;
+    __half* Ys;
+};
 
 // Phase tracer: kernel kinds x CTAs x events of %globaltimer (ns).
 constexpr int kTraceKinds = 3, kTraceCtas = 160, kTraceEvents = 8;

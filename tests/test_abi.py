@@ -55,7 +55,11 @@ def test_workspace_size():
     n1 = L.qmoe_workspace_size(ctypes.byref(d), 1)
     n8 = L.qmoe_workspace_size(ctypes.byref(d), 8)
     assert 0 < n1 < n8
-    assert L.qmoe_workspace_size(ctypes.byref(d), 1000) == n8  # larger batches are sliced
+    # more than 8 tokens: the prefill path's buffers (fp16 hidden vectors and
+    # expert outputs of every (token, expert) pair) dominate
+    n1000 = L.qmoe_workspace_size(ctypes.byref(d), 1000)
+    k, F, dm = d.top_k, d.expert_dim, d.d_model
+    assert n1000 > n8 and n1000 >= 1000 * k * (F + dm) * 2
     bad = Dims(d_model=3000).c()
     assert L.qmoe_workspace_size(ctypes.byref(bad), 1) == 0
 
