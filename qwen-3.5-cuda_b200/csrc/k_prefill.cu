@@ -29,6 +29,8 @@
 // over K, so a common permutation of K leaves it unchanged.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "qmoe_dev.cuh"
 #include "qmoe_dq1.cuh"
 #include "qmoe_internal.h"
@@ -41,30 +43,45 @@ __device__ __forceinline__ __half2 bits_to_half2(uint32_t u) { return *reinterpr
 namespace pf {
 
 constexpr int BM = 128;                // tile rows (tokens or pairs) = MMA M
-constexpr int BN = 256;                // tile columns = MMA N
-constexpr int BK = 64;                 // K per pipeline stage (128 bytes of fp16 per row)
-constexpr int PROD_WARPS = 8;          // weight dequantisation + activation staging
+constexpr int BN = 256;                // tile columns = MMA N (gate/up: 128 of each)
+constexpr int BK = 32;                 // K per pipeline stage (64 bytes of fp16 per row)
+constexpr int NST = 5;                 // pipeline stages
+constexpr int LA = 3;                  // stages whose copies are in flight ahead of the dequantisation
+constexpr int PROD_WARPS = 8;          // copies + weight dequantisation (one B row per thread)
 constexpr int EPI_WARP0 = 8;           // warps 8..11: TMEM epilogue (lane quarter = warp % 4)
 constexpr int MMA_WARP = 12;           // one thread issues the MMAs
 constexpr int THREADS = 13 * 32;
-constexpr uint32_t A_BYTES = BM * 128;  // 16 KB per stage
-constexpr uint32_t B_BYTES = BN * 128;  // 32 KB per weight matrix per stage
+constexpr uint32_t A_BYTES = BM * 64;    // 8 KB: fp16 activations of one stage
+constexpr uint32_t B_BYTES = BN * 64;    // 16 KB: fp16 weights of one stage
+constexpr uint32_t RAW_ROW = 48;         // Q4_K bytes of one row per stage: block header + 32 qs bytes
+constexpr uint32_t RAW_BYTES = BN * RAW_ROW;  // 12 KB
+constexpr uint32_t STAGE = A_BYTES + B_BYTES + RAW_BYTES;  // 36 KB (every part 1024-byte aligned)
+constexpr uint32_t TMEM_COLS = 2 * BN;   // two accumulator buffers
 // instruction descriptor: D F32, A/B fp16, both K-major, N = 256, M = 128
 constexpr uint32_t IDESC = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 
-// byte offset of 16-byte chunk c (0..7) of row r in a swizzled K-major tile
-__device__ __forceinline__ uint32_t sw_off(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+// byte offset of 16-byte chunk c (0..3) of row r in a K-major tile with the
+// 64-byte swizzle (rows of 64 bytes, 8-row groups of 512 bytes; chunk c of
+// row r sits at chunk c ^ ((r / 2) % 4))
+__device__ __forceinline__ uint32_t sw_off(uint32_t r, uint32_t c) { return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4); }
 
-// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (the tile base is 1024-byte aligned)
+// shared-memory matrix descriptor: K-major, 64-byte swizzle, 8-row groups
+// 512 bytes apart (the tile base is 1024-byte aligned)
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
     uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>(1u) << 16;           // leading byte offset (16 B; unused with this swizzle)
-    d |= static_cast<uint64_t>(1024u >> 4) << 32;   // stride byte offset between 8-row groups
-    d |= static_cast<uint64_t>(1u) << 46;           // descriptor version for sm_100
-    d |= static_cast<uint64_t>(2u) << 61;           // 128-byte swizzle
+    d |= static_cast<uint64_t>(1u) << 16;          // leading byte offset (16 B; unused with this swizzle)
+    d |= static_cast<uint64_t>(512u >> 4) << 32;   // stride byte offset between 8-row groups
+    d |= static_cast<uint64_t>(1u) << 46;          // descriptor version for sm_100
+    d |= static_cast<uint64_t>(4u) << 61;          // 64-byte swizzle
     return d;
 }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
     asm volatile(
@@ -106,94 +123,93 @@ __device__ __forceinline__ uint4 pack_chunk(const float (&v)[8]) {
     o.w = h2_bits(__floats2half2_rn(v[5], v[7]));
     return o;
 }
-// the same reordering of a chunk of 8 fp16 values in natural order
-__device__ __forceinline__ uint4 reorder_chunk(uint4 n) {
-    uint4 o;
-    o.x = __byte_perm(n.x, n.y, 0x5410);
-    o.y = __byte_perm(n.x, n.y, 0x7632);
-    o.z = __byte_perm(n.z, n.w, 0x5410);
-    o.w = __byte_perm(n.z, n.w, 0x7632);
-    return o;
-}
-
-// Q4_K: 16 values of one row -- elements k0+8cp .. +7 (low nibbles of qs
-// bytes 8cp..8cp+7 of the 64-element group, sub-block 2g) and k0+32+8cp .. +7
-// (high nibbles, sub-block 2g+1) -- as two chunks.  value = d*sc*q - dmin*m
-// (matmul_q4.cu:76-96), evaluated in fp16 as q*(d*sc) - dmin*m.
-__device__ __forceinline__ void dq_q4k(const uint8_t* row, int k0, int cp, uint4& lo, uint4& hi) {
-    const uint8_t* blk = row + (k0 >> 8) * 144;
-    const int g = (k0 >> 6) & 3;
-    const uint4 hd = __ldg(reinterpret_cast<const uint4*>(blk));
-    const uint2 q = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 32 * g + 8 * cp));
-    float sc0, m0, sc1, m1;
-    kscale(hd.y, hd.z, hd.w, 2 * g, sc0, m0);
-    kscale(hd.y, hd.z, hd.w, 2 * g + 1, sc1, m1);
+__device__ __forceinline__ void dq_q4k_raw(uint32_t raw, int j, uint4 (&out)[4]) {
+    const uint4 hd = lds128(raw);
+    const uint4 qa = lds128(raw + 16), qb = lds128(raw + 32);
+    float sc, m;
+    kscale(hd.y, hd.z, hd.w, j, sc, m);
     const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
-    const __half2 a0 = __float2half2_rn(d * sc0), b0 = __float2half2_rn(dmin * m0);
-    const __half2 a1 = __float2half2_rn(d * sc1), b1 = __float2half2_rn(dmin * m1);
+    const __half2 a = __float2half2_rn(d * sc), nb = __float2half2_rn(-(dmin * m));
     const __half2 k1024 = __float2half2_rn(1024.0f);
-    // half2(1024 + n(byte e), 1024 + n(byte e+2)) from one word: nibble in the mantissa
-    auto cvt = [&](uint32_t w, uint32_t mask, __half2 a, __half2 b) {
-        const __half2 raw = bits_h2((w & mask) | 0x64006400u);
-        return h2_bits(__hfma2(__hsub2(raw, k1024), a, __hneg2(b)));
+    const int sh = (j & 1) * 4;
+    // half2(1024 + n(byte e), 1024 + n(byte e+2)) from one word: element order 0,2 / 1,3
+    auto cvt = [&](uint32_t w) {
+        const __half2 raw2 = bits_h2(((w >> sh) & 0x000F000Fu) | 0x64006400u);
+        return h2_bits(__hfma2(__hsub2(raw2, k1024), a, nb));
     };
-    // low nibbles: words (bytes 0..3) and (4..7) -> element order 0,2,1,3 / 4,6,5,7
-    lo.x = cvt(q.x, 0x000F000Fu, a0, b0);
-    lo.y = cvt(q.x >> 8, 0x000F000Fu, a0, b0);
-    lo.z = cvt(q.y, 0x000F000Fu, a0, b0);
-    lo.w = cvt(q.y >> 8, 0x000F000Fu, a0, b0);
-    // high nibbles, shifted down to bits 0..3 first
-    hi.x = cvt(q.x >> 4, 0x000F000Fu, a1, b1);
-    hi.y = cvt(q.x >> 12, 0x000F000Fu, a1, b1);
-    hi.z = cvt(q.y >> 4, 0x000F000Fu, a1, b1);
-    hi.w = cvt(q.y >> 12, 0x000F000Fu, a1, b1);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        out[c].x = cvt(q[2 * c]);
+        out[c].y = cvt(q[2 * c] >> 8);
+        out[c].z = cvt(q[2 * c + 1]);
+        out[c].w = cvt(q[2 * c + 1] >> 8);
+    }
 }
 
-// any other type: the reference's per-element formulas (dq1), same chunks
-__device__ __forceinline__ void dq_generic(const uint8_t* row, int type, int k0, int cp, uint4& lo, uint4& hi) {
-    float a[8], b[8];
+// any other type: 32 values of one row with the reference's per-element
+// formulas (dq1), read from global memory
+__device__ __forceinline__ void dq_generic(const uint8_t* row, int type, int k0, uint4 (&out)[4]) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        a[e] = dq1(row, type, static_cast<uint64_t>(k0 + 8 * cp + e));
-        b[e] = dq1(row, type, static_cast<uint64_t>(k0 + 32 + 8 * cp + e));
+    for (int c = 0; c < 4; ++c) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = dq1(row, type, static_cast<uint64_t>(k0 + 8 * c + e));
+        out[c] = pack_chunk(v);
     }
-    lo = pack_chunk(a);
-    hi = pack_chunk(b);
 }
 
 struct GemmParams {
-    // A operand
-    const float* x;           // MODE 0: F32 rows, row length K
-    const int32_t* a_rows;    // MODE 0: source row of each output row (null: the output row itself)
-    const __half* a16;        // MODE 1: fp16 rows [rows][K]
-    // B operand: groups of N rows x K, GGUF rows
+    const __half* a16;        // fp16 A rows [*, K] in the chunk element order
+    const int32_t* a_rows;    // source A row of each output row (null: the output row itself)
+    // B operand: groups of weight rows, GGUF rows of K elements
     const uint8_t* w0;        // gate (MODE 0) or down (MODE 1)
     const uint8_t* w1;        // up (MODE 0)
     uint64_t w_group_bytes;
     uint32_t w_row_bytes;
     int wtype;
-    int N, K;
+    int N, K;                 // output columns (F or d), reduction length
     int groups;
     const int32_t* grp_start;   // [groups + 1] first output row of each group
     const int32_t* tile_start;  // [groups + 1] prefix of 128-row tiles per group
-    __half* out;                // [rows][N]
+    __half* out;                // [rows][N]; MODE 0 in the chunk element order
     uint32_t* ctrl;             // error word
 };
 
+// Tile iterator: tile t -> (group, m tile, n tile, row range)
+struct PfTile {
+    int g, mt, nt, r0, r1;
+};
+__device__ __forceinline__ PfTile pf_tile(const GemmParams& p, int t, int nN) {
+    PfTile T;
+    const int mi = t / nN;
+    T.nt = t - mi * nN;
+    int lo = 0, hi = p.groups;  // largest g with tile_start[g] <= mi
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(p.tile_start + mid) <= mi) lo = mid; else hi = mid;
+    }
+    T.g = lo;
+    T.mt = mi - __ldg(p.tile_start + lo);
+    T.r0 = __ldg(p.grp_start + lo) + T.mt * BM;
+    T.r1 = min(T.r0 + BM, __ldg(p.grp_start + lo + 1));
+    return T;
+}
+
+// MODE 0 (gate/up): D[:, 0..127] = gate rows nt*128.., D[:, 128..255] = up rows;
+// out = silu(gate) * up, 128 columns per tile.  MODE 1 (down): 256 columns.
 template <int WT, int MODE>
 __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
-    constexpr int NB = MODE == 0 ? 2 : 1;
-    constexpr uint32_t STAGE = A_BYTES + NB * B_BYTES;
-    constexpr int NST = MODE == 0 ? 2 : 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * STAGE);
     uint64_t* empty = full + NST;
-    uint64_t* accf = empty + NST;
-    uint64_t* accfree = accf + 1;
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accfree + 1);
+    uint64_t* accf = empty + NST;     // [2]
+    uint64_t* accfree = accf + 2;     // [2]
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accfree + 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nN = p.N / BN, nK = p.K / BK;
+    const int ncol = MODE == 0 ? BN / 2 : BN;  // output columns per tile
+    const int nN = p.N / ncol, nK = p.K / BK;
     const int total = __ldg(p.tile_start + p.groups) * nN;
 
     if (tid == 0) {
@@ -201,13 +217,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
             mbar_init(full + s, PROD_WARPS);
             mbar_init(empty + s, 1);
         }
-        mbar_init(accf, 1);
-        mbar_init(accfree, 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(accf + b, 1);
+            mbar_init(accfree + b, 4);
+        }
         fence_mbar_init();
     }
     if (warp == MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
-                     "r"(NB * BN));
+                     "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -215,101 +233,91 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
 
-    // tile index -> (group, m tile, n tile)
-    auto decode = [&](int t, int& g, int& mt, int& nt) {
-        const int mi = t / nN;
-        nt = t - mi * nN;
-        int lo = 0, hi = p.groups;  // largest g with tile_start[g] <= mi
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (__ldg(p.tile_start + mid) <= mi) lo = mid; else hi = mid;
-        }
-        g = lo;
-        mt = mi - __ldg(p.tile_start + g);
-    };
-
     if (warp < PROD_WARPS) {
         // ---------------- producers ----------------
-        int stage = 0, use = 0;  // use = how many times the ring wrapped
-        for (int t = blockIdx.x; t < total; t += gridDim.x) {
-            int g, mt, nt;
-            decode(t, g, mt, nt);
-            const int r0 = __ldg(p.grp_start + g) + mt * BM;
-            const int r1 = min(r0 + BM, __ldg(p.grp_start + g + 1));
-            const uint8_t* wg0 = p.w0 + g * p.w_group_bytes + static_cast<uint64_t>(nt) * BN * p.w_row_bytes;
-            const uint8_t* wg1 = MODE == 0 ? p.w1 + g * p.w_group_bytes + static_cast<uint64_t>(nt) * BN * p.w_row_bytes
-                                           : nullptr;
-            for (int kb = 0; kb < nK; ++kb) {
-                if (use > 0) mbar_wait(empty + stage, (use - 1) & 1, p.ctrl);
-                uint8_t* sa = smem + stage * STAGE;
-                const int k0 = kb * BK;
-                // A: 128 rows x 8 chunks
+        // issue pointer (copies LA steps ahead) and consume pointer (dequantisation)
+        int it = blockIdx.x, ikb = 0, istep = 0;
+        int ct = blockIdx.x, ckb = 0, cstep = 0;
+        PfTile iT = it < total ? pf_tile(p, it, nN) : PfTile{};
+        PfTile cT = iT;
+        const int row = tid;  // B row of this thread; A chunks tid and tid + 256
+        auto wrow = [&](const PfTile& T) -> const uint8_t* {
+            const uint8_t* base = (MODE == 0 && row >= BN / 2) ? p.w1 : p.w0;
+            const int n = MODE == 0 ? T.nt * (BN / 2) + (row & (BN / 2 - 1)) : T.nt * BN + row;
+            return base + T.g * p.w_group_bytes + static_cast<uint64_t>(n) * p.w_row_bytes;
+        };
+        auto issue = [&]() {
+            const int stage = istep % NST;
+            if (istep >= NST) mbar_wait(empty + stage, (istep / NST - 1) & 1, p.ctrl);
+            const uint32_t sa = smem_u32(smem + stage * STAGE);
+            const int k0 = ikb * BK;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int q = tid + j * (PROD_WARPS * 32);
-                    const int r = q >> 3, c = q & 7;
-                    const int row = r0 + r;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (row < r1) {
-                        if (MODE == 0) {
-                            const int src = p.a_rows ? __ldg(p.a_rows + row) : row;
-                            const float4* xp = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(src) * p.K + k0 + 8 * c);
-                            const float4 u0 = __ldg(xp), u1 = __ldg(xp + 1);
-                            const float f[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-                            v = pack_chunk(f);
-                        } else {
-                            v = reorder_chunk(__ldg(reinterpret_cast<const uint4*>(p.a16 + static_cast<size_t>(row) * p.K + k0 + 8 * c)));
-                        }
-                    }
-                    *reinterpret_cast<uint4*>(sa + sw_off(r, c)) = v;
-                }
-                // B: NB matrices x 256 rows x 4 chunk pairs
+            for (int j = 0; j < 2; ++j) {  // A: 128 rows x 4 chunks
+                const int q = tid + j * (PROD_WARPS * 32);
+                const int r = q >> 2, c = q & 3;
+                const int orow = iT.r0 + r;
+                const bool ok = orow < iT.r1;
+                const int src = ok ? (p.a_rows ? __ldg(p.a_rows + orow) : orow) : 0;
+                cp_async16(sa + sw_off(r, c), p.a16 + static_cast<size_t>(src) * p.K + k0 + 8 * c, ok ? 16u : 0u);
+            }
+            if (WT == T_Q4_K) {  // raw bytes of this thread's B row: header + 32 qs bytes of the group
+                const uint8_t* blk = wrow(iT) + (k0 >> 8) * 144;
+                const uint32_t rd = sa + A_BYTES + B_BYTES + row * RAW_ROW;
+                cp_async16(rd, blk, 16u);
+                cp_async16(rd + 16, blk + 16 + 32 * ((k0 >> 6) & 3), 16u);
+                cp_async16(rd + 32, blk + 32 + 32 * ((k0 >> 6) & 3), 16u);
+            }
+            cp_async_commit();
+            ++istep;
+            if (++ikb == nK) {
+                ikb = 0;
+                it += gridDim.x;
+                if (it < total) iT = pf_tile(p, it, nN);
+            }
+        };
+        const int nsteps = ((total - blockIdx.x + gridDim.x - 1) / gridDim.x) * nK;
+        for (int i = 0; i < LA && i < nsteps; ++i) issue();
+        for (; cstep < nsteps; ++cstep) {
+            if (cstep + LA < nsteps) issue(); else cp_async_commit();  // keep one group per step
+            cp_async_wait<LA>();  // this thread's copies for step cstep have landed
+            const int stage = cstep % NST;
+            uint8_t* sb = smem + stage * STAGE + A_BYTES;
+            uint4 v[4];
+            if (WT == T_Q4_K) dq_q4k_raw(smem_u32(sb + B_BYTES + row * RAW_ROW), (ckb * BK / 32) & 7, v);
+            else dq_generic(wrow(cT), WT, ckb * BK, v);
 #pragma unroll
-                for (int m = 0; m < NB; ++m) {
-                    const uint8_t* wb = m == 0 ? wg0 : wg1;
-                    uint8_t* sb = sa + A_BYTES + m * B_BYTES;
-#pragma unroll 2
-                    for (int j = 0; j < 4; ++j) {
-                        const int q = tid + j * (PROD_WARPS * 32);
-                        const int n = q >> 2, cp = q & 3;
-                        const uint8_t* row = wb + static_cast<uint64_t>(n) * p.w_row_bytes;
-                        uint4 lo, hi;
-                        if (WT == T_Q4_K) dq_q4k(row, k0, cp, lo, hi);
-                        else dq_generic(row, WT, k0, cp, lo, hi);
-                        *reinterpret_cast<uint4*>(sb + sw_off(n, cp)) = lo;
-                        *reinterpret_cast<uint4*>(sb + sw_off(n, cp + 4)) = hi;
-                    }
-                }
-                fence_async_smem();  // generic-proxy stores -> visible to the tensor core
-                __syncwarp();
-                if (lane == 0) mbar_arrive(full + stage);
-                if (++stage == NST) { stage = 0; ++use; }
+            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sb + sw_off(row, c)) = v[c];
+            fence_async_smem();  // generic and cp.async stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full + stage);
+            if (++ckb == nK) {
+                ckb = 0;
+                ct += gridDim.x;
+                if (ct < total) cT = pf_tile(p, ct, nN);
             }
         }
+        cp_async_wait<0>();
     } else if (warp == MMA_WARP) {
         // ---------------- MMA issue ----------------
-        int stage = 0, use = 0, ti = 0;
+        int step = 0, ti = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
-            if (ti > 0) mbar_wait(accfree, (ti - 1) & 1, p.ctrl);
+            const int buf = ti & 1;
+            if (ti >= 2) mbar_wait(accfree + buf, ((ti >> 1) - 1) & 1, p.ctrl);
             tc_fence_after();
-            for (int kb = 0; kb < nK; ++kb) {
-                mbar_wait(full + stage, use & 1, p.ctrl);
+            for (int kb = 0; kb < nK; ++kb, ++step) {
+                const int stage = step % NST;
+                mbar_wait(full + stage, (step / NST) & 1, p.ctrl);
                 tc_fence_after();
                 if (lane == 0) {
                     const uint32_t sa = smem_u32(smem + stage * STAGE);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t ad = sdesc(sa + kk * 32);
-                        const uint32_t acc = (kb | kk) != 0;
-                        mma_f16(tmem, ad, sdesc(sa + A_BYTES + kk * 32), acc);
-                        if (MODE == 0) mma_f16(tmem + BN, ad, sdesc(sa + A_BYTES + B_BYTES + kk * 32), acc);
-                    }
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        mma_f16(tmem + buf * BN, sdesc(sa + kk * 32), sdesc(sa + A_BYTES + kk * 32), (kb | kk) != 0);
                     mma_commit(empty + stage);  // the stage is free once these MMAs have read it
                 }
                 __syncwarp();
-                if (++stage == NST) { stage = 0; ++use; }
             }
-            if (lane == 0) mma_commit(accf);  // accumulators complete
+            if (lane == 0) mma_commit(accf + buf);  // accumulators complete
             __syncwarp();
         }
     } else {
@@ -317,29 +325,33 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 = tile rows
         int ti = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
-            int g, mt, nt;
-            decode(t, g, mt, nt);
-            const int r0 = __ldg(p.grp_start + g) + mt * BM;
-            const int r1 = min(r0 + BM, __ldg(p.grp_start + g + 1));
-            mbar_wait(accf, ti & 1, p.ctrl);
+            const PfTile T = pf_tile(p, t, nN);
+            const int buf = ti & 1;
+            mbar_wait(accf + buf, (ti >> 1) & 1, p.ctrl);
             tc_fence_after();
-            const int row = r0 + 32 * quarter + lane;
-            const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
-            __half* orow = p.out + static_cast<size_t>(row) * p.N + nt * BN;
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            const int orow = T.r0 + 32 * quarter + lane;
+            const uint32_t tl = tmem + buf * BN + (static_cast<uint32_t>(32 * quarter) << 16);
+            __half* dst = p.out + static_cast<size_t>(orow) * p.N + T.nt * ncol;
+            for (int c0 = 0; c0 < ncol; c0 += 32) {
                 uint32_t a[32];
                 tmem_ld32(tl + c0, a);
                 uint32_t o[16];
                 if (MODE == 0) {
                     uint32_t u[32];
-                    tmem_ld32(tl + BN + c0, u);
+                    tmem_ld32(tl + BN / 2 + c0, u);
                     tmem_wait_ld();
+                    float h[32];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float g0 = __uint_as_float(a[2 * i]), g1 = __uint_as_float(a[2 * i + 1]);
-                        const float h0 = g0 / (1.0f + expf(-g0)) * __uint_as_float(u[2 * i]);  // moe.cu:64
-                        const float h1 = g1 / (1.0f + expf(-g1)) * __uint_as_float(u[2 * i + 1]);
-                        o[i] = h2_bits(__floats2half2_rn(h0, h1));
+                    for (int i = 0; i < 32; ++i) {
+                        const float g = __uint_as_float(a[i]);
+                        h[i] = g / (1.0f + expf(-g)) * __uint_as_float(u[i]);  // moe.cu:64
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {  // chunk element order for the down GEMM
+                        o[4 * c] = h2_bits(__floats2half2_rn(h[8 * c], h[8 * c + 2]));
+                        o[4 * c + 1] = h2_bits(__floats2half2_rn(h[8 * c + 1], h[8 * c + 3]));
+                        o[4 * c + 2] = h2_bits(__floats2half2_rn(h[8 * c + 4], h[8 * c + 6]));
+                        o[4 * c + 3] = h2_bits(__floats2half2_rn(h[8 * c + 5], h[8 * c + 7]));
                     }
                 } else {
                     tmem_wait_ld();
@@ -347,31 +359,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
                     for (int i = 0; i < 16; ++i)
                         o[i] = h2_bits(__floats2half2_rn(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1])));
                 }
-                if (row < r1) {
-                    uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+                if (orow < T.r1) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(accfree);
+            if (lane == 0) mbar_arrive(accfree + buf);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == MMA_WARP) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NB * BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     }
 }
 
-template <int MODE>
-size_t gemm_smem_bytes() {
-    constexpr int NB = MODE == 0 ? 2 : 1;
-    constexpr int NST = MODE == 0 ? 2 : 4;
-    return 1024 + static_cast<size_t>(NST) * (A_BYTES + NB * B_BYTES) + 256;
-}
+inline size_t gemm_smem_bytes() { return 1024 + static_cast<size_t>(NST) * STAGE + 256; }
 
 }  // namespace pf
 
@@ -384,7 +391,8 @@ __device__ __forceinline__ float pf_tree8(float (&acc)[2][4]);
 
 template <int CH>
 __global__ void __launch_bounds__(256) k_norm_many(const float* __restrict__ x, const float* __restrict__ w,
-                                                   float eps, float* __restrict__ out, int T, int d) {
+                                                   float eps, float* __restrict__ out, __half* __restrict__ x16,
+                                                   int T, int d) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -419,10 +427,19 @@ __global__ void __launch_bounds__(256) k_norm_many(const float* __restrict__ x, 
                 v[i][hh].w = __fmul_rn(__fmul_rn(v[i][hh].w, sc), nv.w);
             }
     }
+    __half* hrow = x16 + static_cast<size_t>(t) * d;
 #pragma unroll
     for (int i = 0; i < CH; ++i)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) *reinterpret_cast<float4*>(orow + 256 * i + 128 * hh + 4 * lane) = v[i][hh];
+        for (int hh = 0; hh < 2; ++hh) {
+            const int e0 = 256 * i + 128 * hh + 4 * lane;
+            *reinterpret_cast<float4*>(orow + e0) = v[i][hh];
+            // fp16 copy for the tensor cores, in the chunk element order
+            // (0,2,1,3,4,6,5,7): this lane holds half of an 8-element chunk
+            const uint2 hv = make_uint2(pf::h2_bits(__floats2half2_rn(v[i][hh].x, v[i][hh].z)),
+                                        pf::h2_bits(__floats2half2_rn(v[i][hh].y, v[i][hh].w)));
+            *reinterpret_cast<uint2*>(hrow + (e0 & ~7) + 4 * (lane & 1)) = hv;
+        }
 }
 
 // The reference GEMV's reduction of the 8 per-lane chains (lane L plays
@@ -481,44 +498,65 @@ __device__ __forceinline__ void pf_load_row(float4 (&w)[CH][2], const uint8_t* r
         }
 }
 
+constexpr int RM_NBUF = 4;  // x_in rows in flight per CTA
+
 template <int CH>
 __global__ void __launch_bounds__(256) k_route_many(const uint8_t* __restrict__ router, int router_type,
                                                     const uint8_t* __restrict__ sgate, int sgate_type,
                                                     const float* __restrict__ bias, const float* __restrict__ xin,
                                                     float* __restrict__ logits, int T, int d, int E, int has_shared,
-                                                    int tchunk) {
-    const int lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+                                                    int tchunk, uint32_t* ctrl) {
+    // x_in rows are bulk-copied into shared memory, RM_NBUF ahead; every warp
+    // reads each row once for its two router rows
+    __shared__ __align__(128) float s_x[RM_NBUF][256 * CH];
+    __shared__ __align__(8) uint64_t s_full[RM_NBUF];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = blockIdx.x * 8 + warp;
     const int nrows = E + (has_shared ? 1 : 0);
     const int ra = 2 * gw, rb = 2 * gw + 1;
-    if (ra >= nrows) return;
-    const bool has_b = rb < nrows;
+    const bool has_a = ra < nrows, has_b = rb < nrows;
+    const int t0 = blockIdx.y * tchunk, t1 = min(T, t0 + tchunk);
+    const uint32_t row_bytes_x = static_cast<uint32_t>(d) * 4u;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < RM_NBUF; ++i) mbar_init(s_full + i, 1);
+        fence_mbar_init();
+        for (int i = 0; i < RM_NBUF && t0 + i < t1; ++i) {
+            mbar_arrive_expect_tx(s_full + i, row_bytes_x);
+            bulk_g2s(s_x[i], xin + static_cast<size_t>(t0 + i) * d, row_bytes_x, s_full + i, ctrl);
+        }
+    }
     float4 wa[CH][2], wb[CH][2];
     auto row_ptr = [&](int r, int& type) {
         type = r < E ? router_type : sgate_type;
         return r < E ? router + static_cast<size_t>(r) * d * (type == T_F32 ? 4 : 2) : sgate;
     };
-    int ta, tb = 0;
-    pf_load_row<CH>(wa, row_ptr(ra, ta), ta, lane);
+    int ta = 0, tb = 0;
+    if (has_a) {
+        pf_load_row<CH>(wa, row_ptr(ra, ta), ta, lane);
+    } else {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) wa[i][0] = wa[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (has_b) {
         pf_load_row<CH>(wb, row_ptr(rb, tb), tb, lane);
     } else {
 #pragma unroll
         for (int i = 0; i < CH; ++i) wb[i][0] = wb[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const float bias_a = (ra < E && bias) ? __ldg(bias + ra) : 0.0f;
+    const float bias_a = (has_a && ra < E && bias) ? __ldg(bias + ra) : 0.0f;
     const float bias_b = (has_b && rb < E && bias) ? __ldg(bias + rb) : 0.0f;
     const int LS = E + 1;
-    const int t0 = blockIdx.y * tchunk, t1 = min(T, t0 + tchunk);
-    for (int t = t0; t < t1; ++t) {
-        const float* xr = xin + static_cast<size_t>(t) * d;
+    __syncthreads();
+    for (int t = t0, n = 0; t < t1; ++t, ++n) {
+        const int buf = n % RM_NBUF;
+        mbar_wait(s_full + buf, (n / RM_NBUF) & 1, ctrl);
         float aa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         float ab[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
         for (int i = 0; i < CH; ++i)
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                const float4 xv = __ldg(reinterpret_cast<const float4*>(xr + 256 * i + 128 * hh + 4 * lane));
+                const float4 xv = *reinterpret_cast<const float4*>(&s_x[buf][256 * i + 128 * hh + 4 * lane]);
                 aa[hh][0] = __fmaf_rn(wa[i][hh].x, xv.x, aa[hh][0]);
                 aa[hh][1] = __fmaf_rn(wa[i][hh].y, xv.y, aa[hh][1]);
                 aa[hh][2] = __fmaf_rn(wa[i][hh].z, xv.z, aa[hh][2]);
@@ -531,12 +569,13 @@ __global__ void __launch_bounds__(256) k_route_many(const uint8_t* __restrict__ 
         float va = pf_tree8(aa);
         float vb = pf_tree8(ab);
         if (lane == 0) {
-            if (ra < E && bias) va = __fadd_rn(va, bias_a);
-            logits[static_cast<size_t>(t) * LS + ra] = va;
-            if (has_b) {
-                if (rb < E && bias) vb = __fadd_rn(vb, bias_b);
-                logits[static_cast<size_t>(t) * LS + rb] = vb;
-            }
+            if (has_a) logits[static_cast<size_t>(t) * LS + ra] = (ra < E && bias) ? __fadd_rn(va, bias_a) : va;
+            if (has_b) logits[static_cast<size_t>(t) * LS + rb] = (rb < E && bias) ? __fadd_rn(vb, bias_b) : vb;
+        }
+        __syncthreads();  // every warp is done with this buffer
+        if (threadIdx.x == 0 && t + RM_NBUF < t1) {
+            mbar_arrive_expect_tx(s_full + buf, row_bytes_x);
+            bulk_g2s(s_x[buf], xin + static_cast<size_t>(t + RM_NBUF) * d, row_bytes_x, s_full + buf, ctrl);
         }
     }
 }
@@ -699,7 +738,7 @@ template <int MODE>
 cudaError_t launch_pgemm(const pf::GemmParams& p, cudaStream_t s) {
     GemmKern<MODE> kern = pick_gemm<MODE>(p.wtype);
     if (!kern) return cudaErrorInvalidValue;
-    const size_t smem = pf::gemm_smem_bytes<MODE>();
+    const size_t smem = pf::gemm_smem_bytes();
     cudaError_t e = pf_set_smem(kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<pf_num_sms(), pf::THREADS, smem, s>>>(p);
@@ -712,7 +751,7 @@ bool prefill_supported(const DecodeParams& P) {
     auto ok_type = [](int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_Q8_0; };
     if (!ok_type(P.gate.type) || P.up.type != P.gate.type || !ok_type(P.down.type)) return false;
     if (P.has_shared && (!ok_type(P.sgate.type) || P.sup.type != P.sgate.type || !ok_type(P.sdown.type))) return false;
-    if (P.d % pf::BN || P.F % pf::BN || P.Fs % pf::BN || P.d % pf::BK || P.F % pf::BK || P.Fs % pf::BK) return false;
+    if (P.d % pf::BN || P.F % (pf::BN / 2) || P.Fs % (pf::BN / 2) || P.F % pf::BK || P.Fs % pf::BK) return false;
     if (P.d > kMaxNormDim || P.d % 256) return false;
     return pf_num_sms() > 0;
 }
@@ -727,10 +766,10 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     {
         const dim3 grid((T + 7) / 8);
         switch (CH) {
-            case 1: k_norm_many<1><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, T, d); break;
-            case 2: k_norm_many<2><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, T, d); break;
-            case 4: k_norm_many<4><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, T, d); break;
-            case 8: k_norm_many<8><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, T, d); break;
+            case 1: k_norm_many<1><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
+            case 2: k_norm_many<2><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
+            case 4: k_norm_many<4><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
+            case 8: k_norm_many<8><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
             default: return cudaErrorInvalidValue;
         }
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -738,11 +777,14 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     // 2. router logits
     {
         const int nrows = E + (P.has_shared ? 1 : 0);
-        const int tchunk = 64;
-        const dim3 grid((((nrows + 1) / 2) + 7) / 8, (T + tchunk - 1) / tchunk);
+        const int rgroups = (((nrows + 1) / 2) + 7) / 8;  // CTAs of 16 router rows
+        // token chunks: about four CTAs per SM in total
+        const int chunks = std::max(1, std::min((T + 15) / 16, 4 * pf_num_sms() / rgroups));
+        const int tchunk = (T + chunks - 1) / chunks;
+        const dim3 grid(rgroups, (T + tchunk - 1) / tchunk);
 #define QMOE_RM(C)                                                                                               \
     k_route_many<C><<<grid, 256, 0, s>>>(P.router, P.router_type, P.sgate_inp, P.sgate_type, P.bias, P.xnorm, \
-                                         P.logits, T, d, E, P.has_shared, tchunk)
+                                         P.logits, T, d, E, P.has_shared, tchunk, P.ctrl)
         switch (CH) {
             case 1: QMOE_RM(1); break;
             case 2: QMOE_RM(2); break;
@@ -763,7 +805,7 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // 6. gate/up: routed, then shared
     pf::GemmParams g{};
-    g.x = P.xnorm;
+    g.a16 = B.X16;
     g.a_rows = B.tok_of_pos;
     g.w0 = P.gate.p;
     g.w1 = P.up.p;

@@ -341,6 +341,7 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
             pb.sh_grp = reinterpret_cast<int32_t*>(w + L.sh_grp);
             pb.sh_tiles = pb.sh_grp + 2;
             pb.disp = reinterpret_cast<int32_t*>(w + L.disp);
+            pb.X16 = reinterpret_cast<__half*>(w + L.X16);
             pb.H = reinterpret_cast<__half*>(w + L.Hpf);
             pb.Hs = reinterpret_cast<__half*>(w + L.Hs);
             pb.Y = reinterpret_cast<__half*>(w + L.Y);

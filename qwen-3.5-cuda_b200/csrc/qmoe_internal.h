@@ -60,7 +60,7 @@ struct WsLayout {
     // prefill regions (T > kDecodeMaxT): source token per permuted pair, tile
     // prefix per expert, the shared expert's group, dispatch scratch, fp16
     // hidden vectors and expert outputs
-    size_t tok_of_pos, tile_start, sh_grp, disp, Hpf, Hs, Y, Ys;
+    size_t tok_of_pos, tile_start, sh_grp, disp, X16, Hpf, Hs, Y, Ys;
     size_t xq_stride;  // bytes per token of x planes in shared memory: 3*d + (d/16)*8
     size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
     int H;             // max(F, Fs)
@@ -100,6 +100,7 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
         L.tile_start = take(sizeof(int32_t) * (E + 1));
         L.sh_grp = take(sizeof(int32_t) * 4);  // {0, T} and the shared expert's tile prefix {0, tiles}
         L.disp = take(sizeof(int32_t) * static_cast<size_t>(E) * 32);
+        L.X16 = take(2 * static_cast<size_t>(T) * d);
         L.Hpf = take(2 * static_cast<size_t>(P) * F);
         L.Hs = take(2 * static_cast<size_t>(T) * Fs);
         L.Y = take(2 * static_cast<size_t>(P) * d);
@@ -116,6 +117,7 @@ struct PrefillBufs {
     int32_t* sh_grp;    // [2] {0, T}
     int32_t* sh_tiles;  // [2] {0, ceil(T / 128)}
     int32_t* disp;
+    __half* X16;  // fp16 block input, chunk element order
     __half* H;
     __half* Hs;
     __half* Y;
