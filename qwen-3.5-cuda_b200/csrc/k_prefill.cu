@@ -9,7 +9,7 @@
 //                   experts as the reference for every token
 //   k_topk_many     one warp per token: top-k, softmax, checks (moe.cu:7-57,
 //                   layer_moe.cpp:102-124)
-//   k_dispatch      stable (expert, token, slot) permutation (k_dispatch.cu)
+//   k_pf_count/scan/place  stable (expert, token, slot) permutation
 //   k_pf_plan       source token of every permuted pair, tile prefix per expert
 //   k_pgemm<W,0>    gate/up: H[pair] = silu(x Wg^T) * (x Wu^T), fp16 (routed
 //                   experts: rows gathered by token; shared expert: all tokens)
@@ -610,6 +610,89 @@ __global__ void __launch_bounds__(256) k_topk_many(const float* __restrict__ log
 }
 
 // ---------------------------------------------------------------------------
+// Stable (expert, token, slot) permutation of the top-k result for many
+// tokens.  A token selects an expert at most once, so within a block of 64
+// tokens the pairs of expert e are described by a 64-bit token mask; a pair's
+// position is its expert's offset, plus the pairs of e in earlier blocks,
+// plus the earlier tokens of its own block in the mask.  Three small
+// kernels: masks -> per-block counts, one scan, placement.
+// ---------------------------------------------------------------------------
+constexpr int DB = 64;  // tokens per dispatch block
+
+__device__ __forceinline__ void pf_block_masks(const int32_t* idx, int T, int k, int E, int b,
+                                               unsigned long long* mask) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) mask[e] = 0ull;
+    __syncthreads();
+    const int t0 = b * DB;
+    for (int q = threadIdx.x; q < DB * k; q += blockDim.x) {
+        const int tl = q / k, t = t0 + tl;
+        if (t >= T) continue;
+        const int e = __ldg(idx + t * k + (q - tl * k));
+        if (e >= 0 && e < E) atomicOr(mask + e, 1ull << tl);
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) k_pf_count(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                  int32_t* __restrict__ counts) {
+    __shared__ unsigned long long mask[kMaxExperts];
+    pf_block_masks(idx, T, k, E, blockIdx.x, mask);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) counts[blockIdx.x * E + e] = __popcll(mask[e]);
+}
+
+// counts[b][e] -> first position of block b's pairs of expert e; offsets[E+1]
+__global__ void __launch_bounds__(256) k_pf_scan(int32_t* __restrict__ counts, int nb, int E, int32_t* __restrict__ offsets) {
+    __shared__ int s_wsum[8];
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    int run = 0;
+    if (e < E)
+        for (int b = 0; b < nb; ++b) {
+            const int c = counts[b * E + e];
+            counts[b * E + e] = run;
+            run += c;
+        }
+    int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) s_wsum[warp] = inc;
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int w = 0; w < 8; ++w) {
+        base += w < warp ? s_wsum[w] : 0;
+        total += s_wsum[w];
+    }
+    const int off = base + inc - run;
+    if (e < E) {
+        offsets[e] = off;
+        for (int b = 0; b < nb; ++b) counts[b * E + e] += off;
+    }
+    if (e == 0) offsets[E] = total;
+}
+
+__global__ void __launch_bounds__(256) k_pf_place(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                  const int32_t* __restrict__ counts, int32_t* __restrict__ perm,
+                                                  int32_t* __restrict__ inv_perm) {
+    __shared__ unsigned long long mask[kMaxExperts];
+    pf_block_masks(idx, T, k, E, blockIdx.x, mask);
+    const int t0 = blockIdx.x * DB;
+    for (int q = threadIdx.x; q < DB * k; q += blockDim.x) {
+        const int tl = q / k, t = t0 + tl;
+        if (t >= T) continue;
+        const int p = t * k + (q - tl * k);
+        const int e = __ldg(idx + p);
+        int rank = -1;
+        if (e >= 0 && e < E) {
+            rank = counts[blockIdx.x * E + e] + __popcll(mask[e] & ((1ull << tl) - 1ull));
+            perm[rank] = p;
+        }
+        inv_perm[p] = rank;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Source token of every permuted pair and the 128-row tile prefix per expert
 // (routed experts) plus the shared expert's single group [0, T).
 // ---------------------------------------------------------------------------
@@ -702,9 +785,6 @@ __global__ void __launch_bounds__(256) k_pf_combine(const __half* __restrict__ Y
 // Host side
 // ---------------------------------------------------------------------------
 namespace qmoe {
-
-cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
-                            int32_t* table, cudaStream_t s);
 
 namespace {
 
@@ -799,7 +879,13 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     k_topk_many<<<(T + 7) / 8, 256, 0, s>>>(P.logits, T, E, k, P.topk_idx, P.topk_w, P.out_idx, P.out_w, P.ctrl);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // 4. permutation
-    if ((e = launch_dispatch(P.topk_idx, T * k, E, P.offsets, P.perm, P.inv_perm, B.disp, s)) != cudaSuccess) return e;
+    {
+        const int nb = (T + DB - 1) / DB;
+        k_pf_count<<<nb, 256, 0, s>>>(P.topk_idx, T, k, E, B.disp);
+        k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, P.offsets);
+        k_pf_place<<<nb, 256, 0, s>>>(P.topk_idx, T, k, E, B.disp, P.perm, P.inv_perm);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
     // 5. plan
     k_pf_plan<<<64, 256, 0, s>>>(P.offsets, P.perm, E, k, T, B.tok_of_pos, B.tile_start, B.sh_grp, B.sh_tiles);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -99,7 +99,7 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
         L.tok_of_pos = take(sizeof(int32_t) * P);
         L.tile_start = take(sizeof(int32_t) * (E + 1));
         L.sh_grp = take(sizeof(int32_t) * 4);  // {0, T} and the shared expert's tile prefix {0, tiles}
-        L.disp = take(sizeof(int32_t) * static_cast<size_t>(E) * 32);
+        L.disp = take(sizeof(int32_t) * static_cast<size_t>(E) * ((T + 63) / 64));  // per-64-token-block counts
         L.X16 = take(2 * static_cast<size_t>(T) * d);
         L.Hpf = take(2 * static_cast<size_t>(P) * F);
         L.Hs = take(2 * static_cast<size_t>(T) * Fs);
