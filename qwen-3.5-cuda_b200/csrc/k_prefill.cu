@@ -47,15 +47,16 @@ constexpr int BN = 256;                // tile columns = MMA N (gate/up: 128 of 
 constexpr int BK = 32;                 // K per pipeline stage (64 bytes of fp16 per row)
 constexpr int NST = 5;                 // pipeline stages
 constexpr int LA = 3;                  // stages whose copies are in flight ahead of the dequantisation
-constexpr int PROD_WARPS = 8;          // copies + weight dequantisation (one B row per thread)
-constexpr int EPI_WARP0 = 8;           // warps 8..11: TMEM epilogue (lane quarter = warp % 4)
-constexpr int MMA_WARP = 12;           // one thread issues the MMAs
-constexpr int THREADS = 13 * 32;
+constexpr int PROD_WARPS = 16;         // copies + weight dequantisation (half a B row per thread)
+constexpr int PROD_THREADS = PROD_WARPS * 32;
+constexpr int EPI_WARP0 = 16;          // warps 16..19: TMEM epilogue (lane quarter = warp % 4)
+constexpr int MMA_WARP = 20;           // one thread issues the MMAs
+constexpr int THREADS = 21 * 32;
 constexpr uint32_t A_BYTES = BM * 64;    // 8 KB: fp16 activations of one stage
 constexpr uint32_t B_BYTES = BN * 64;    // 16 KB: fp16 weights of one stage
-constexpr uint32_t RAW_ROW = 48;         // Q4_K bytes of one row per stage: block header + 32 qs bytes
-constexpr uint32_t RAW_BYTES = BN * RAW_ROW;  // 12 KB
-constexpr uint32_t STAGE = A_BYTES + B_BYTES + RAW_BYTES;  // 36 KB (every part 1024-byte aligned)
+constexpr uint32_t RAW_SLOT = 32;        // Q4_K bytes per producer thread and stage: block header + 16 qs bytes
+constexpr uint32_t RAW_BYTES = PROD_THREADS * RAW_SLOT;  // 16 KB
+constexpr uint32_t STAGE = A_BYTES + B_BYTES + RAW_BYTES;  // 40 KB (every part 1024-byte aligned)
 constexpr uint32_t TMEM_COLS = 2 * BN;   // two accumulator buffers
 // instruction descriptor: D F32, A/B fp16, both K-major, N = 256, M = 128
 constexpr uint32_t IDESC = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
@@ -108,6 +109,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
+// 16 consecutive TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -123,9 +132,14 @@ __device__ __forceinline__ uint4 pack_chunk(const float (&v)[8]) {
     o.w = h2_bits(__floats2half2_rn(v[5], v[7]));
     return o;
 }
-__device__ __forceinline__ void dq_q4k_raw(uint32_t raw, int j, uint4 (&out)[4]) {
+// Two chunks (16 values) of one sub-block of a Q4_K row from a producer
+// thread's staged raw bytes: the block header (d, dmin, 12 scale bytes) and
+// 16 qs bytes of the 64-element group; sub-block j uses the low (j even) or
+// high nibbles.  value = d*sc*q - dmin*m (matmul_q4.cu:76-96), evaluated in
+// fp16 as (q*(d*sc)) - dmin*m after an exact nibble-to-half conversion.
+__device__ __forceinline__ void dq_q4k_raw(uint32_t raw, int j, uint4 (&out)[2]) {
     const uint4 hd = lds128(raw);
-    const uint4 qa = lds128(raw + 16), qb = lds128(raw + 32);
+    const uint4 q = lds128(raw + 16);
     float sc, m;
     kscale(hd.y, hd.z, hd.w, j, sc, m);
     const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
@@ -137,24 +151,18 @@ __device__ __forceinline__ void dq_q4k_raw(uint32_t raw, int j, uint4 (&out)[4])
         const __half2 raw2 = bits_h2(((w >> sh) & 0x000F000Fu) | 0x64006400u);
         return h2_bits(__hfma2(__hsub2(raw2, k1024), a, nb));
     };
-    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        out[c].x = cvt(q[2 * c]);
-        out[c].y = cvt(q[2 * c] >> 8);
-        out[c].z = cvt(q[2 * c + 1]);
-        out[c].w = cvt(q[2 * c + 1] >> 8);
-    }
+    out[0] = make_uint4(cvt(q.x), cvt(q.x >> 8), cvt(q.y), cvt(q.y >> 8));
+    out[1] = make_uint4(cvt(q.z), cvt(q.z >> 8), cvt(q.w), cvt(q.w >> 8));
 }
 
-// any other type: 32 values of one row with the reference's per-element
-// formulas (dq1), read from global memory
-__device__ __forceinline__ void dq_generic(const uint8_t* row, int type, int k0, uint4 (&out)[4]) {
+// any other type: 16 values (chunks c0, c0+1) of one row with the
+// reference's per-element formulas (dq1), read from global memory
+__device__ __forceinline__ void dq_generic(const uint8_t* row, int type, int k0, int c0, uint4 (&out)[2]) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
         float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = dq1(row, type, static_cast<uint64_t>(k0 + 8 * c + e));
+        for (int e = 0; e < 8; ++e) v[e] = dq1(row, type, static_cast<uint64_t>(k0 + 8 * (c0 + c) + e));
         out[c] = pack_chunk(v);
     }
 }
@@ -240,7 +248,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
         int ct = blockIdx.x, ckb = 0, cstep = 0;
         PfTile iT = it < total ? pf_tile(p, it, nN) : PfTile{};
         PfTile cT = iT;
-        const int row = tid;  // B row of this thread; A chunks tid and tid + 256
+        const int row = tid >> 1, half = tid & 1;  // chunks 2*half, 2*half+1 of B row `row`; A chunk tid
+        // source row of this thread's A chunk, looked up once per tile
+        int a_src = -1;
+        auto a_rows_of = [&](const PfTile& T) {
+            const int orow = T.r0 + (tid >> 2);
+            a_src = orow < T.r1 ? (p.a_rows ? __ldg(p.a_rows + orow) : orow) : -1;
+        };
+        if (it < total) a_rows_of(iT);
         auto wrow = [&](const PfTile& T) -> const uint8_t* {
             const uint8_t* base = (MODE == 0 && row >= BN / 2) ? p.w1 : p.w0;
             const int n = MODE == 0 ? T.nt * (BN / 2) + (row & (BN / 2 - 1)) : T.nt * BN + row;
@@ -251,28 +266,27 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
             if (istep >= NST) mbar_wait(empty + stage, (istep / NST - 1) & 1, p.ctrl);
             const uint32_t sa = smem_u32(smem + stage * STAGE);
             const int k0 = ikb * BK;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {  // A: 128 rows x 4 chunks
-                const int q = tid + j * (PROD_WARPS * 32);
-                const int r = q >> 2, c = q & 3;
-                const int orow = iT.r0 + r;
-                const bool ok = orow < iT.r1;
-                const int src = ok ? (p.a_rows ? __ldg(p.a_rows + orow) : orow) : 0;
-                cp_async16(sa + sw_off(r, c), p.a16 + static_cast<size_t>(src) * p.K + k0 + 8 * c, ok ? 16u : 0u);
+            {  // A: 128 rows x 4 chunks (rows past the group are zero-filled)
+                const int r = tid >> 2, c = tid & 3;
+                const bool ok = a_src >= 0;
+                cp_async16(sa + sw_off(r, c), p.a16 + static_cast<size_t>(ok ? a_src : 0) * p.K + k0 + 8 * c,
+                           ok ? 16u : 0u);
             }
-            if (WT == T_Q4_K) {  // raw bytes of this thread's B row: header + 32 qs bytes of the group
+            if (WT == T_Q4_K) {  // raw bytes: block header + this half's 16 qs bytes of the group
                 const uint8_t* blk = wrow(iT) + (k0 >> 8) * 144;
-                const uint32_t rd = sa + A_BYTES + B_BYTES + row * RAW_ROW;
+                const uint32_t rd = sa + A_BYTES + B_BYTES + tid * RAW_SLOT;
                 cp_async16(rd, blk, 16u);
-                cp_async16(rd + 16, blk + 16 + 32 * ((k0 >> 6) & 3), 16u);
-                cp_async16(rd + 32, blk + 32 + 32 * ((k0 >> 6) & 3), 16u);
+                cp_async16(rd + 16, blk + 16 + 32 * ((k0 >> 6) & 3) + 16 * half, 16u);
             }
             cp_async_commit();
             ++istep;
             if (++ikb == nK) {
                 ikb = 0;
                 it += gridDim.x;
-                if (it < total) iT = pf_tile(p, it, nN);
+                if (it < total) {
+                    iT = pf_tile(p, it, nN);
+                    a_rows_of(iT);
+                }
             }
         };
         const int nsteps = ((total - blockIdx.x + gridDim.x - 1) / gridDim.x) * nK;
@@ -282,11 +296,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
             cp_async_wait<LA>();  // this thread's copies for step cstep have landed
             const int stage = cstep % NST;
             uint8_t* sb = smem + stage * STAGE + A_BYTES;
-            uint4 v[4];
-            if (WT == T_Q4_K) dq_q4k_raw(smem_u32(sb + B_BYTES + row * RAW_ROW), (ckb * BK / 32) & 7, v);
-            else dq_generic(wrow(cT), WT, ckb * BK, v);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(sb + sw_off(row, c)) = v[c];
+            uint4 v[2];
+            if (WT == T_Q4_K) dq_q4k_raw(smem_u32(sb + B_BYTES + tid * RAW_SLOT), (ckb * BK / 32) & 7, v);
+            else dq_generic(wrow(cT), WT, ckb * BK, 2 * half, v);
+            *reinterpret_cast<uint4*>(sb + sw_off(row, 2 * half)) = v[0];
+            *reinterpret_cast<uint4*>(sb + sw_off(row, 2 * half + 1)) = v[1];
             fence_async_smem();  // generic and cp.async stores -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(full + stage);
@@ -332,22 +346,23 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
             const int orow = T.r0 + 32 * quarter + lane;
             const uint32_t tl = tmem + buf * BN + (static_cast<uint32_t>(32 * quarter) << 16);
             __half* dst = p.out + static_cast<size_t>(orow) * p.N + T.nt * ncol;
-            for (int c0 = 0; c0 < ncol; c0 += 32) {
-                uint32_t a[32];
-                tmem_ld32(tl + c0, a);
-                uint32_t o[16];
+            for (int c0 = 0; c0 < ncol; c0 += 16) {
+                uint32_t a[16];
+                tmem_ld16(tl + c0, a);
+                uint32_t o[8];
                 if (MODE == 0) {
-                    uint32_t u[32];
-                    tmem_ld32(tl + BN / 2 + c0, u);
+                    uint32_t u[16];
+                    tmem_ld16(tl + BN / 2 + c0, u);
                     tmem_wait_ld();
-                    float h[32];
+                    float h[16];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
+                    for (int i = 0; i < 16; ++i) {
                         const float g = __uint_as_float(a[i]);
-                        h[i] = g / (1.0f + expf(-g)) * __uint_as_float(u[i]);  // moe.cu:64
+                        // moe.cu:64 (fast exp/divide: the result is rounded to fp16 next)
+                        h[i] = __fdividef(g, 1.0f + __expf(-g)) * __uint_as_float(u[i]);
                     }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {  // chunk element order for the down GEMM
+                    for (int c = 0; c < 2; ++c) {  // chunk element order for the down GEMM
                         o[4 * c] = h2_bits(__floats2half2_rn(h[8 * c], h[8 * c + 2]));
                         o[4 * c + 1] = h2_bits(__floats2half2_rn(h[8 * c + 1], h[8 * c + 3]));
                         o[4 * c + 2] = h2_bits(__floats2half2_rn(h[8 * c + 4], h[8 * c + 6]));
@@ -356,13 +371,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
                 } else {
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
+                    for (int i = 0; i < 8; ++i)
                         o[i] = h2_bits(__floats2half2_rn(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1])));
                 }
                 if (orow < T.r1) {
                     uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                    d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
                 }
             }
             tc_fence_before();
