@@ -283,10 +283,133 @@ def run_ours(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"], line["parity"] = cpu_baseline(args, blocks, inputs, dims, dc, ws, nws)
+    if world == 1 and not args.no_extra:
+        line["prefill"] = measure_prefill(blocks[0], dims)
+        line["config3"] = measure_config3(dims)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+PREFILL_T = 4096
+ZIPF_BETA = 1.0  # per-expert logit bias -beta * 1.1 * ln(rank): a Zipf(1.1)-like hit histogram
+
+
+def measure_prefill(blk, dims):
+    """one MoE block over T=4096 tokens (prefill), Q4_K
+    experts, router skewed by a seeded per-expert logit bias so expert
+    popularity is heavy-tailed; grouped expert GEMMs on the tensor cores.
+    Timed with CUDA events over repeated calls (inputs: 32 MB of tokens and
+    ~460 MB of weights per call, larger than L2)."""
+    import numpy as np
+    import torch
+
+    from qmoe import _lib
+
+    T = PREFILL_T
+    dc = dims.c()
+    rng = np.random.default_rng(SEED + 4)
+    ranks = rng.permutation(dims.num_experts) + 1
+    bias = torch.tensor(-ZIPF_BETA * 1.1 * np.log(ranks), dtype=torch.float32, device="cuda")
+    c = blk.c()
+    c.expert_bias = bias.data_ptr()
+    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
+    x = torch.randn(T, dims.d_model, generator=g, device="cuda", dtype=torch.float32)
+    n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
+    out = torch.empty_like(x)
+
+    def run():
+        _lib.check(_lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(), out.data_ptr(),
+                                                 None, T, ws.data_ptr(), n, None), "prefill block_forward")
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    st, flags, _ = _check_errors(_lib, ws, dc)
+    p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_OFFSETS)
+    off = p - ws.data_ptr()
+    counts = np.diff(ws[off:off + 4 * (dims.num_experts + 1)].cpu().numpy().view(np.int32))
+    k, F, d = dims.top_k, dims.expert_dim, dims.d_model
+    flop = 2.0 * T * k * 3 * F * d + 2.0 * T * 3 * dims.shared_dim * d  # routed + shared expert products
+    tflops = flop / (us * 1e-6) / 1e12
+    peak = _bf16_peak()
+    return {"config": "config4: T=4096 tokens x d=2048, 256 Q4_K experts, top-8, Zipf(1.1)-like routing "
+                      "(logit bias -1.1*beta*ln(rank), beta=%.1f)" % ZIPF_BETA,
+            "us_per_block": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 0),
+            "expert_gflop": round(flop / 1e9, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak[0], "unit": "TFLOP/s",
+                         "frac": round(tflops / peak[0], 4), "peak_kind": peak[1],
+                         "note": "whole block (router, top-k, dispatch, GEMMs, combine) against dense bf16 peak"},
+            "routing": {"experts_hit": int((counts > 0).sum()), "max_per_expert": int(counts.max()),
+                        "mean_per_hit_expert": round(float(counts[counts > 0].mean()), 1)},
+            "error_flags": flags}
+
+
+def measure_config3(dims):
+    """mixed-quant decode (gate/up Q4_K, down Q6_K, shared
+    Q8_0, per-expert router bias ~N(0,1)) at B = 1, 2, 4, 8 tokens per call,
+    through 8 layers (~4 GB of weights, larger than L2)."""
+    import torch
+
+    from qmoe import _lib, synth
+
+    L = 8
+    blocks = [synth.Block(dims, synth.MIXED_TYPES, seed=SEED + 3, layer=l, device="cuda", bias=True) for l in range(L)]
+    cbs = [b.c() for b in blocks]
+    dc = dims.c()
+    res = []
+    for B in (1, 2, 4, 8):
+        n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), B)
+        ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+        _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
+        x = synth.inputs(B, dims.d_model, seed=SEED + B, tag=3)
+        bufs = [torch.empty_like(x), torch.empty_like(x)]
+        gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")
+
+        def step():
+            cur = x
+            for l in range(L):
+                o = bufs[l % 2]
+                _lib.check(_lib.lib().qmoe_block_forward_prenorm(ctypes.byref(cbs[l]), ctypes.byref(dc),
+                                                                 cur.data_ptr(), gamma.data_ptr(), EPS,
+                                                                 o.data_ptr(), B, ws.data_ptr(), n, None))
+                cur = o
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        reps = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+        st, flags, _ = _check_errors(_lib, ws, dc)
+        res.append({"B": B, "us_per_block": round(us, 2), "us_per_token_block": round(us / B, 2),
+                    "error_flags": flags})
+    return {"config": "config3: mixed-quant decode (gate/up Q4_K, down Q6_K, shared Q8_0, router bias N(0,1)), "
+                      "8 layers, eager launches", "results": res}
+
+
+def _bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def _check_errors(_lib, ws, dc):
@@ -431,6 +554,7 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the prefill (config 4) and mixed decode (config 3) lines")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
