@@ -14,8 +14,12 @@ blocks run in sequence like in the model.  Metric: microseconds per token per Mo
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (torchrun, one rank per GPU): independent replicas of the same decode
-stream (the decode path does not shard); max-over-ranks device time.
+N > 1 (torchrun, one rank per GPU): the headline decode line runs
+independent replicas of the same decode stream (decode does not shard);
+max-over-ranks device time.  The path that shards is prefill: the
+``ep_prefill`` object runs T=16384 tokens through one
+block with the experts split over the N GPUs and NCCL all-to-all between
+them; at N = 1 it is the same block on one GPU.
 --impl reference: the reference's CPU path for the same op (the C
 restatement in oracle/, all host threads), rank 0 only.
 """
@@ -286,6 +290,9 @@ def run_ours(args):
     if world == 1 and not args.no_extra:
         line["prefill"] = measure_prefill(blocks[0], dims)
         line["config3"] = measure_config3(dims)
+    if not args.no_extra:
+        del blocks, cblocks
+        line["ep_prefill"] = measure_ep(world, rank, dims)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
@@ -309,9 +316,7 @@ def measure_prefill(blk, dims):
 
     T = PREFILL_T
     dc = dims.c()
-    rng = np.random.default_rng(SEED + 4)
-    ranks = rng.permutation(dims.num_experts) + 1
-    bias = torch.tensor(-ZIPF_BETA * 1.1 * np.log(ranks), dtype=torch.float32, device="cuda")
+    bias = _zipf_bias(dims)
     c = blk.c()
     c.expert_bias = bias.data_ptr()
     g = torch.Generator(device="cuda").manual_seed(SEED + 5)
@@ -354,6 +359,109 @@ def measure_prefill(blk, dims):
             "routing": {"experts_hit": int((counts > 0).sum()), "max_per_expert": int(counts.max()),
                         "mean_per_hit_expert": round(float(counts[counts > 0].mean()), 1)},
             "error_flags": flags}
+
+
+EP_T = 16384
+
+
+def _zipf_bias(dims):
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(SEED + 4)
+    ranks = rng.permutation(dims.num_experts) + 1
+    return torch.tensor(-ZIPF_BETA * 1.1 * np.log(ranks), dtype=torch.float32, device="cuda")
+
+
+def measure_ep(world, rank, dims):
+    """T=16384 tokens of prefill through one Q4_K MoE block,
+    uniform and Zipf-skewed routing.  world == 1: the whole block on one GPU
+    (qmoe_block_forward).  world > 1: expert parallelism -- E/world experts
+    per rank, T/world tokens per rank, NCCL all-to-all of the (token, expert)
+    rows and of their outputs (qmoe/ep.py).  Every rank also runs the 1-GPU
+    block on all T tokens once and checks that its routing is bit-identical
+    and its output equal.  Time: CUDA events around repeated calls, max over
+    ranks; tokens/s counts all T tokens (total work fixed: strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from qmoe import _lib, ep, synth
+
+    T, d, E, k = EP_T, dims.d_model, dims.num_experts, dims.top_k
+    Tl = T // world
+    dc = dims.c()
+    blk = synth.Block(dims, synth.Q4K_TYPES, seed=SEED + 7, device="cuda")  # the same bytes on every rank
+    g = torch.Generator(device="cuda").manual_seed(SEED + 8)
+    x_all = torch.randn(T, d, generator=g, device="cuda", dtype=torch.float32)
+    x = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
+    zipf = _zipf_bias(dims)
+    n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
+    out_all = torch.empty_like(x_all)
+    flop = 2.0 * T * k * 3 * dims.expert_dim * d + 2.0 * T * 3 * dims.shared_dim * d
+    peak = _bf16_peak()
+    reps = 10
+    res = {"config": f"config5: T={T} tokens x d={d}, {E} Q4_K experts ({E // world} per GPU), top-{k}, "
+                     f"{world} GPU(s), fp16 rows over NCCL all-to-all" if world > 1 else
+                     f"config5 at 1 GPU: T={T} tokens x d={d}, {E} Q4_K experts, top-{k}, one block_forward",
+           "n_gpus": world, "scaling": "strong", "routings": {}}
+    for routing in ("uniform", "zipf"):
+        c = blk.c()
+        if routing == "zipf":
+            c.expert_bias = zipf.data_ptr()
+
+        def one_gpu():
+            _lib.check(_lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(dc), x_all.data_ptr(),
+                                                     out_all.data_ptr(), None, T, ws.data_ptr(), n, None),
+                       "block_forward")
+
+        one_gpu()
+        torch.cuda.synchronize()
+        entry = {}
+        if world == 1:
+            run = one_gpu
+        else:
+            p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_TOPK_IDX)
+            off = p - ws.data_ptr()
+            want_idx = ws[off:off + T * k * 4].view(torch.int32).view(T, k)[rank * Tl:(rank + 1) * Tl].clone()
+            lb, ld = ep.local_block(c, dc, rank, world)
+            be = ep.CudaBackend(c, lb, dc, ld, max_tokens=Tl, max_rows=2 * Tl * k)
+            moe = ep.ExpertParallelMoE(be, E, k, d)
+            got = moe.forward(x)
+            idx = be._view(_lib.WS_TOPK_IDX, Tl * k, torch.int32).view(Tl, k)
+            want = out_all[rank * Tl:(rank + 1) * Tl]
+            chk = torch.tensor([0.0 if torch.equal(idx, want_idx) else 1.0, float((got - want).abs().max())],
+                               dtype=torch.float64, device="cuda")
+            dist.all_reduce(chk, op=dist.ReduceOp.MAX)
+            entry["parity"] = {"ids_bit_identical_to_1gpu": chk[0].item() == 0.0, "max_abs_diff_vs_1gpu": chk[1].item()}
+
+            def run():
+                moe.forward(x)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        if world > 1:
+            t = torch.tensor([us], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t[0])
+        tflops = flop / (us * 1e-6) / 1e12
+        entry.update({"us_per_block": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 0),
+                      "tflops_per_gpu": round(tflops / world, 1),
+                      "frac_of_peak_per_gpu": round(tflops / world / peak[0], 4)})
+        res["routings"][routing] = entry
+    res["peak"] = {"bf16_tflops": peak[0], "kind": peak[1]}
+    res["expert_gflop"] = round(flop / 1e9, 1)
+    return res
 
 
 def measure_config3(dims):

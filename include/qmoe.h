@@ -20,6 +20,7 @@
  *   qmoe_expert_gateup    src/layer_moe.cpp:131-135, 147-149 (gate/up GEMVs,
  *                         moe_silu_mul) for all routed pairs + shared expert
  *   qmoe_expert_block     src/layer_moe.cpp:127-154 (all expert work after routing)
+ *   qmoe_ep_*             no counterpart (expert parallelism across GPUs)
  *   qmoe_down_combine     src/layer_moe.cpp:138-141, 150-154 (down GEMVs,
  *                         moe_add, moe_shared_add, final copy)
  *   qmoe_block_forward    src/layer_moe.cpp:82-155   MoeLayer::forward, for
@@ -103,7 +104,9 @@ enum qmoe_ws_buffer {
     QMOE_WS_INV_PERM = 5, /* int32 [T*k]  permuted position of each pair (-1: invalid) */
     QMOE_WS_HIDDEN = 6,   /* float [T*k + T][max(F,Fs)] silu(gate)*up: routed pairs, then shared per token */
     QMOE_WS_ERROR = 7,    /* uint32 [4]: error flags, first failing token, spare */
-    QMOE_WS_INPUT = 8     /* float [T][d] the block input as the router saw it (after the fused norm) */
+    QMOE_WS_INPUT = 8,    /* float [T][d] the block input as the router saw it (after the fused norm) */
+    QMOE_WS_INPUT16 = 9   /* fp16 [T][d] the same input for the tensor cores (T > 8 only), each
+                             8-element chunk stored in the order 0,2,1,3,4,6,5,7 */
 };
 
 /* ABI version of this header (bumped on any incompatible change). */
@@ -180,6 +183,32 @@ QMOE_API int qmoe_down_combine(const qmoe_block* blk, const qmoe_dims* dims, int
 QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int T,
                       float* out, const float* residual,
                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Expert parallelism for prefill (experts sharded across GPUs; the caller
+ * moves rows between ranks, e.g. with NCCL all-to-all).  No counterpart in
+ * the reference, which runs on one GPU.  For T > 8 local tokens:
+ *   qmoe_ep_route    x_in (optional pre-MoE RMSNorm), its fp16 copy
+ *                    (QMOE_WS_INPUT16) and the top-k of every local token
+ *                    (QMOE_WS_TOPK_IDX / QMOE_WS_TOPK_W), in `workspace`
+ *   qmoe_ep_experts  this rank's experts on n received rows: rows [n][d] in
+ *                    the QMOE_WS_INPUT16 format, expert_ids [n] local to the
+ *                    rank (0 .. local_dims->num_experts-1), y_rows [n][d] fp16
+ *                    = down(silu(gate x) * up x) of each row's expert
+ *   qmoe_ep_combine  shared expert and combine of the T local tokens from
+ *                    y_pairs [T*k][d] fp16 in pair order (p = t*k + j):
+ *                    out[t] = residual[t] + sum_j w[t][j] y_pairs[t*k+j]
+ *                             + sigmoid(shared gate) * shared(x_in[t])
+ * local_blk holds the rank's slices of the expert tensors (router and shared
+ * tensors are not read); its workspace comes from qmoe_ep_rows_workspace_size. */
+QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max_rows);
+QMOE_API int qmoe_ep_route(const qmoe_block* blk, const qmoe_dims* dims, const float* x, const float* norm_weight,
+                   float eps, int T, void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+QMOE_API int qmoe_ep_experts(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
+                     const int32_t* expert_ids, int n_rows, void* y_rows, void* workspace,
+                     size_t workspace_bytes, qmoe_stream_t stream);
+QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs, int T,
+                     const float* residual, float* out, void* workspace, size_t workspace_bytes,
+                     qmoe_stream_t stream);
 
 /* Number of kernels one qmoe_block_forward call with these arguments launches
  * (for profiling and launch accounting); negative status on bad arguments. */

@@ -181,6 +181,7 @@ struct GemmParams {
     const int32_t* grp_start;   // [groups + 1] first output row of each group
     const int32_t* tile_start;  // [groups + 1] prefix of 128-row tiles per group
     __half* out;                // [rows][N]; MODE 0 in the chunk element order
+    const int32_t* out_rows;    // MODE 1: output row of each tile row (null: the tile row itself)
     uint32_t* ctrl;             // error word
 };
 
@@ -345,7 +346,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
             tc_fence_after();
             const int orow = T.r0 + 32 * quarter + lane;
             const uint32_t tl = tmem + buf * BN + (static_cast<uint32_t>(32 * quarter) << 16);
-            __half* dst = p.out + static_cast<size_t>(orow) * p.N + T.nt * ncol;
+            const int drow = (MODE == 1 && p.out_rows && orow < T.r1) ? __ldg(p.out_rows + orow) : orow;
+            __half* dst = p.out + static_cast<size_t>(drow) * p.N + T.nt * ncol;
             for (int c0 = 0; c0 < ncol; c0 += 16) {
                 uint32_t a[16];
                 tmem_ld16(tl + c0, a);
@@ -758,7 +760,9 @@ __global__ void __launch_bounds__(256) k_pf_combine(const __half* __restrict__ Y
     __shared__ float s_w[kMaxTopK];
     __shared__ float s_sg;
     if (threadIdx.x < k) {
-        s_pos[threadIdx.x] = __ldg(inv_perm + t * k + threadIdx.x);
+        // pair (t, j) sits at its permuted position, or at t*k + j when the
+        // expert outputs come back in pair order (expert-parallel path)
+        s_pos[threadIdx.x] = inv_perm ? __ldg(inv_perm + t * k + threadIdx.x) : t * k + threadIdx.x;
         s_w[threadIdx.x] = __ldg(wts + t * k + threadIdx.x);
     }
     if (threadIdx.x == 0) s_sg = has_shared ? 1.0f / (1.0f + expf(-__ldg(logits + static_cast<size_t>(t) * (E + 1) + E))) : 0.0f;
@@ -851,25 +855,24 @@ bool prefill_supported(const DecodeParams& P) {
     return pf_num_sms() > 0;
 }
 
-// The whole block for T tokens through the prefill kernels.  `xin` is the
-// block input after the optional norm, `pf` the prefill workspace regions.
-cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) {
+// Steps of the prefill path, also used by the expert-parallel entry points.
+// x_in / X16 and the routing of T tokens.
+cudaError_t pf_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) {
     const int T = P.T, d = P.d, E = P.E, k = P.k;
     const int CH = d / 256;
     cudaError_t e = cudaSuccess;
-    // 1. x_in
     {
         const dim3 grid((T + 7) / 8);
+        const float* nw = P.prenorm ? P.norm_w : nullptr;
         switch (CH) {
-            case 1: k_norm_many<1><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
-            case 2: k_norm_many<2><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
-            case 4: k_norm_many<4><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
-            case 8: k_norm_many<8><<<grid, 256, 0, s>>>(P.x, P.prenorm ? P.norm_w : nullptr, P.eps, P.xnorm, B.X16, T, d); break;
+            case 1: k_norm_many<1><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
+            case 2: k_norm_many<2><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
+            case 4: k_norm_many<4><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
+            case 8: k_norm_many<8><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
             default: return cudaErrorInvalidValue;
         }
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    // 2. router logits
     {
         const int nrows = E + (P.has_shared ? 1 : 0);
         const int rgroups = (((nrows + 1) / 2) + 7) / 8;  // CTAs of 16 router rows
@@ -890,23 +893,30 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
 #undef QMOE_RM
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    // 3. top-k per token
     k_topk_many<<<(T + 7) / 8, 256, 0, s>>>(P.logits, T, E, k, P.topk_idx, P.topk_w, P.out_idx, P.out_w, P.ctrl);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    // 4. permutation
-    {
-        const int nb = (T + DB - 1) / DB;
-        k_pf_count<<<nb, 256, 0, s>>>(P.topk_idx, T, k, E, B.disp);
-        k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, P.offsets);
-        k_pf_place<<<nb, 256, 0, s>>>(P.topk_idx, T, k, E, B.disp, P.perm, P.inv_perm);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    // 5. plan
-    k_pf_plan<<<64, 256, 0, s>>>(P.offsets, P.perm, E, k, T, B.tok_of_pos, B.tile_start, B.sh_grp, B.sh_tiles);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    // 6. gate/up: routed, then shared
+    return cudaGetLastError();
+}
+
+// Permutation of the (row, slot) pairs of `idx` [T][k] by expert, and the
+// GEMM tile plan.
+static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t* offsets, int32_t* perm,
+                               int32_t* inv_perm, const PrefillBufs& B, cudaStream_t s) {
+    const int nb = (T + DB - 1) / DB;
+    k_pf_count<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp);
+    k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, offsets);
+    k_pf_place<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp, perm, inv_perm);
+    k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, T, B.tok_of_pos, B.tile_start, B.sh_grp, B.sh_tiles);
+    return cudaGetLastError();
+}
+
+// Routed experts: rows A (fp16, chunk order) gathered through tok_of_pos,
+// hidden H, outputs Y (rows = permuted positions, or `out_rows` order).
+static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const __half* a16, __half* y,
+                             const int32_t* out_rows, cudaStream_t s) {
+    const int d = P.d;
+    cudaError_t e;
     pf::GemmParams g{};
-    g.a16 = B.X16;
+    g.a16 = a16;
     g.a_rows = B.tok_of_pos;
     g.w0 = P.gate.p;
     g.w1 = P.up.p;
@@ -915,28 +925,12 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     g.wtype = P.gate.type;
     g.N = P.F;
     g.K = d;
-    g.groups = E;
+    g.groups = P.E;
     g.grp_start = P.offsets;
     g.tile_start = B.tile_start;
     g.out = B.H;
     g.ctrl = P.ctrl;
     if ((e = launch_pgemm<0>(g, s)) != cudaSuccess) return e;
-    if (P.has_shared) {
-        pf::GemmParams gs = g;
-        gs.a_rows = nullptr;
-        gs.w0 = P.sgate.p;
-        gs.w1 = P.sup.p;
-        gs.w_row_bytes = static_cast<uint32_t>(row_bytes(P.sgate.type, d));
-        gs.w_group_bytes = static_cast<uint64_t>(P.Fs) * gs.w_row_bytes;
-        gs.wtype = P.sgate.type;
-        gs.N = P.Fs;
-        gs.groups = 1;
-        gs.grp_start = B.sh_grp;
-        gs.tile_start = B.sh_tiles;
-        gs.out = B.Hs;
-        if ((e = launch_pgemm<0>(gs, s)) != cudaSuccess) return e;
-    }
-    // 7. down: routed, then shared
     pf::GemmParams dn{};
     dn.a16 = B.H;
     dn.w0 = P.down.p;
@@ -945,30 +939,83 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     dn.wtype = P.down.type;
     dn.N = d;
     dn.K = P.F;
-    dn.groups = E;
+    dn.groups = P.E;
     dn.grp_start = P.offsets;
     dn.tile_start = B.tile_start;
-    dn.out = B.Y;
+    dn.out = y;
+    dn.out_rows = out_rows;
     dn.ctrl = P.ctrl;
-    if ((e = launch_pgemm<1>(dn, s)) != cudaSuccess) return e;
+    return launch_pgemm<1>(dn, s);
+}
+
+// Shared expert over all T tokens (rows of X16), then the combine of the
+// routed outputs Y (at inv_perm positions, or in pair order when null).
+static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B, const __half* Y,
+                                     const int32_t* inv_perm, cudaStream_t s) {
+    const int d = P.d;
+    cudaError_t e;
     if (P.has_shared) {
-        pf::GemmParams ds = dn;
+        pf::GemmParams gs{};
+        gs.a16 = B.X16;
+        gs.w0 = P.sgate.p;
+        gs.w1 = P.sup.p;
+        gs.w_row_bytes = static_cast<uint32_t>(row_bytes(P.sgate.type, d));
+        gs.w_group_bytes = static_cast<uint64_t>(P.Fs) * gs.w_row_bytes;
+        gs.wtype = P.sgate.type;
+        gs.N = P.Fs;
+        gs.K = d;
+        gs.groups = 1;
+        gs.grp_start = B.sh_grp;
+        gs.tile_start = B.sh_tiles;
+        gs.out = B.Hs;
+        gs.ctrl = P.ctrl;
+        if ((e = launch_pgemm<0>(gs, s)) != cudaSuccess) return e;
+        pf::GemmParams ds{};
         ds.a16 = B.Hs;
         ds.w0 = P.sdown.p;
         ds.w_row_bytes = static_cast<uint32_t>(row_bytes(P.sdown.type, P.Fs));
         ds.w_group_bytes = static_cast<uint64_t>(d) * ds.w_row_bytes;
         ds.wtype = P.sdown.type;
+        ds.N = d;
         ds.K = P.Fs;
         ds.groups = 1;
         ds.grp_start = B.sh_grp;
         ds.tile_start = B.sh_tiles;
         ds.out = B.Ys;
+        ds.ctrl = P.ctrl;
         if ((e = launch_pgemm<1>(ds, s)) != cudaSuccess) return e;
     }
-    // 8. combine
-    k_pf_combine<<<T, 256, 0, s>>>(B.Y, B.Ys, P.inv_perm, P.topk_w, P.logits, P.residual, P.out, d, E, k,
-                                   P.has_shared);
+    k_pf_combine<<<P.T, 256, 0, s>>>(Y, B.Ys, inv_perm, P.topk_w, P.logits, P.residual, P.out, d, P.E, P.k,
+                                     P.has_shared);
     return cudaGetLastError();
+}
+
+// The whole block for T tokens through the prefill kernels.
+cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) {
+    cudaError_t e;
+    if ((e = pf_route(P, B, s)) != cudaSuccess) return e;
+    if ((e = pf_dispatch(P.topk_idx, P.T, P.k, P.E, P.offsets, P.perm, P.inv_perm, B, s)) != cudaSuccess) return e;
+    if ((e = pf_routed(P, B, B.X16, B.Y, nullptr, s)) != cudaSuccess) return e;
+    return pf_shared_combine(P, B, B.Y, P.inv_perm, s);
+}
+
+// Expert-parallel pieces.  Route: x_in, X16 and top-k of T local tokens.
+cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) { return pf_route(P, B, s); }
+
+// This rank's experts on n received rows: rows x16 [n][d] (chunk order),
+// local expert ids eid [n]; outputs y [n][d] fp16 in row order.  P is set
+// up for T = n rows, k = 1, E = local experts.
+cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* eid,
+                              __half* y, cudaStream_t s) {
+    cudaError_t e;
+    if ((e = pf_dispatch(eid, P.T, 1, P.E, P.offsets, P.perm, P.inv_perm, B, s)) != cudaSuccess) return e;
+    return pf_routed(P, B, x16, y, B.tok_of_pos, s);
+}
+
+// Shared expert and combine of T local tokens, y_pairs [T*k][d] fp16 in
+// pair order (zero rows for pairs of failed tokens).
+cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs, cudaStream_t s) {
+    return pf_shared_combine(P, B, y_pairs, nullptr, s);
 }
 
 }  // namespace qmoe

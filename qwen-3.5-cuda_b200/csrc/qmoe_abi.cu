@@ -14,6 +14,10 @@ bool decode_supported(const DecodeParams& P);
 bool fused_supported(const DecodeParams& P);
 bool prefill_supported(const DecodeParams& P);
 cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
+cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
+cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* eid,
+                              __half* y, cudaStream_t s);
+cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs, cudaStream_t s);
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
 int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
@@ -139,6 +143,23 @@ DecodeParams make_params(const qmoe_block* B, const qmoe_dims* D, const float* x
     return P;
 }
 
+PrefillBufs prefill_bufs(const qmoe_dims& D, int T, void* ws) {
+    const WsLayout L = ws_layout(D, T);
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    PrefillBufs pb;
+    pb.tok_of_pos = reinterpret_cast<int32_t*>(w + L.tok_of_pos);
+    pb.tile_start = reinterpret_cast<int32_t*>(w + L.tile_start);
+    pb.sh_grp = reinterpret_cast<int32_t*>(w + L.sh_grp);
+    pb.sh_tiles = pb.sh_grp + 2;
+    pb.disp = reinterpret_cast<int32_t*>(w + L.disp);
+    pb.X16 = reinterpret_cast<__half*>(w + L.X16);
+    pb.H = reinterpret_cast<__half*>(w + L.Hpf);
+    pb.Hs = reinterpret_cast<__half*>(w + L.Hs);
+    pb.Y = reinterpret_cast<__half*>(w + L.Y);
+    pb.Ys = reinterpret_cast<__half*>(w + L.Ys);
+    return pb;
+}
+
 int check_common(const qmoe_block* B, const qmoe_dims* D, int T, void* ws, size_t ws_bytes, int maxT) {
     int st;
     if ((st = check_dims(D))) return st;
@@ -219,6 +240,7 @@ void* qmoe_ws_view(void* ws, const qmoe_dims* D, int T, int which) {
         case QMOE_WS_HIDDEN: return w + L.hidden;
         case QMOE_WS_ERROR: return w + L.ctrl + CTRL_ERROR * 4;
         case QMOE_WS_INPUT: return w + L.xnorm;
+        case QMOE_WS_INPUT16: return T > kDecodeMaxT ? w + L.X16 : nullptr;
         default: return nullptr;
     }
 }
@@ -303,6 +325,79 @@ int qmoe_expert_block(const qmoe_block* B, const qmoe_dims* D, int T, float* out
     return cuda_status(e);
 }
 
+// ---- expert parallelism ----
+static qmoe_dims ep_row_dims(const qmoe_dims& D) {
+    qmoe_dims r = D;
+    r.top_k = 1;  // one (row, expert) pair per received row
+    return r;
+}
+
+size_t qmoe_ep_rows_workspace_size(const qmoe_dims* D, int max_rows) {
+    if (check_dims(D) || max_rows <= 0) return 0;
+    return ws_layout(ep_row_dims(*D), std::max(max_rows, kDecodeMaxT + 1)).total;
+}
+
+int qmoe_ep_route(const qmoe_block* B, const qmoe_dims* D, const float* x, const float* norm_w, float eps, int T,
+                  void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
+    if (st) return st;
+    if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
+    if (!x) return QMOE_ERR_ARG;
+    if (!aligned16(x) || (norm_w && !aligned16(norm_w))) return QMOE_ERR_ALIGN;
+    if (norm_w && !(eps > 0.0f)) return QMOE_ERR_ARG;
+    if (ws_layout(*D, T).total > ws_bytes) return QMOE_ERR_WORKSPACE;
+    DecodeParams P = make_params(B, D, x, nullptr, nullptr, T, ws);
+    if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    if (norm_w) {
+        P.prenorm = 1;
+        P.norm_w = norm_w;
+        P.eps = eps;
+    }
+    return cuda_status(launch_ep_route(P, prefill_bufs(*D, T, ws), reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* eid, int n, void* y,
+                    void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    int st;
+    if (!B || (st = check_dims(D))) return B ? st : QMOE_ERR_ARG;
+    if (n < 0) return QMOE_ERR_ARG;
+    if (n == 0) return QMOE_OK;
+    if (!x16 || !eid || !y || !ws) return QMOE_ERR_ARG;
+    if (!aligned16(x16) || !aligned16(y) || !aligned16(ws)) return QMOE_ERR_ALIGN;
+    const uint64_t d = D->d_model, E = D->num_experts, F = D->expert_dim;
+    if ((st = check_tensor(B->gate_exps, E * F * d, expert_type))) return st;
+    if ((st = check_tensor(B->up_exps, E * F * d, expert_type))) return st;
+    if ((st = check_tensor(B->down_exps, E * d * F, expert_type))) return st;
+    if (B->up_exps.ggml_type != B->gate_exps.ggml_type) return QMOE_ERR_TYPE;
+    const qmoe_dims RD = ep_row_dims(*D);
+    const int Tp = std::max(n, kDecodeMaxT + 1);
+    if (ws_layout(RD, Tp).total > ws_bytes) return QMOE_ERR_WORKSPACE;
+    qmoe_block lb = *B;  // the router and shared tensors are not read
+    lb.router = lb.shared_gate_inp = B->gate_exps;
+    lb.shared_gate = lb.shared_up = B->gate_exps;
+    lb.shared_down = B->down_exps;
+    DecodeParams P = make_params(&lb, &RD, nullptr, nullptr, nullptr, Tp, ws);
+    P.T = n;
+    P.has_shared = 0;
+    if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    return cuda_status(launch_ep_experts(P, prefill_bufs(RD, Tp, ws), static_cast<const __half*>(x16), eid,
+                                         static_cast<__half*>(y), reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, int T, const float* residual,
+                    float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
+    if (st) return st;
+    if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
+    if (!y_pairs || !out) return QMOE_ERR_ARG;
+    if (!aligned16(y_pairs)) return QMOE_ERR_ALIGN;
+    if (ws_layout(*D, T).total > ws_bytes) return QMOE_ERR_WORKSPACE;
+    DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
+    if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    return cuda_status(launch_ep_combine(P, prefill_bufs(*D, T, ws), static_cast<const __half*>(y_pairs),
+                                         reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int qmoe_block_kernel_count(const qmoe_block* B, const qmoe_dims* D, int T) {
     int st;
     if (T <= 0) return -QMOE_ERR_ARG;
@@ -333,20 +428,7 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
             P.eps = eps;
         }
         if (prefill_supported(P)) {
-            const WsLayout L = ws_layout(*D, T);
-            uint8_t* w = static_cast<uint8_t*>(ws);
-            PrefillBufs pb;
-            pb.tok_of_pos = reinterpret_cast<int32_t*>(w + L.tok_of_pos);
-            pb.tile_start = reinterpret_cast<int32_t*>(w + L.tile_start);
-            pb.sh_grp = reinterpret_cast<int32_t*>(w + L.sh_grp);
-            pb.sh_tiles = pb.sh_grp + 2;
-            pb.disp = reinterpret_cast<int32_t*>(w + L.disp);
-            pb.X16 = reinterpret_cast<__half*>(w + L.X16);
-            pb.H = reinterpret_cast<__half*>(w + L.Hpf);
-            pb.Hs = reinterpret_cast<__half*>(w + L.Hs);
-            pb.Y = reinterpret_cast<__half*>(w + L.Y);
-            pb.Ys = reinterpret_cast<__half*>(w + L.Ys);
-            return cuda_status(launch_prefill(P, pb, s));
+            return cuda_status(launch_prefill(P, prefill_bufs(*D, T, ws), s));
         }
     }
     for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {

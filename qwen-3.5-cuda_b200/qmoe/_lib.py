@@ -24,7 +24,7 @@ QMOE_ERR_ROUTING = 10
 QMOE_ERR_NOT_NORMALIZED = 11
 QMOE_ERR_TIMEOUT = 12
 
-WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR, WS_INPUT = range(9)
+WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR, WS_INPUT, WS_INPUT16 = range(10)
 
 
 class QmoeTensor(ctypes.Structure):
@@ -62,6 +62,13 @@ SIGNATURES = [
                                   c_size_t, c_void_p]),
     ("qmoe_expert_block", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int, c_void_p, c_void_p, c_void_p,
                                   c_size_t, c_void_p]),
+    ("qmoe_ep_rows_workspace_size", c_size_t, [POINTER(QmoeDims), c_int]),
+    ("qmoe_ep_route", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_float, c_int, c_void_p,
+                              c_size_t, c_void_p]),
+    ("qmoe_ep_experts", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                c_size_t, c_void_p]),
+    ("qmoe_ep_combine", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                c_size_t, c_void_p]),
     ("qmoe_block_kernel_count", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int]),
     ("qmoe_block_forward", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_void_p, c_int,
                                    c_void_p, c_size_t, c_void_p]),

@@ -1,0 +1,167 @@
+"""Expert parallelism on the GPU: the qmoe_ep_* entry points against the
+1-GPU qmoe_block_forward on the same bytes -- routing bit-identical, outputs
+bit-identical too (each row's grouped-GEMM result and the combine order do
+not depend on where the row ran), checked here within the north-star
+tolerance and for exact equality.
+
+test_ep_shards_on_one_gpu runs every shard of a G-way split on one GPU (no
+exchange; the rows a rank would receive are gathered locally);
+test_ep_nccl runs ExpertParallelMoE with one process per GPU over NCCL and
+needs at least two GPUs."""
+from __future__ import annotations
+
+import ctypes
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from qmoe import _lib, ep, synth
+
+from gpu_util import assert_close
+
+pytestmark = pytest.mark.gpu
+
+SEED = 4242
+
+
+def _reference(blk, x, residual):
+    """1-GPU prefill block: out and the top-k ids of every token."""
+    import torch
+    T = x.shape[0]
+    dc = blk.dims.c()
+    n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
+    ws = torch.empty(n, dtype=torch.uint8, device=x.device)
+    _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
+    out = torch.empty_like(x)
+    c = blk.c()
+    _lib.check(_lib.lib().qmoe_block_forward(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(), out.data_ptr(),
+                                             residual.data_ptr(), T, ws.data_ptr(), n, None), "block_forward")
+    p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_TOPK_IDX)
+    off = p - ws.data_ptr()
+    k = blk.dims.top_k
+    idx = ws[off:off + T * k * 4].view(torch.int32).view(T, k).clone()
+    torch.cuda.synchronize()
+    return out, idx
+
+
+@pytest.mark.parametrize("G,types,bias", [(2, synth.Q4K_TYPES, False), (8, synth.MIXED_TYPES, True)])
+def test_ep_shards_on_one_gpu(cuda, G, types, bias):
+    import torch
+    dims = synth.Dims()
+    T = 300
+    blk = synth.Block(dims, types, seed=SEED, bias=bias)
+    x = synth.inputs(T, dims.d_model, seed=17, tag=3)
+    residual = synth.inputs(T, dims.d_model, seed=18, tag=4)
+    want, want_idx = _reference(blk, x, residual)
+
+    full, dc = blk.c(), dims.c()
+    L = _lib.lib()
+    be = ep.CudaBackend(full, full, dc, dc, max_tokens=T, max_rows=T * dims.top_k)
+    idx, rows = be.route(x)
+    assert torch.equal(idx, want_idx)
+    pairs, dest_eid, counts = ep.plan_sends(idx, dims.num_experts, G)
+    y_pairs = torch.zeros((T * dims.top_k, dims.d_model), dtype=torch.float16, device="cuda")
+    start = 0
+    for r in range(G):
+        n = int(counts[r])
+        lb, ld = ep.local_block(full, dc, r, G)
+        p = pairs[start:start + n]
+        rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), max(n, 1))
+        rws = torch.empty(rws_bytes, dtype=torch.uint8, device="cuda")
+        r_rows = rows.index_select(0, p // dims.top_k).contiguous()
+        r_eid = dest_eid[start:start + n].contiguous()
+        y = torch.empty_like(r_rows)
+        _lib.check(L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), r_rows.data_ptr(), r_eid.data_ptr(), n,
+                                     y.data_ptr(), rws.data_ptr(), rws_bytes, None), "ep_experts")
+        y_pairs.index_copy_(0, p, y)
+        start += n
+    assert start == T * dims.top_k
+    got = be.combine(y_pairs, residual)
+    torch.cuda.synchronize()
+    assert_close(got.cpu().numpy(), want.cpu().numpy(), f"ep G={G}")
+    assert torch.equal(got, want)
+
+
+def test_ep_argument_checks(cuda):
+    import torch
+    dims = synth.Dims(512, 32, 4, 256, 256)
+    blk = synth.Block(dims, synth.Q4K_TYPES, seed=3)
+    full, dc = blk.c(), dims.c()
+    L = _lib.lib()
+    lb, ld = ep.local_block(full, dc, 1, 4)
+    assert ld.num_experts == 8
+    rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), 16)
+    rws = torch.empty(rws_bytes, dtype=torch.uint8, device="cuda")
+    rows = torch.zeros((16, 512), dtype=torch.float16, device="cuda")
+    eid = torch.zeros(16, dtype=torch.int32, device="cuda")
+    y = torch.empty_like(rows)
+    # zero rows is a no-op, too small a workspace is refused, decode-sized routing is refused
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), None, None, 0, None, None, 0, None) == _lib.QMOE_OK
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), eid.data_ptr(), 16, y.data_ptr(),
+                             rws.data_ptr(), 1024, None) == _lib.QMOE_ERR_WORKSPACE
+    ws_bytes = L.qmoe_workspace_size(ctypes.byref(dc), 64)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    x = torch.zeros((8, 512), dtype=torch.float32, device="cuda")
+    assert L.qmoe_ep_route(ctypes.byref(full), ctypes.byref(dc), x.data_ptr(), None, 1e-6, 8, ws.data_ptr(),
+                           ws_bytes, None) == _lib.QMOE_ERR_UNSUPPORTED
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, t_local, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dims = synth.Dims()
+        blk = synth.Block(dims, synth.Q4K_TYPES, seed=SEED)          # the same bytes on every rank
+        T = t_local * world
+        x_all = synth.inputs(T, dims.d_model, seed=23, tag=5)
+        r_all = synth.inputs(T, dims.d_model, seed=24, tag=6)
+        want, want_idx = _reference(blk, x_all, r_all)
+        sl = slice(rank * t_local, (rank + 1) * t_local)
+        x, res = x_all[sl].contiguous(), r_all[sl].contiguous()
+        full, dc = blk.c(), dims.c()
+        lb, ld = ep.local_block(full, dc, rank, world)
+        be = ep.CudaBackend(full, lb, dc, ld, max_tokens=t_local, max_rows=t_local * dims.top_k)
+        moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model)
+        got = moe.forward(x, res)
+        idx = be._view(_lib.WS_TOPK_IDX, t_local * dims.top_k, torch.int32).view(t_local, dims.top_k)
+        torch.cuda.synchronize()
+        ids_equal = bool(torch.equal(idx, want_idx[sl]))
+        max_err = float((got - want[sl]).abs().max())
+        q.put((rank, ids_equal, max_err, bool(torch.equal(got, want[sl]))))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_nccl(cuda):
+    import torch
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_nccl_worker, args=(r, world, port, 160, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+    for rank, ids_equal, max_err, exact in sorted(q.get() for _ in range(world)):
+        assert ids_equal, rank
+        assert max_err <= 1e-3, (rank, max_err)
+        assert exact, (rank, max_err)
