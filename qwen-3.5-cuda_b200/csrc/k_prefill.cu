@@ -604,9 +604,16 @@ __global__ void __launch_bounds__(256) k_route_many(const uint8_t* __restrict__ 
 __global__ void __launch_bounds__(256) k_topk_many(const float* __restrict__ logits, int T, int E, int k,
                                                    int32_t* __restrict__ idx, float* __restrict__ wts,
                                                    int32_t* __restrict__ out_idx, float* __restrict__ out_w,
-                                                   uint32_t* ctrl) {
+                                                   int32_t* __restrict__ sh_grp, uint32_t* ctrl) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t == 0 && lane == 0) {
+        // the shared expert's one-group GEMM plan: all T tokens, ceil(T / 128) tiles
+        sh_grp[0] = 0;
+        sh_grp[1] = T;
+        sh_grp[2] = 0;
+        sh_grp[3] = (T + pf::BM - 1) / pf::BM;
+    }
     if (t >= T) return;
     int my_idx;
     float wj;
@@ -714,9 +721,8 @@ __global__ void __launch_bounds__(256) k_pf_place(const int32_t* __restrict__ id
 // (routed experts) plus the shared expert's single group [0, T).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_pf_plan(const int32_t* __restrict__ offsets, const int32_t* __restrict__ perm,
-                                                 int E, int k, int T, int32_t* __restrict__ tok_of_pos,
-                                                 int32_t* __restrict__ tile_start, int32_t* __restrict__ sh_grp,
-                                                 int32_t* __restrict__ sh_tiles) {
+                                                 int E, int k, int32_t* __restrict__ tok_of_pos,
+                                                 int32_t* __restrict__ tile_start) {
     const int npairs = __ldg(offsets + E);
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npairs; i += gridDim.x * blockDim.x)
         tok_of_pos[i] = __ldg(perm + i) / k;
@@ -737,13 +743,7 @@ __global__ void __launch_bounds__(256) k_pf_plan(const int32_t* __restrict__ off
             if (e < E) tile_start[e] = run + inc - v;
             run += __shfl_sync(0xffffffffu, inc, 31);
         }
-        if (lane == 0) {
-            tile_start[E] = run;
-            sh_grp[0] = 0;
-            sh_grp[1] = T;
-            sh_tiles[0] = 0;
-            sh_tiles[1] = (T + pf::BM - 1) / pf::BM;
-        }
+        if (lane == 0) tile_start[E] = run;
     }
 }
 
@@ -893,7 +893,8 @@ cudaError_t pf_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s
 #undef QMOE_RM
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    k_topk_many<<<(T + 7) / 8, 256, 0, s>>>(P.logits, T, E, k, P.topk_idx, P.topk_w, P.out_idx, P.out_w, P.ctrl);
+    k_topk_many<<<(T + 7) / 8, 256, 0, s>>>(P.logits, T, E, k, P.topk_idx, P.topk_w, P.out_idx, P.out_w, B.sh_grp,
+                                            P.ctrl);
     return cudaGetLastError();
 }
 
@@ -905,7 +906,7 @@ static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t*
     k_pf_count<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp);
     k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, offsets);
     k_pf_place<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp, perm, inv_perm);
-    k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, T, B.tok_of_pos, B.tile_start, B.sh_grp, B.sh_tiles);
+    k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, B.tok_of_pos, B.tile_start);
     return cudaGetLastError();
 }
 

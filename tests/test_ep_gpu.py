@@ -27,6 +27,15 @@ pytestmark = pytest.mark.gpu
 SEED = 4242
 
 
+def _poison(be):
+    """Fill a backend's workspaces with a non-zero pattern (then re-initialise
+    the control words) so that nothing can pass by reading memory left behind
+    by an earlier call."""
+    be.ws.fill_(0xA5)
+    be.rws.fill_(0xA5)
+    _lib.check(_lib.lib().qmoe_workspace_init(be.ws.data_ptr(), be.ws_bytes, None))
+
+
 def _reference(blk, x, residual):
     """1-GPU prefill block: out and the top-k ids of every token."""
     import torch
@@ -60,6 +69,7 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias):
     full, dc = blk.c(), dims.c()
     L = _lib.lib()
     be = ep.CudaBackend(full, full, dc, dc, max_tokens=T, max_rows=T * dims.top_k)
+    _poison(be)
     idx, rows = be.route(x)
     assert torch.equal(idx, want_idx)
     pairs, dest_eid, counts = ep.plan_sends(idx, dims.num_experts, G)
@@ -70,7 +80,7 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias):
         lb, ld = ep.local_block(full, dc, r, G)
         p = pairs[start:start + n]
         rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), max(n, 1))
-        rws = torch.empty(rws_bytes, dtype=torch.uint8, device="cuda")
+        rws = torch.full((rws_bytes,), 0xA5, dtype=torch.uint8, device="cuda")
         r_rows = rows.index_select(0, p // dims.top_k).contiguous()
         r_eid = dest_eid[start:start + n].contiguous()
         y = torch.empty_like(r_rows)
@@ -134,6 +144,7 @@ def _nccl_worker(rank, world, port, t_local, q):
         full, dc = blk.c(), dims.c()
         lb, ld = ep.local_block(full, dc, rank, world)
         be = ep.CudaBackend(full, lb, dc, ld, max_tokens=t_local, max_rows=t_local * dims.top_k)
+        _poison(be)
         moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model)
         got = moe.forward(x, res)
         idx = be._view(_lib.WS_TOPK_IDX, t_local * dims.top_k, torch.int32).view(t_local, dims.top_k)
