@@ -184,31 +184,48 @@ QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int
                       float* out, const float* residual,
                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 
-/* Expert parallelism for prefill (experts sharded across GPUs; the caller
- * moves rows between ranks, e.g. with NCCL all-to-all).  No counterpart in
- * the reference, which runs on one GPU.  For T > 8 local tokens:
- *   qmoe_ep_route    x_in (optional pre-MoE RMSNorm), its fp16 copy
- *                    (QMOE_WS_INPUT16) and the top-k of every local token
- *                    (QMOE_WS_TOPK_IDX / QMOE_WS_TOPK_W), in `workspace`
- *   qmoe_ep_experts  this rank's experts on n received rows: rows [n][d] in
- *                    the QMOE_WS_INPUT16 format, expert_ids [n] local to the
- *                    rank (0 .. local_dims->num_experts-1), y_rows [n][d] fp16
- *                    = down(silu(gate x) * up x) of each row's expert
- *   qmoe_ep_combine  shared expert and combine of the T local tokens from
- *                    y_pairs [T*k][d] fp16 in pair order (p = t*k + j):
- *                    out[t] = residual[t] + sum_j w[t][j] y_pairs[t*k+j]
- *                             + sigmoid(shared gate) * shared(x_in[t])
- * local_blk holds the rank's slices of the expert tensors (router and shared
- * tensors are not read); its workspace comes from qmoe_ep_rows_workspace_size. */
-QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max_rows);
+/* Expert parallelism for prefill (experts sharded contiguously over G ranks,
+ * E/G per rank; the caller moves buffers between ranks, e.g. with NCCL
+ * all-to-all).  No counterpart in the reference, which runs on one GPU.
+ * Per rank, for T > 8 local tokens:
+ *   qmoe_ep_route     x_in (optional pre-MoE RMSNorm), its fp16 copy
+ *                     (QMOE_WS_INPUT16) and the top-k of every local token
+ *                     (QMOE_WS_TOPK_IDX / QMOE_WS_TOPK_W), in `workspace`
+ *   qmoe_ep_dispatch  send buffers from that routing: one fp16 row per
+ *                     (token, rank) pair that has at least one expert on the
+ *                     rank -- grouped by rank, token order inside a rank --
+ *                     with a meta row of k ints (slot j: the expert's id local
+ *                     to that rank, or -1); counts[r] = rows to rank r,
+ *                     counts[G + r] = (token, slot) pairs to rank r; and
+ *                     pair_pos[t*k + j] = the position of pair (t, j) in the
+ *                     returned outputs (grouped by rank; inside a rank in
+ *                     (row, slot) order), -1 for a failed token
+ *   qmoe_ep_experts   this rank's experts on n received rows and meta rows
+ *                     (any concatenation of the ranks' chunks): y_pairs
+ *                     [pairs][d] fp16 = down(silu(gate x) * up x) for every
+ *                     valid slot, in (row, slot) order -- the order that
+ *                     pair_pos on the sending rank refers to
+ *   qmoe_ep_combine   shared expert and combine of the T local tokens:
+ *                     out[t] = residual[t] + sum_j w[t][j] y[pair_pos[t*k+j]]
+ *                              + sigmoid(shared gate) * shared(x_in[t])
+ * send_rows holds at most T * min(G, k) rows (send_meta the same number of
+ * k-int rows); `scratch` comes from qmoe_ep_dispatch_scratch_size.  local_blk
+ * holds the rank's slices of the expert tensors (router and shared tensors are
+ * not read), local_dims its expert count (top_k = the layer's k); the
+ * workspace of qmoe_ep_experts comes from qmoe_ep_rows_workspace_size. */
 QMOE_API int qmoe_ep_route(const qmoe_block* blk, const qmoe_dims* dims, const float* x, const float* norm_weight,
                    float eps, int T, void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+QMOE_API size_t qmoe_ep_dispatch_scratch_size(int T, int G);
+QMOE_API int qmoe_ep_dispatch(const qmoe_dims* dims, int T, int G, void* workspace, size_t workspace_bytes,
+                      void* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos, void* scratch,
+                      size_t scratch_bytes, qmoe_stream_t stream);
+QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max_rows);
 QMOE_API int qmoe_ep_experts(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
-                     const int32_t* expert_ids, int n_rows, void* y_rows, void* workspace,
-                     size_t workspace_bytes, qmoe_stream_t stream);
-QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs, int T,
-                     const float* residual, float* out, void* workspace, size_t workspace_bytes,
+                     const int32_t* meta, int n_rows, void* y_pairs, void* workspace, size_t workspace_bytes,
                      qmoe_stream_t stream);
+QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs,
+                     const int32_t* pair_pos, int T, const float* residual, float* out, void* workspace,
+                     size_t workspace_bytes, qmoe_stream_t stream);
 
 /* Number of kernels one qmoe_block_forward call with these arguments launches
  * (for profiling and launch accounting); negative status on bad arguments. */

@@ -722,10 +722,14 @@ __global__ void __launch_bounds__(256) k_pf_place(const int32_t* __restrict__ id
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_pf_plan(const int32_t* __restrict__ offsets, const int32_t* __restrict__ perm,
                                                  int E, int k, int32_t* __restrict__ tok_of_pos,
-                                                 int32_t* __restrict__ tile_start) {
+                                                 int32_t* __restrict__ tile_start, const int32_t* __restrict__ qmap,
+                                                 int32_t* __restrict__ out_pos) {
     const int npairs = __ldg(offsets + E);
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npairs; i += gridDim.x * blockDim.x)
-        tok_of_pos[i] = __ldg(perm + i) / k;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < npairs; i += gridDim.x * blockDim.x) {
+        const int p = __ldg(perm + i);
+        tok_of_pos[i] = p / k;
+        if (qmap) out_pos[i] = __ldg(qmap + p);  // output row of the pair (expert-parallel path)
+    }
     if (blockIdx.x == 0 && threadIdx.x < 32) {
         // warp 0: exclusive scan of ceil(count / 128) over the experts
         const int lane = threadIdx.x;
@@ -901,12 +905,13 @@ cudaError_t pf_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s
 // Permutation of the (row, slot) pairs of `idx` [T][k] by expert, and the
 // GEMM tile plan.
 static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t* offsets, int32_t* perm,
-                               int32_t* inv_perm, const PrefillBufs& B, cudaStream_t s) {
+                               int32_t* inv_perm, const PrefillBufs& B, cudaStream_t s,
+                               const int32_t* qmap = nullptr, int32_t* out_pos = nullptr) {
     const int nb = (T + DB - 1) / DB;
     k_pf_count<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp);
     k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, offsets);
     k_pf_place<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp, perm, inv_perm);
-    k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, B.tok_of_pos, B.tile_start);
+    k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, B.tok_of_pos, B.tile_start, qmap, out_pos);
     return cudaGetLastError();
 }
 
@@ -1003,20 +1008,24 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
 // Expert-parallel pieces.  Route: x_in, X16 and top-k of T local tokens.
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) { return pf_route(P, B, s); }
 
-// This rank's experts on n received rows: rows x16 [n][d] (chunk order),
-// local expert ids eid [n]; outputs y [n][d] fp16 in row order.  P is set
-// up for T = n rows, k = 1, E = local experts.
-cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* eid,
-                              __half* y, cudaStream_t s) {
+// This rank's experts on n received rows: rows x16 [n][d] (chunk order) and
+// meta [n][k] (local expert id per slot or -1; P.k = k, P.E = local experts);
+// qmap [n*k] numbers the valid slots in (row, slot) order, out_pos receives
+// that number for every expert-sorted pair; outputs y [pairs][d] fp16 in that
+// order.
+cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
+                              const int32_t* qmap, int32_t* out_pos, __half* y, cudaStream_t s) {
     cudaError_t e;
-    if ((e = pf_dispatch(eid, P.T, 1, P.E, P.offsets, P.perm, P.inv_perm, B, s)) != cudaSuccess) return e;
-    return pf_routed(P, B, x16, y, B.tok_of_pos, s);
+    if ((e = pf_dispatch(meta, P.T, P.k, P.E, P.offsets, P.perm, P.inv_perm, B, s, qmap, out_pos)) != cudaSuccess)
+        return e;
+    return pf_routed(P, B, x16, y, out_pos, s);
 }
 
-// Shared expert and combine of T local tokens, y_pairs [T*k][d] fp16 in
-// pair order (zero rows for pairs of failed tokens).
-cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs, cudaStream_t s) {
-    return pf_shared_combine(P, B, y_pairs, nullptr, s);
+// Shared expert and combine of T local tokens; the routed outputs of pair
+// (t, j) are row pair_pos[t*k + j] of y_pairs (-1: none).
+cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
+                              const int32_t* pair_pos, cudaStream_t s) {
+    return pf_shared_combine(P, B, y_pairs, pair_pos, s);
 }
 
 }  // namespace qmoe

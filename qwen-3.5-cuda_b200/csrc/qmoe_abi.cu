@@ -15,9 +15,16 @@ bool fused_supported(const DecodeParams& P);
 bool prefill_supported(const DecodeParams& P);
 cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
-cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* eid,
-                              __half* y, cudaStream_t s);
-cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs, cudaStream_t s);
+cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
+                              const int32_t* qmap, int32_t* out_pos, __half* y, cudaStream_t s);
+cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
+                              const int32_t* pair_pos, cudaStream_t s);
+size_t ep_dispatch_scratch_bytes(int T, int G);
+bool ep_dispatch_supported(int k, int G);
+cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, const __half* x16, int d,
+                               __half* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos,
+                               void* scratch, cudaStream_t s);
+cudaError_t launch_ep_qmap(const int32_t* meta, int n, int k, int32_t* qblk, int32_t* qmap, cudaStream_t s);
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
 int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
@@ -326,17 +333,6 @@ int qmoe_expert_block(const qmoe_block* B, const qmoe_dims* D, int T, float* out
 }
 
 // ---- expert parallelism ----
-static qmoe_dims ep_row_dims(const qmoe_dims& D) {
-    qmoe_dims r = D;
-    r.top_k = 1;  // one (row, expert) pair per received row
-    return r;
-}
-
-size_t qmoe_ep_rows_workspace_size(const qmoe_dims* D, int max_rows) {
-    if (check_dims(D) || max_rows <= 0) return 0;
-    return ws_layout(ep_row_dims(*D), std::max(max_rows, kDecodeMaxT + 1)).total;
-}
-
 int qmoe_ep_route(const qmoe_block* B, const qmoe_dims* D, const float* x, const float* norm_w, float eps, int T,
                   void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
@@ -356,45 +352,90 @@ int qmoe_ep_route(const qmoe_block* B, const qmoe_dims* D, const float* x, const
     return cuda_status(launch_ep_route(P, prefill_bufs(*D, T, ws), reinterpret_cast<cudaStream_t>(stream)));
 }
 
-int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* eid, int n, void* y,
+size_t qmoe_ep_dispatch_scratch_size(int T, int G) {
+    if (T <= 0 || G <= 0 || G > 32) return 0;
+    return ep_dispatch_scratch_bytes(T, G);
+}
+
+int qmoe_ep_dispatch(const qmoe_dims* D, int T, int G, void* ws, size_t ws_bytes, void* send_rows,
+                     int32_t* send_meta, int32_t* counts, int32_t* pair_pos, void* scratch, size_t scratch_bytes,
+                     qmoe_stream_t stream) {
+    int st;
+    if ((st = check_dims(D))) return st;
+    if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
+    if (G <= 0 || D->num_experts % G) return QMOE_ERR_ARG;
+    if (!ep_dispatch_supported(D->top_k, G)) return QMOE_ERR_UNSUPPORTED;
+    if (!ws || !send_rows || !send_meta || !counts || !pair_pos || !scratch) return QMOE_ERR_ARG;
+    if (!aligned16(ws) || !aligned16(send_rows)) return QMOE_ERR_ALIGN;
+    if (ws_layout(*D, T).total > ws_bytes || ep_dispatch_scratch_bytes(T, G) > scratch_bytes)
+        return QMOE_ERR_WORKSPACE;
+    const WsLayout L = ws_layout(*D, T);
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    return cuda_status(launch_ep_dispatch(reinterpret_cast<const int32_t*>(w + L.topk_idx), T, D->top_k,
+                                          D->num_experts, G, reinterpret_cast<const __half*>(w + L.X16), D->d_model,
+                                          static_cast<__half*>(send_rows), send_meta, counts, pair_pos, scratch,
+                                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
+size_t qmoe_ep_rows_workspace_size(const qmoe_dims* D, int max_rows) {
+    if (check_dims(D) || max_rows <= 0) return 0;
+    return ep_rows_layout(*D, max_rows).total;
+}
+
+int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n, void* y,
                     void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     int st;
     if (!B || (st = check_dims(D))) return B ? st : QMOE_ERR_ARG;
     if (n < 0) return QMOE_ERR_ARG;
     if (n == 0) return QMOE_OK;
-    if (!x16 || !eid || !y || !ws) return QMOE_ERR_ARG;
+    if (!x16 || !meta || !y || !ws) return QMOE_ERR_ARG;
     if (!aligned16(x16) || !aligned16(y) || !aligned16(ws)) return QMOE_ERR_ALIGN;
+    if (D->top_k > 8) return QMOE_ERR_UNSUPPORTED;
     const uint64_t d = D->d_model, E = D->num_experts, F = D->expert_dim;
     if ((st = check_tensor(B->gate_exps, E * F * d, expert_type))) return st;
     if ((st = check_tensor(B->up_exps, E * F * d, expert_type))) return st;
     if ((st = check_tensor(B->down_exps, E * d * F, expert_type))) return st;
     if (B->up_exps.ggml_type != B->gate_exps.ggml_type) return QMOE_ERR_TYPE;
-    const qmoe_dims RD = ep_row_dims(*D);
-    const int Tp = std::max(n, kDecodeMaxT + 1);
-    if (ws_layout(RD, Tp).total > ws_bytes) return QMOE_ERR_WORKSPACE;
+    const EpRowsLayout L = ep_rows_layout(*D, n);
+    if (L.total > ws_bytes) return QMOE_ERR_WORKSPACE;
     qmoe_block lb = *B;  // the router and shared tensors are not read
     lb.router = lb.shared_gate_inp = B->gate_exps;
     lb.shared_gate = lb.shared_up = B->gate_exps;
     lb.shared_down = B->down_exps;
-    DecodeParams P = make_params(&lb, &RD, nullptr, nullptr, nullptr, Tp, ws);
+    DecodeParams P = make_params(&lb, D, nullptr, nullptr, nullptr, kDecodeMaxT, ws);
+    uint8_t* w = static_cast<uint8_t*>(ws);
     P.T = n;
     P.has_shared = 0;
+    P.ctrl = reinterpret_cast<uint32_t*>(w + L.ctrl);
+    P.offsets = reinterpret_cast<int32_t*>(w + L.offsets);
+    P.perm = reinterpret_cast<int32_t*>(w + L.perm);
+    P.inv_perm = reinterpret_cast<int32_t*>(w + L.inv_perm);
     if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
-    return cuda_status(launch_ep_experts(P, prefill_bufs(RD, Tp, ws), static_cast<const __half*>(x16), eid,
-                                         static_cast<__half*>(y), reinterpret_cast<cudaStream_t>(stream)));
+    PrefillBufs pb{};
+    pb.tok_of_pos = reinterpret_cast<int32_t*>(w + L.tok_of_pos);
+    pb.tile_start = reinterpret_cast<int32_t*>(w + L.tile_start);
+    pb.disp = reinterpret_cast<int32_t*>(w + L.disp);
+    pb.H = reinterpret_cast<__half*>(w + L.H);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int32_t* qmap = reinterpret_cast<int32_t*>(w + L.qmap);
+    cudaError_t e = launch_ep_qmap(meta, n, D->top_k, reinterpret_cast<int32_t*>(w + L.qblk), qmap, s);
+    if (e == cudaSuccess)
+        e = launch_ep_experts(P, pb, static_cast<const __half*>(x16), meta, qmap,
+                              reinterpret_cast<int32_t*>(w + L.out_pos), static_cast<__half*>(y), s);
+    return cuda_status(e);
 }
 
-int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, int T, const float* residual,
-                    float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos, int T,
+                    const float* residual, float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
     if (st) return st;
     if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
-    if (!y_pairs || !out) return QMOE_ERR_ARG;
+    if (!y_pairs || !pair_pos || !out) return QMOE_ERR_ARG;
     if (!aligned16(y_pairs)) return QMOE_ERR_ALIGN;
     if (ws_layout(*D, T).total > ws_bytes) return QMOE_ERR_WORKSPACE;
     DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
     if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
-    return cuda_status(launch_ep_combine(P, prefill_bufs(*D, T, ws), static_cast<const __half*>(y_pairs),
+    return cuda_status(launch_ep_combine(P, prefill_bufs(*D, T, ws), static_cast<const __half*>(y_pairs), pair_pos,
                                          reinterpret_cast<cudaStream_t>(stream)));
 }
 

@@ -110,6 +110,32 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
     return L;
 }
 
+// Workspace of qmoe_ep_experts for up to n received rows of k slots (the
+// expert-parallel receiver): dispatch of the (row, slot) pairs over the local
+// experts, the GEMM tile plan and the hidden vectors of the pairs.
+struct EpRowsLayout {
+    size_t ctrl, offsets, perm, inv_perm, tok_of_pos, out_pos, qmap, qblk, tile_start, disp, H, total;
+};
+inline EpRowsLayout ep_rows_layout(const qmoe_dims& D, int n) {
+    EpRowsLayout L{};
+    const size_t P = static_cast<size_t>(n) * D.top_k, E = D.num_experts;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 256); return r; };
+    L.ctrl = take(64 * 4);
+    L.offsets = take(sizeof(int32_t) * (E + 1));
+    L.perm = take(sizeof(int32_t) * P);
+    L.inv_perm = take(sizeof(int32_t) * P);
+    L.tok_of_pos = take(sizeof(int32_t) * P);
+    L.out_pos = take(sizeof(int32_t) * P);
+    L.qmap = take(sizeof(int32_t) * P);
+    L.qblk = take(sizeof(int32_t) * ((static_cast<size_t>(n) + 255) / 256 + 1));
+    L.tile_start = take(sizeof(int32_t) * (E + 1));
+    L.disp = take(sizeof(int32_t) * E * ((static_cast<size_t>(n) + 63) / 64));
+    L.H = take(2 * P * static_cast<size_t>(D.expert_dim));
+    L.total = o;
+    return L;
+}
+
 // Prefill buffers of a workspace (fp16 data as raw 16-bit words).
 struct PrefillBufs {
     int32_t* tok_of_pos;

@@ -1,21 +1,26 @@
 """Expert-parallel MoE block for prefill: the E experts
 are sharded contiguously across the G ranks of a process group (E/G per
-rank, one GPU per rank), tokens are split across ranks, and the (token,
-expert) pairs travel to the rank that owns the expert and back.
+rank, one GPU per rank), tokens are split across ranks, and each token's row
+travels once to every rank that owns one of its experts; the expert outputs
+of its (token, slot) pairs travel back.
 
 Per rank and call (T local tokens):
-  1. route    x_in, its fp16 copy and the top-k of every local token
-              (qmoe_ep_route: bit-identical routing to the 1-GPU path, since
-              the router and top-k are per-token functions)
-  2. send     pairs grouped by destination rank (stable: pair order within a
-              rank), one fp16 row of x_in per pair plus the expert id local to
-              the destination; counts, rows and ids with all-to-all
-  3. experts  the rank's experts on the received rows (qmoe_ep_experts,
-              tcgen05 grouped GEMMs)
-  4. return   outputs back with the reverse all-to-all, placed at their pair
-              index t*k + j
-  5. combine  shared expert and the slot-ordered combine of the local tokens
-              (qmoe_ep_combine)
+  1. route     x_in, its fp16 copy and the top-k of every local token
+               (qmoe_ep_route: the same kernels as the 1-GPU path, so the
+               routing is bit-identical to it -- router and top-k are
+               per-token functions)
+  2. dispatch  send buffers on the device (qmoe_ep_dispatch): one fp16 row
+               per (token, rank) with a meta row of local expert ids per slot,
+               grouped by rank; rows and pairs per rank; pair_pos, the place
+               of every (token, slot) output in the returned buffer
+  3. exchange  the per-rank counts (all-to-all, then the one host
+               synchronisation of the call: NCCL needs the split sizes), then
+               rows and meta rows (all-to-all with those splits)
+  4. experts   the rank's experts on the received rows (qmoe_ep_experts,
+               tcgen05 grouped GEMMs), outputs in (row, slot) order
+  5. return    outputs back with the reverse all-to-all
+  6. combine   shared expert and the slot-ordered combine of the local tokens
+               through pair_pos (qmoe_ep_combine)
 The exchange runs on torch.distributed (NCCL on GPUs, gloo in the CPU
 tests); the compute goes through a backend object, `CudaBackend` in
 production, so the exchange logic can be tested without a GPU.
@@ -35,28 +40,6 @@ def shard_bounds(E: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
-def plan_sends(idx, E: int, world: int):
-    """Pairs of a [T, k] top-k result grouped by destination rank.
-
-    Returns (pairs, dest_eid, counts): pair ids p = t*k + j in (destination,
-    p) order for the valid pairs (expert >= 0), the expert id local to each
-    pair's destination, and the number of pairs per destination."""
-    import torch
-    T, k = idx.shape
-    n_loc = E // world
-    flat = idx.reshape(-1).to(torch.int64)
-    valid = flat >= 0
-    dest = torch.where(valid, flat // n_loc, torch.full_like(flat, world))
-    # stable sort by destination keeps the pair order inside each destination
-    key = dest * (T * k) + torch.arange(T * k, device=idx.device)
-    order = torch.argsort(key)
-    n_valid = int(valid.sum())
-    pairs = order[:n_valid]
-    dest_eid = (flat[pairs] - dest[pairs] * n_loc).to(torch.int32)
-    counts = torch.bincount(dest[pairs], minlength=world)[:world]
-    return pairs, dest_eid, counts
-
-
 class ExpertParallelMoE:
     """One MoE layer sharded over the ranks of `group` (torch.distributed)."""
 
@@ -73,43 +56,58 @@ class ExpertParallelMoE:
     def _a2a(self, send, send_counts, recv_counts):
         import torch
         recv = torch.empty((int(sum(recv_counts)),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-        self.dist.all_to_all_single(recv, send.contiguous(), [int(c) for c in recv_counts],
-                                    [int(c) for c in send_counts], group=self.group)
+        self.dist.all_to_all_single(recv, send, [int(c) for c in recv_counts], [int(c) for c in send_counts],
+                                    group=self.group)
         return recv
+
+    def exchange_counts(self, counts):
+        """counts [2G] (rows to each rank, then pairs to each rank) -> host
+        lists (rows sent, pairs sent, rows received, pairs received)."""
+        import torch
+        G = self.world
+        mine = counts.view(2, G).t().contiguous()  # [G][2]: (rows, pairs) for rank r
+        theirs = torch.empty_like(mine)
+        self.dist.all_to_all_single(theirs, mine, group=self.group)
+        both = torch.cat([mine.reshape(-1), theirs.reshape(-1)]).tolist()
+        return both[0:2 * G:2], both[1:2 * G:2], both[2 * G::2], both[2 * G + 1::2]
 
     def forward(self, x, residual=None):
         """x: [T, d] local tokens.  Returns out [T, d] (float32)."""
-        import torch
-        T = x.shape[0]
-        idx, rows = self.backend.route(x)                     # [T, k] int32, [T, d] row payload
-        pairs, dest_eid, counts = plan_sends(idx, self.E, self.world)
-        recv_counts = torch.empty_like(counts)
-        self.dist.all_to_all_single(recv_counts, counts, group=self.group)
-        sc, rc = counts.tolist(), recv_counts.tolist()
-        send_rows = rows.index_select(0, pairs // self.k)
-        recv_rows = self._a2a(send_rows, sc, rc)
-        recv_eid = self._a2a(dest_eid, sc, rc)
-        y_recv = self.backend.experts(recv_rows, recv_eid)    # [n_recv, d]
-        y_back = self._a2a(y_recv, rc, sc)
-        y_pairs = torch.zeros((T * self.k, self.d), dtype=y_back.dtype, device=y_back.device)
-        y_pairs.index_copy_(0, pairs, y_back)
-        return self.backend.combine(y_pairs, residual)
+        be = self.backend
+        be.route(x)
+        send_rows, send_meta, counts, pair_pos = be.dispatch(self.world)
+        s_rows, s_pairs, r_rows, r_pairs = self.exchange_counts(counts)
+        ns = sum(s_rows)
+        recv_rows = self._a2a(send_rows[:ns], s_rows, r_rows)
+        recv_meta = self._a2a(send_meta[:ns], s_rows, r_rows)
+        y = be.experts(recv_rows, recv_meta, sum(r_pairs))
+        y_back = self._a2a(y, r_pairs, s_pairs)
+        return be.combine(y_back, pair_pos, residual)
 
 
 class CudaBackend:
     """The qmoe C-ABI on one GPU: the full layer's router and shared expert,
     this rank's slice of the expert tensors."""
 
-    def __init__(self, blk, local_blk, dims, local_dims, max_tokens: int, max_rows: int, norm_weight=None,
-                 eps: float = 1e-6):
+    def __init__(self, blk, local_blk, dims, local_dims, world: int, max_tokens: int, max_rows: int,
+                 norm_weight=None, eps: float = 1e-6):
         import torch
         self.blk, self.local_blk = blk, local_blk
         self.dims, self.local_dims = dims, local_dims
         self.norm_weight, self.eps = norm_weight, eps
+        self.world = world
         L = _lib.lib()
+        k, d = dims.top_k, dims.d_model
         self.ws_bytes = L.qmoe_workspace_size(ctypes.byref(dims), max_tokens)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device="cuda")
         _lib.check(L.qmoe_workspace_init(self.ws.data_ptr(), self.ws_bytes, None))
+        self.scratch_bytes = L.qmoe_ep_dispatch_scratch_size(max_tokens, world)
+        self.scratch = torch.empty(self.scratch_bytes, dtype=torch.uint8, device="cuda")
+        cap = max_tokens * min(world, k)
+        self.send_rows = torch.empty((cap, d), dtype=torch.float16, device="cuda")
+        self.send_meta = torch.empty((cap, k), dtype=torch.int32, device="cuda")
+        self.counts = torch.empty(2 * world, dtype=torch.int32, device="cuda")
+        self.pair_pos = torch.empty(max_tokens * k, dtype=torch.int32, device="cuda")
         self._rows_ws(max_rows)
         self.T = 0
 
@@ -120,6 +118,7 @@ class CudaBackend:
         if not self.rws_bytes:
             raise ValueError("qmoe_ep_rows_workspace_size: bad local dims")
         self.rws = torch.empty(self.rws_bytes, dtype=torch.uint8, device="cuda")
+        _lib.check(_lib.lib().qmoe_workspace_init(self.rws.data_ptr(), self.rws_bytes, None))
 
     def _view(self, which, count, dtype):
         import torch
@@ -131,36 +130,47 @@ class CudaBackend:
     def route(self, x):
         import torch
         self.T = T = x.shape[0]
-        self.x = x
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(_lib.lib().qmoe_ep_route(
             ctypes.byref(self.blk), ctypes.byref(self.dims), x.data_ptr(),
             None if self.norm_weight is None else self.norm_weight.data_ptr(), self.eps, T,
             self.ws.data_ptr(), self.ws_bytes, stream), "ep_route")
-        k, d = self.dims.top_k, self.dims.d_model
-        idx = self._view(_lib.WS_TOPK_IDX, T * k, torch.int32).view(T, k)
-        rows = self._view(_lib.WS_INPUT16, T * d, torch.float16).view(T, d)
-        return idx, rows
 
-    def experts(self, rows, eid):
+    def topk_idx(self):
+        import torch
+        k = self.dims.top_k
+        return self._view(_lib.WS_TOPK_IDX, self.T * k, torch.int32).view(self.T, k)
+
+    def dispatch(self, world: int):
+        import torch
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(_lib.lib().qmoe_ep_dispatch(
+            ctypes.byref(self.dims), self.T, world, self.ws.data_ptr(), self.ws_bytes, self.send_rows.data_ptr(),
+            self.send_meta.data_ptr(), self.counts.data_ptr(), self.pair_pos.data_ptr(), self.scratch.data_ptr(),
+            self.scratch_bytes, stream), "ep_dispatch")
+        return self.send_rows, self.send_meta, self.counts, self.pair_pos[:self.T * self.dims.top_k]
+
+    def experts(self, rows, meta, n_pairs: int):
         import torch
         n = rows.shape[0]
-        y = torch.empty_like(rows)
+        y = torch.empty((n_pairs, self.dims.d_model), dtype=torch.float16, device="cuda")
         if n:
             if n > self.max_rows:  # a rank received more rows than planned: grow its row workspace
                 self._rows_ws(n)
             stream = torch.cuda.current_stream().cuda_stream
             _lib.check(_lib.lib().qmoe_ep_experts(
-                ctypes.byref(self.local_blk), ctypes.byref(self.local_dims), rows.data_ptr(), eid.data_ptr(), n,
+                ctypes.byref(self.local_blk), ctypes.byref(self.local_dims), rows.data_ptr(), meta.data_ptr(), n,
                 y.data_ptr(), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts")
         return y
 
-    def combine(self, y_pairs, residual=None):
+    def combine(self, y, pair_pos, residual=None):
         import torch
         out = torch.empty((self.T, self.dims.d_model), dtype=torch.float32, device="cuda")
+        if y.shape[0] == 0:  # no pair anywhere (every token failed routing): any valid pointer will do
+            y = torch.zeros((1, self.dims.d_model), dtype=torch.float16, device="cuda")
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(_lib.lib().qmoe_ep_combine(
-            ctypes.byref(self.blk), ctypes.byref(self.dims), y_pairs.data_ptr(), self.T,
+            ctypes.byref(self.blk), ctypes.byref(self.dims), y.data_ptr(), pair_pos.data_ptr(), self.T,
             None if residual is None else residual.data_ptr(), out.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
             stream), "ep_combine")
         return out
@@ -180,5 +190,5 @@ def local_block(blk: "_lib.QmoeBlock", dims, rank: int, world: int) -> tuple["_l
 
     lb = _lib.QmoeBlock(blk.router, sl(blk.gate_exps, F, d), sl(blk.up_exps, F, d), sl(blk.down_exps, d, F),
                         blk.shared_gate_inp, blk.shared_gate, blk.shared_up, blk.shared_down, None)
-    ld = _lib.QmoeDims(d, n, dims.top_k, F, dims.shared_dim)
+    ld = _lib.QmoeDims(d, n, dims.top_k, F, dims.shared_dim)  # top_k: the layer's k (meta row width)
     return lb, ld

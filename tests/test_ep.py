@@ -1,9 +1,11 @@
 """Expert-parallel exchange (qmoe/ep.py) on CPU: gloo ranks and a fake compute
 backend whose experts are simple per-expert scalings, checked against the same
-block computed without the exchange.  The backend's route/experts/combine are
-the three qmoe_ep_* calls on a GPU; here they are numpy so that only the
-exchange logic (destination grouping, all-to-all counts, return placement,
-invalid pairs, ragged and empty ranks) is under test."""
+block computed without the exchange.  The backend's route / dispatch /
+experts / combine are the qmoe_ep_* calls on a GPU; here they are numpy (the
+dispatch layout from tests/ep_plan_ref.py, which the CUDA kernels are checked
+against on the GPU) so that only the exchange logic (count exchange, row and
+meta all-to-all, return of the outputs, pair placement, invalid slots, ragged
+and empty ranks) is under test."""
 from __future__ import annotations
 
 import os
@@ -15,6 +17,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+import ep_plan_ref
 from qmoe import ep
 
 D, K = 16, 4
@@ -55,26 +58,41 @@ def _reference(x: np.ndarray, E: int, seed: int) -> np.ndarray:
 
 
 class FakeBackend:
+    """route / dispatch / experts / combine with the semantics of the
+    qmoe_ep_* calls, on the host."""
+
     def __init__(self, E: int, lo: int, seed: int):
         self.E, self.lo, self.seed = E, lo, seed
         self.received = 0
 
     def route(self, x):
         self.x = x.numpy()
-        idx, self.w = _routing(self.x, self.E, self.seed)
-        return torch.from_numpy(idx), x.clone()
+        self.idx, self.w = _routing(self.x, self.E, self.seed)
 
-    def experts(self, rows, eid):
-        self.received += rows.shape[0]
-        e = eid.numpy().astype(np.int64)
-        assert (e >= 0).all() and (e < self.E).all()
-        s = _scale(self.E)[self.lo + e] if len(e) else np.zeros(0, np.float32)
-        return rows * torch.from_numpy(s)[:, None]
+    def dispatch(self, G):
+        tok, meta, counts, pair_pos = ep_plan_ref.dispatch_plan(self.idx, self.E, G)
+        rows = self.x[tok] if len(tok) else np.zeros((0, D), np.float32)
+        return (torch.from_numpy(np.ascontiguousarray(rows)), torch.from_numpy(meta.reshape(-1, K)),
+                torch.from_numpy(counts), torch.from_numpy(pair_pos))
 
-    def combine(self, y_pairs, residual=None):
+    def experts(self, rows, meta, n_pairs):
+        m = meta.numpy()
+        r, e = ep_plan_ref.pair_rows(m)
+        assert len(r) == n_pairs
+        self.received += n_pairs
+        assert (e < self.E).all()
+        y = rows.numpy()[r] * _scale(self.E)[self.lo + e][:, None] if n_pairs else np.zeros((0, D), np.float32)
+        return torch.from_numpy(np.ascontiguousarray(y, dtype=np.float32))
+
+    def combine(self, y, pair_pos, residual=None):
         T = self.x.shape[0]
-        y = y_pairs.numpy().reshape(T, K, D)
-        return torch.from_numpy(self.x + (self.w[:, :, None] * y).sum(1))
+        yv, pp = y.numpy(), pair_pos.numpy()
+        out = self.x.copy()
+        for t in range(T):
+            for j in range(K):
+                if pp[t * K + j] >= 0:
+                    out[t] += self.w[t, j] * yv[pp[t * K + j]]
+        return torch.from_numpy(out)
 
 
 def _worker(rank, world, port, E, token_counts, seed, q):
@@ -107,13 +125,15 @@ def _run(world, E, token_counts, seed=5):
     return res
 
 
-def test_plan_sends_groups_by_destination():
-    idx = torch.tensor([[5, 0, 3], [-1, 2, 7], [6, 1, -1]], dtype=torch.int32)
-    pairs, eid, counts = ep.plan_sends(idx, 8, 2)
-    # rank 0 owns experts 0..3, rank 1 owns 4..7; pair order kept inside a rank
-    assert pairs.tolist() == [1, 2, 4, 7, 0, 5, 6]
-    assert eid.tolist() == [0, 3, 2, 1, 1, 3, 2]
-    assert counts.tolist() == [4, 3]
+def test_dispatch_plan_layout():
+    idx = np.array([[5, 0, 3], [-1, -1, -1], [6, 1, 4]], dtype=np.int32)
+    tok, meta, counts, pair_pos = ep_plan_ref.dispatch_plan(idx, 8, 2)
+    # rank 0 owns experts 0..3, rank 1 owns 4..7; one row per (token, rank)
+    assert tok.tolist() == [0, 2, 0, 2]
+    assert meta.tolist() == [[-1, 0, 3], [-1, 1, -1], [1, -1, -1], [2, -1, 0]]
+    assert counts.tolist() == [2, 2, 3, 3]
+    # returned outputs: rank 0's pairs (0,1) (0,2) (2,1), then rank 1's (0,0) (2,0) (2,2)
+    assert pair_pos.tolist() == [3, 0, 1, -1, -1, -1, 4, 2, 5]
 
 
 def test_shard_bounds():

@@ -18,6 +18,7 @@ from datetime import timedelta
 import numpy as np
 import pytest
 
+import ep_plan_ref
 from qmoe import _lib, ep, synth
 
 from gpu_util import assert_close
@@ -31,9 +32,11 @@ def _poison(be):
     """Fill a backend's workspaces with a non-zero pattern (then re-initialise
     the control words) so that nothing can pass by reading memory left behind
     by an earlier call."""
-    be.ws.fill_(0xA5)
-    be.rws.fill_(0xA5)
+    import torch
+    for buf in (be.ws, be.rws, be.scratch, be.send_rows, be.send_meta, be.pair_pos):
+        buf.view(torch.uint8).fill_(0xA5)
     _lib.check(_lib.lib().qmoe_workspace_init(be.ws.data_ptr(), be.ws_bytes, None))
+    _lib.check(_lib.lib().qmoe_workspace_init(be.rws.data_ptr(), be.rws_bytes, None))
 
 
 def _reference(blk, x, residual):
@@ -58,38 +61,53 @@ def _reference(blk, x, residual):
 
 @pytest.mark.parametrize("G,types,bias", [(2, synth.Q4K_TYPES, False), (8, synth.MIXED_TYPES, True)])
 def test_ep_shards_on_one_gpu(cuda, G, types, bias):
+    """Every rank of a G-way split on one GPU: the send layout bit-exact
+    against tests/ep_plan_ref.py, each rank's chunk through its local experts,
+    the chunks' outputs concatenated in rank order as the all-to-all returns
+    them, then the combine -- equal to the 1-GPU block."""
     import torch
     dims = synth.Dims()
     T = 300
+    k, d = dims.top_k, dims.d_model
     blk = synth.Block(dims, types, seed=SEED, bias=bias)
-    x = synth.inputs(T, dims.d_model, seed=17, tag=3)
-    residual = synth.inputs(T, dims.d_model, seed=18, tag=4)
+    x = synth.inputs(T, d, seed=17, tag=3)
+    residual = synth.inputs(T, d, seed=18, tag=4)
     want, want_idx = _reference(blk, x, residual)
 
     full, dc = blk.c(), dims.c()
     L = _lib.lib()
-    be = ep.CudaBackend(full, full, dc, dc, max_tokens=T, max_rows=T * dims.top_k)
+    be = ep.CudaBackend(full, full, dc, dc, G, max_tokens=T, max_rows=T)
     _poison(be)
-    idx, rows = be.route(x)
+    be.route(x)
+    idx = be.topk_idx()
     assert torch.equal(idx, want_idx)
-    pairs, dest_eid, counts = ep.plan_sends(idx, dims.num_experts, G)
-    y_pairs = torch.zeros((T * dims.top_k, dims.d_model), dtype=torch.float16, device="cuda")
-    start = 0
+    send_rows, send_meta, counts, pair_pos = be.dispatch(G)
+    tok, meta, cnt, pp = ep_plan_ref.dispatch_plan(idx.cpu().numpy(), dims.num_experts, G)
+    torch.cuda.synchronize()
+    assert counts.cpu().numpy().tolist() == cnt.tolist()
+    assert np.array_equal(pair_pos.cpu().numpy(), pp)
+    ns = len(tok)
+    assert np.array_equal(send_meta[:ns].cpu().numpy(), meta)
+    x16 = be._view(_lib.WS_INPUT16, T * d, torch.float16).view(T, d)
+    assert torch.equal(send_rows[:ns], x16[torch.from_numpy(tok).cuda()])
+
+    chunks, r0 = [], 0
     for r in range(G):
-        n = int(counts[r])
+        nr, npairs = int(cnt[r]), int(cnt[G + r])
         lb, ld = ep.local_block(full, dc, r, G)
-        p = pairs[start:start + n]
-        rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), max(n, 1))
+        rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), max(nr, 1))
         rws = torch.full((rws_bytes,), 0xA5, dtype=torch.uint8, device="cuda")
-        r_rows = rows.index_select(0, p // dims.top_k).contiguous()
-        r_eid = dest_eid[start:start + n].contiguous()
-        y = torch.empty_like(r_rows)
-        _lib.check(L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), r_rows.data_ptr(), r_eid.data_ptr(), n,
-                                     y.data_ptr(), rws.data_ptr(), rws_bytes, None), "ep_experts")
-        y_pairs.index_copy_(0, p, y)
-        start += n
-    assert start == T * dims.top_k
-    got = be.combine(y_pairs, residual)
+        _lib.check(L.qmoe_workspace_init(rws.data_ptr(), rws_bytes, None))
+        y = torch.empty((npairs, d), dtype=torch.float16, device="cuda")
+        if nr:
+            _lib.check(L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), send_rows[r0:r0 + nr].data_ptr(),
+                                         send_meta[r0:r0 + nr].data_ptr(), nr, y.data_ptr(), rws.data_ptr(),
+                                         rws_bytes, None), "ep_experts")
+        chunks.append(y)
+        r0 += nr
+    y_ret = torch.cat(chunks)
+    assert y_ret.shape[0] == int((idx >= 0).sum())
+    got = be.combine(y_ret, pair_pos, residual)
     torch.cuda.synchronize()
     assert_close(got.cpu().numpy(), want.cpu().numpy(), f"ep G={G}")
     assert torch.equal(got, want)
@@ -106,11 +124,11 @@ def test_ep_argument_checks(cuda):
     rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), 16)
     rws = torch.empty(rws_bytes, dtype=torch.uint8, device="cuda")
     rows = torch.zeros((16, 512), dtype=torch.float16, device="cuda")
-    eid = torch.zeros(16, dtype=torch.int32, device="cuda")
     y = torch.empty_like(rows)
+    meta = torch.zeros((16, 4), dtype=torch.int32, device="cuda")
     # zero rows is a no-op, too small a workspace is refused, decode-sized routing is refused
     assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), None, None, 0, None, None, 0, None) == _lib.QMOE_OK
-    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), eid.data_ptr(), 16, y.data_ptr(),
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), meta.data_ptr(), 16, y.data_ptr(),
                              rws.data_ptr(), 1024, None) == _lib.QMOE_ERR_WORKSPACE
     ws_bytes = L.qmoe_workspace_size(ctypes.byref(dc), 64)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
@@ -143,11 +161,11 @@ def _nccl_worker(rank, world, port, t_local, q):
         x, res = x_all[sl].contiguous(), r_all[sl].contiguous()
         full, dc = blk.c(), dims.c()
         lb, ld = ep.local_block(full, dc, rank, world)
-        be = ep.CudaBackend(full, lb, dc, ld, max_tokens=t_local, max_rows=t_local * dims.top_k)
+        be = ep.CudaBackend(full, lb, dc, ld, world, max_tokens=t_local, max_rows=t_local)
         _poison(be)
         moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model)
         got = moe.forward(x, res)
-        idx = be._view(_lib.WS_TOPK_IDX, t_local * dims.top_k, torch.int32).view(t_local, dims.top_k)
+        idx = be.topk_idx()
         torch.cuda.synchronize()
         ids_equal = bool(torch.equal(idx, want_idx[sl]))
         max_err = float((got - want[sl]).abs().max())
