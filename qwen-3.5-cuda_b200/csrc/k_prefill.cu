@@ -403,13 +403,52 @@ inline size_t gemm_smem_bytes() { return 1024 + static_cast<size_t>(NST) * STAGE
 // RMSNorm of every token (ops.cu:25-65 structure): one warp per token, the sum
 // of squares with the reference GEMV's thread/shuffle structure (as in the
 // decode router), then (x * scale) * weight.  Without a norm weight it copies.
+// Besides x_in (F32) it writes the fp16 copy for the tensor cores, the copy in
+// the router's leaf order (pf_perm_pos) for k_route_tile, and the shared-expert
+// gate logit x_in . w_sg in the reference GEMV order (logits[t][E]).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float pf_tree8(float (&acc)[2][4]);
+
+// Position of element k = 256i + 128hh + 32g + 4l + c of a row in the router
+// leaf order: the reference GEMV's 256 FMA chains (thread 4(8g+l)+c+128hh,
+// elements i = 0..CH-1) grouped by the first level of its reduction tree
+// (eight chains l = 0..7 of one (hh, g, c)), each chain's elements contiguous.
+template <int CH>
+__device__ __forceinline__ int pf_perm_pos(int i, int hh, int g, int l, int c) {
+    return ((((hh * 4 + g) * 4 + c) * 8 + l) * CH) + i;
+}
+
+// Lane L of a warp holds v[i][hh] = elements 256i + 128hh + 4L + (0..3) of a
+// row; write them in the leaf order (CH consecutive floats per chain).
+template <int CH>
+__device__ __forceinline__ void pf_store_perm(float* __restrict__ dst, const float4 (&v)[CH][2], int lane) {
+    const int g = lane >> 3, l = lane & 7;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float e[CH];
+#pragma unroll
+            for (int i = 0; i < CH; ++i) e[i] = c == 0 ? v[i][hh].x : c == 1 ? v[i][hh].y : c == 2 ? v[i][hh].z : v[i][hh].w;
+            float* o = dst + pf_perm_pos<CH>(0, hh, g, l, c);
+            if (CH % 4 == 0) {
+#pragma unroll
+                for (int i = 0; i < CH; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(e[i], e[i + 1], e[i + 2], e[i + 3]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < CH; ++i) o[i] = e[i];
+            }
+        }
+}
+
+template <int CH>
+__device__ __forceinline__ void pf_load_row(float4 (&w)[CH][2], const uint8_t* row, int type, int lane);
 
 template <int CH>
 __global__ void __launch_bounds__(256) k_norm_many(const float* __restrict__ x, const float* __restrict__ w,
                                                    float eps, float* __restrict__ out, __half* __restrict__ x16,
-                                                   int T, int d) {
+                                                   float* __restrict__ xperm, const uint8_t* __restrict__ sgate,
+                                                   int sgate_type, float* __restrict__ logits, int E, int T, int d) {
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -457,6 +496,24 @@ __global__ void __launch_bounds__(256) k_norm_many(const float* __restrict__ x, 
                                         pf::h2_bits(__floats2half2_rn(v[i][hh].y, v[i][hh].w)));
             *reinterpret_cast<uint2*>(hrow + (e0 & ~7) + 4 * (lane & 1)) = hv;
         }
+    pf_store_perm<CH>(xperm + static_cast<size_t>(t) * d, v, lane);
+    if (sgate) {  // shared-expert gate logit, row E of the router output (layer_moe.cpp:140-144)
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            float4 sg[1][2];  // the gate elements of this lane at step i
+            pf_load_row<1>(sg, sgate + (sgate_type == T_F32 ? 4 : 2) * 256 * i, sgate_type, lane);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                acc[hh][0] = __fmaf_rn(sg[0][hh].x, v[i][hh].x, acc[hh][0]);
+                acc[hh][1] = __fmaf_rn(sg[0][hh].y, v[i][hh].y, acc[hh][1]);
+                acc[hh][2] = __fmaf_rn(sg[0][hh].z, v[i][hh].z, acc[hh][2]);
+                acc[hh][3] = __fmaf_rn(sg[0][hh].w, v[i][hh].w, acc[hh][3]);
+            }
+        }
+        const float lg = pf_tree8(acc);
+        if (lane == 0) logits[static_cast<size_t>(t) * (E + 1) + E] = lg;
+    }
 }
 
 // The reference GEMV's reduction of the 8 per-lane chains (lane L plays
@@ -488,10 +545,20 @@ __device__ __forceinline__ float pf_tree8(float (&acc)[2][4]) {
 }
 
 // ---------------------------------------------------------------------------
-// Router logits of many tokens, reference GEMV order.  Each warp holds two
-// router rows in registers (rows 2*gw and 2*gw+1 of the E+1 rows: the E
-// expert rows, then the shared-expert gate vector) and walks a chunk of
-// tokens; each x_in value it loads serves both rows.
+// Router logits of many tokens in the reference GEMV order (matmul_q4.cu:
+// 140-167: 256 threads, thread j accumulates elements j*4+c+... with one FMA
+// chain per (thread, component), then a fixed shuffle/partial-sum tree).
+// Every logit is that fixed arithmetic DAG: 256 chains of CH FMAs, grouped by
+// the tree into 32 first-level groups G(hh, g, c) of eight chains,
+//   G = ((v0 + v4) + (v2 + v6)) + ((v1 + v5) + (v3 + v7))   (v_l: chain 8g+l),
+//   s(hh, g) = (G(c=0) + G(c=2)) + (G(c=1) + G(c=3)),
+//   logit = ((z00 + z10) + (z02 + z12)) + ((z01 + z11) + (z03 + z13)),
+//   z_hg = (s(h, g) + 0) + 0.
+// k_route_tile evaluates it for a 64-token x 32-expert tile per CTA: the
+// inputs come in the leaf order (pf_perm_pos), one first-level group (96 rows
+// x 8*CH floats) per pipeline stage, and every lane computes 4 tokens x 2
+// experts with the whole tree in registers -- no shuffles, each shared-memory
+// value feeding 2 or 4 FMAs.
 // ---------------------------------------------------------------------------
 template <int CH>
 __device__ __forceinline__ void pf_load_row(float4 (&w)[CH][2], const uint8_t* row, int type, int lane) {
@@ -515,85 +582,163 @@ __device__ __forceinline__ void pf_load_row(float4 (&w)[CH][2], const uint8_t* r
         }
 }
 
-constexpr int RM_NBUF = 4;  // x_in rows in flight per CTA
+// Router rows (expert rows, any supported row type) -> F32 in the leaf order.
+template <int CH>
+__global__ void __launch_bounds__(256) k_perm_rows(const uint8_t* __restrict__ router, int type, int E, int d,
+                                                   float* __restrict__ wp) {
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (e >= E) return;
+    float4 w[CH][2];
+    pf_load_row<CH>(w, router + static_cast<size_t>(e) * d * (type == T_F32 ? 4 : 2), type, lane);
+    pf_store_perm<CH>(wp + static_cast<size_t>(e) * d, w, lane);
+}
+
+namespace rt {
+constexpr int TT = 64, TE = 32, ROWS = TT + TE, NSTG = 4;
+template <int CH>
+constexpr int rs() { return 8 * CH + 4; }  // padded row stride in floats (rows land on distinct bank groups)
+template <int CH>
+constexpr size_t smem_bytes() { return static_cast<size_t>(NSTG) * ROWS * rs<CH>() * sizeof(float); }
+
+// Chain l of the current group for this lane's 8 (token, expert) pairs:
+// pair p = (token p/2, expert p%2), acc = fma(w_i, x_i, acc) over i = 0..CH-1.
+template <int CH>
+__device__ __forceinline__ void chains(const float* xr, const float* wr, float (&v)[8]) {
+    constexpr int RS = rs<CH>();
+    float xv[4][CH], wv[2][CH];
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+        const float* src = xr + tt * 4 * RS;
+        if (CH % 4 == 0) {
+#pragma unroll
+            for (int i = 0; i < CH; i += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(src + i);
+                xv[tt][i] = q.x; xv[tt][i + 1] = q.y; xv[tt][i + 2] = q.z; xv[tt][i + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) xv[tt][i] = src[i];
+        }
+    }
+#pragma unroll
+    for (int ee = 0; ee < 2; ++ee) {
+        const float* src = wr + ee * 8 * RS;
+        if (CH % 4 == 0) {
+#pragma unroll
+            for (int i = 0; i < CH; i += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(src + i);
+                wv[ee][i] = q.x; wv[ee][i + 1] = q.y; wv[ee][i + 2] = q.z; wv[ee][i + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) wv[ee][i] = src[i];
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CH; ++i) acc = __fmaf_rn(wv[p & 1][i], xv[p >> 1][i], acc);
+        v[p] = acc;
+    }
+}
+}  // namespace rt
 
 template <int CH>
-__global__ void __launch_bounds__(256) k_route_many(const uint8_t* __restrict__ router, int router_type,
-                                                    const uint8_t* __restrict__ sgate, int sgate_type,
-                                                    const float* __restrict__ bias, const float* __restrict__ xin,
-                                                    float* __restrict__ logits, int T, int d, int E, int has_shared,
-                                                    int tchunk, uint32_t* ctrl) {
-    // x_in rows are bulk-copied into shared memory, RM_NBUF ahead; every warp
-    // reads each row once for its two router rows
-    __shared__ __align__(128) float s_x[RM_NBUF][256 * CH];
-    __shared__ __align__(8) uint64_t s_full[RM_NBUF];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = blockIdx.x * 8 + warp;
-    const int nrows = E + (has_shared ? 1 : 0);
-    const int ra = 2 * gw, rb = 2 * gw + 1;
-    const bool has_a = ra < nrows, has_b = rb < nrows;
-    const int t0 = blockIdx.y * tchunk, t1 = min(T, t0 + tchunk);
-    const uint32_t row_bytes_x = static_cast<uint32_t>(d) * 4u;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < RM_NBUF; ++i) mbar_init(s_full + i, 1);
-        fence_mbar_init();
-        for (int i = 0; i < RM_NBUF && t0 + i < t1; ++i) {
-            mbar_arrive_expect_tx(s_full + i, row_bytes_x);
-            bulk_g2s(s_x[i], xin + static_cast<size_t>(t0 + i) * d, row_bytes_x, s_full + i, ctrl);
-        }
-    }
-    float4 wa[CH][2], wb[CH][2];
-    auto row_ptr = [&](int r, int& type) {
-        type = r < E ? router_type : sgate_type;
-        return r < E ? router + static_cast<size_t>(r) * d * (type == T_F32 ? 4 : 2) : sgate;
-    };
-    int ta = 0, tb = 0;
-    if (has_a) {
-        pf_load_row<CH>(wa, row_ptr(ra, ta), ta, lane);
-    } else {
-#pragma unroll
-        for (int i = 0; i < CH; ++i) wa[i][0] = wa[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    if (has_b) {
-        pf_load_row<CH>(wb, row_ptr(rb, tb), tb, lane);
-    } else {
-#pragma unroll
-        for (int i = 0; i < CH; ++i) wb[i][0] = wb[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    const float bias_a = (has_a && ra < E && bias) ? __ldg(bias + ra) : 0.0f;
-    const float bias_b = (has_b && rb < E && bias) ? __ldg(bias + rb) : 0.0f;
-    const int LS = E + 1;
-    __syncthreads();
-    for (int t = t0, n = 0; t < t1; ++t, ++n) {
-        const int buf = n % RM_NBUF;
-        mbar_wait(s_full + buf, (n / RM_NBUF) & 1, ctrl);
-        float aa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        float ab[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-        for (int i = 0; i < CH; ++i)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const float4 xv = *reinterpret_cast<const float4*>(&s_x[buf][256 * i + 128 * hh + 4 * lane]);
-                aa[hh][0] = __fmaf_rn(wa[i][hh].x, xv.x, aa[hh][0]);
-                aa[hh][1] = __fmaf_rn(wa[i][hh].y, xv.y, aa[hh][1]);
-                aa[hh][2] = __fmaf_rn(wa[i][hh].z, xv.z, aa[hh][2]);
-                aa[hh][3] = __fmaf_rn(wa[i][hh].w, xv.w, aa[hh][3]);
-                ab[hh][0] = __fmaf_rn(wb[i][hh].x, xv.x, ab[hh][0]);
-                ab[hh][1] = __fmaf_rn(wb[i][hh].y, xv.y, ab[hh][1]);
-                ab[hh][2] = __fmaf_rn(wb[i][hh].z, xv.z, ab[hh][2]);
-                ab[hh][3] = __fmaf_rn(wb[i][hh].w, xv.w, ab[hh][3]);
+__global__ void __launch_bounds__(256, 2) k_route_tile(const float* __restrict__ xp, const float* __restrict__ wp,
+                                                       const float* __restrict__ bias, float* __restrict__ logits,
+                                                       int T, int E, int d) {
+    constexpr int GS = 8 * CH, RS = rt::rs<CH>();
+    extern __shared__ __align__(16) float rt_smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t0 = blockIdx.x * rt::TT, e0 = blockIdx.y * rt::TE;
+    // warp: 16 tokens x 16 experts; lane: tokens wt*16 + tt*4 + tg, experts we*16 + ee*8 + eg
+    const int wt = warp & 3, we = warp >> 2, tg = lane >> 3, eg = lane & 7;
+    // group q = 4u + ci in tree order: unit u -> (g, hh), ci -> c
+    auto stage = [&](int q) {
+        const int u = q >> 2, ci = q & 3;
+        const int g = (0x3120 >> (4 * (u >> 1))) & 0xF;   // units pair g = 0, 2, 1, 3
+        const int hh = u & 1;
+        const int c = (0x3120 >> (4 * ci)) & 0xF;          // c = 0, 2, 1, 3
+        const int off = ((hh * 4 + g) * 4 + c) * GS;
+        float* buf = rt_smem + (q % rt::NSTG) * rt::ROWS * RS;
+        for (int ch = tid; ch < rt::ROWS * (GS / 4); ch += 256) {
+            const int row = ch / (GS / 4), col = (ch % (GS / 4)) * 4;
+            const float* src;
+            bool ok;
+            if (row < rt::TT) {
+                const int t = t0 + row;
+                ok = t < T;
+                src = xp + static_cast<size_t>(ok ? t : 0) * d + off + col;
+            } else {
+                const int e = e0 + row - rt::TT;
+                ok = e < E;
+                src = wp + static_cast<size_t>(ok ? e : 0) * d + off + col;
             }
-        float va = pf_tree8(aa);
-        float vb = pf_tree8(ab);
-        if (lane == 0) {
-            if (has_a) logits[static_cast<size_t>(t) * LS + ra] = (ra < E && bias) ? __fadd_rn(va, bias_a) : va;
-            if (has_b) logits[static_cast<size_t>(t) * LS + rb] = (rb < E && bias) ? __fadd_rn(vb, bias_b) : vb;
+            pf::cp_async16(smem_u32(buf + row * RS + col), src, ok ? 16u : 0u);
         }
-        __syncthreads();  // every warp is done with this buffer
-        if (threadIdx.x == 0 && t + RM_NBUF < t1) {
-            mbar_arrive_expect_tx(s_full + buf, row_bytes_x);
-            bulk_g2s(s_x[buf], xin + static_cast<size_t>(t + RM_NBUF) * d, row_bytes_x, s_full + buf, ctrl);
+        pf::cp_async_commit();
+    };
+    float r0[8], r1[8], r2[8];  // pending partial sums of the last tree level
+#pragma unroll
+    for (int p = 0; p < 8; ++p) r0[p] = r1[p] = r2[p] = 0.0f;
+    for (int q = 0; q < rt::NSTG - 1; ++q) stage(q);
+    for (int u = 0; u < 8; ++u) {
+        float sp[8], s1[8], sv[8];
+#pragma unroll
+        for (int ci = 0; ci < 4; ++ci) {
+            const int q = 4 * u + ci;
+            pf::cp_async_wait<rt::NSTG - 2>();  // group q has landed (this thread's copies)
+            __syncthreads();                    // everyone's copies; everyone is done with group q-1
+            if (q + rt::NSTG - 1 < 32) stage(q + rt::NSTG - 1); else pf::cp_async_commit();
+            const float* buf = rt_smem + ci * rt::ROWS * RS;  // q % NSTG == ci
+            const float* xr = buf + (wt * 16 + tg) * RS;
+            const float* wr = buf + (rt::TT + we * 16 + eg) * RS;
+            float G[8], A[8], C[8], tmp[8], v[8];
+#pragma unroll
+            for (int li = 0; li < 8; ++li) {
+                const int l = (0x73516240 >> (4 * li)) & 0xF;  // 0, 4, 2, 6, 1, 5, 3, 7
+                rt::chains<CH>(xr + l * CH, wr + l * CH, v);
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    if (li == 0 || li == 2 || li == 4 || li == 6) tmp[p] = v[p];
+                    else if (li == 1) A[p] = __fadd_rn(tmp[p], v[p]);
+                    else if (li == 3) A[p] = __fadd_rn(A[p], __fadd_rn(tmp[p], v[p]));
+                    else if (li == 5) C[p] = __fadd_rn(tmp[p], v[p]);
+                    else G[p] = __fadd_rn(A[p], __fadd_rn(C[p], __fadd_rn(tmp[p], v[p])));
+                }
+            }
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+                if (ci == 0) sp[p] = G[p];
+                else if (ci == 1) sp[p] = __fadd_rn(sp[p], G[p]);
+                else if (ci == 2) s1[p] = G[p];
+                else sv[p] = __fadd_rn(sp[p], __fadd_rn(s1[p], G[p]));
+            }
         }
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            const float z = __fadd_rn(__fadd_rn(sv[p], 0.0f), 0.0f);
+            switch (u) {
+                case 0: r0[p] = z; break;
+                case 1: r0[p] = __fadd_rn(r0[p], z); break;
+                case 2: r1[p] = z; break;
+                case 3: r0[p] = __fadd_rn(r0[p], __fadd_rn(r1[p], z)); break;
+                case 4: r1[p] = z; break;
+                case 5: r1[p] = __fadd_rn(r1[p], z); break;
+                case 6: r2[p] = z; break;
+                default: r0[p] = __fadd_rn(r0[p], __fadd_rn(r1[p], __fadd_rn(r2[p], z))); break;
+            }
+        }
+    }
+    pf::cp_async_wait<0>();
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const int t = t0 + wt * 16 + (p >> 1) * 4 + tg;
+        const int e = e0 + we * 16 + (p & 1) * 8 + eg;
+        if (t < T && e < E)
+            logits[static_cast<size_t>(t) * (E + 1) + e] = bias ? __fadd_rn(r0[p], __ldg(bias + e)) : r0[p];
     }
 }
 
@@ -865,38 +1010,26 @@ cudaError_t pf_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s
     const int T = P.T, d = P.d, E = P.E, k = P.k;
     const int CH = d / 256;
     cudaError_t e = cudaSuccess;
-    {
-        const dim3 grid((T + 7) / 8);
-        const float* nw = P.prenorm ? P.norm_w : nullptr;
-        switch (CH) {
-            case 1: k_norm_many<1><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
-            case 2: k_norm_many<2><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
-            case 4: k_norm_many<4><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
-            case 8: k_norm_many<8><<<grid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, T, d); break;
-            default: return cudaErrorInvalidValue;
-        }
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const float* nw = P.prenorm ? P.norm_w : nullptr;
+    const uint8_t* sg = P.has_shared ? P.sgate_inp : nullptr;
+    const dim3 ngrid((T + 7) / 8), pgrid((E + 7) / 8), rgrid((T + rt::TT - 1) / rt::TT, (E + rt::TE - 1) / rt::TE);
+#define QMOE_ROUTE(C)                                                                                               \
+    do {                                                                                                            \
+        k_norm_many<C><<<ngrid, 256, 0, s>>>(P.x, nw, P.eps, P.xnorm, B.X16, B.xperm, sg, P.sgate_type, P.logits, E, \
+                                             T, d);                                                                 \
+        k_perm_rows<C><<<pgrid, 256, 0, s>>>(P.router, P.router_type, E, d, B.wperm);                                \
+        if ((e = pf_set_smem(k_route_tile<C>, rt::smem_bytes<C>())) != cudaSuccess) return e;                       \
+        k_route_tile<C><<<rgrid, 256, rt::smem_bytes<C>(), s>>>(B.xperm, B.wperm, P.bias, P.logits, T, E, d);       \
+    } while (0)
+    switch (CH) {
+        case 1: QMOE_ROUTE(1); break;
+        case 2: QMOE_ROUTE(2); break;
+        case 4: QMOE_ROUTE(4); break;
+        case 8: QMOE_ROUTE(8); break;
+        default: return cudaErrorInvalidValue;
     }
-    {
-        const int nrows = E + (P.has_shared ? 1 : 0);
-        const int rgroups = (((nrows + 1) / 2) + 7) / 8;  // CTAs of 16 router rows
-        // token chunks: about four CTAs per SM in total
-        const int chunks = std::max(1, std::min((T + 15) / 16, 4 * pf_num_sms() / rgroups));
-        const int tchunk = (T + chunks - 1) / chunks;
-        const dim3 grid(rgroups, (T + tchunk - 1) / tchunk);
-#define QMOE_RM(C)                                                                                               \
-    k_route_many<C><<<grid, 256, 0, s>>>(P.router, P.router_type, P.sgate_inp, P.sgate_type, P.bias, P.xnorm, \
-                                         P.logits, T, d, E, P.has_shared, tchunk, P.ctrl)
-        switch (CH) {
-            case 1: QMOE_RM(1); break;
-            case 2: QMOE_RM(2); break;
-            case 4: QMOE_RM(4); break;
-            case 8: QMOE_RM(8); break;
-            default: return cudaErrorInvalidValue;
-        }
-#undef QMOE_RM
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
+#undef QMOE_ROUTE
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_topk_many<<<(T + 7) / 8, 256, 0, s>>>(P.logits, T, E, k, P.topk_idx, P.topk_w, P.out_idx, P.out_w, B.sh_grp,
                                             P.ctrl);
     return cudaGetLastError();

@@ -164,6 +164,8 @@ PrefillBufs prefill_bufs(const qmoe_dims& D, int T, void* ws) {
     pb.Hs = reinterpret_cast<__half*>(w + L.Hs);
     pb.Y = reinterpret_cast<__half*>(w + L.Y);
     pb.Ys = reinterpret_cast<__half*>(w + L.Ys);
+    pb.xperm = reinterpret_cast<float*>(w + L.xperm);
+    pb.wperm = reinterpret_cast<float*>(w + L.wperm);
     return pb;
 }
 

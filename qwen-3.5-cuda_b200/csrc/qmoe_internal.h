@@ -60,7 +60,7 @@ struct WsLayout {
     // prefill regions (T > kDecodeMaxT): source token per permuted pair, tile
     // prefix per expert, the shared expert's group, dispatch scratch, fp16
     // hidden vectors and expert outputs
-    size_t tok_of_pos, tile_start, sh_grp, disp, X16, Hpf, Hs, Y, Ys;
+    size_t tok_of_pos, tile_start, sh_grp, disp, X16, Hpf, Hs, Y, Ys, xperm, wperm;
     size_t xq_stride;  // bytes per token of x planes in shared memory: 3*d + (d/16)*8
     size_t hq_stride;  // bytes per hidden vector of planes: 3*H + (H/16)*8
     int H;             // max(F, Fs)
@@ -105,6 +105,9 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
         L.Hs = take(2 * static_cast<size_t>(T) * Fs);
         L.Y = take(2 * static_cast<size_t>(P) * d);
         L.Ys = take(2 * static_cast<size_t>(T) * d);
+        // x_in and the expert router rows in the router's leaf order (F32)
+        L.xperm = take(sizeof(float) * static_cast<size_t>(T) * d);
+        L.wperm = take(sizeof(float) * static_cast<size_t>(E) * d);
     }
     L.total = o;
     return L;
@@ -148,6 +151,8 @@ struct PrefillBufs {
     __half* Hs;
     __half* Y;
     __half* Ys;
+    float* xperm;  // [T][d] x_in in the router leaf order
+    float* wperm;  // [E][d] router rows in that order
 };
 
 // Phase tracer: kernel kinds x CTAs x events of %globaltimer (ns).
