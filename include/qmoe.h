@@ -202,9 +202,10 @@ QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int
  *                     (row, slot) order), -1 for a failed token
  *   qmoe_ep_experts   this rank's experts on n received rows and meta rows
  *                     (any concatenation of the ranks' chunks): y_pairs
- *                     [pairs][d] fp16 = down(silu(gate x) * up x) for every
+ *                     [n_pairs][d] fp16 = down(silu(gate x) * up x) for every
  *                     valid slot, in (row, slot) order -- the order that
- *                     pair_pos on the sending rank refers to
+ *                     pair_pos on the sending rank refers to; n_pairs = the
+ *                     valid slots of the rows (the senders' pair counts)
  *   qmoe_ep_combine   shared expert and combine of the T local tokens:
  *                     out[t] = residual[t] + sum_j w[t][j] y[pair_pos[t*k+j]]
  *                              + sigmoid(shared gate) * shared(x_in[t])
@@ -221,8 +222,8 @@ QMOE_API int qmoe_ep_dispatch(const qmoe_dims* dims, int T, int G, void* workspa
                       size_t scratch_bytes, qmoe_stream_t stream);
 QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max_rows);
 QMOE_API int qmoe_ep_experts(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
-                     const int32_t* meta, int n_rows, void* y_pairs, void* workspace, size_t workspace_bytes,
-                     qmoe_stream_t stream);
+                     const int32_t* meta, int n_rows, int n_pairs, void* y_pairs, void* workspace,
+                     size_t workspace_bytes, qmoe_stream_t stream);
 QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs,
                      const int32_t* pair_pos, int T, const float* residual, float* out, void* workspace,
                      size_t workspace_bytes, qmoe_stream_t stream);

@@ -35,6 +35,7 @@
 #include "qmoe_dq1.cuh"
 #include "qmoe_internal.h"
 #include "qmoe_route.cuh"
+#include "qmoe_tgemm.h"
 
 namespace qmoe {
 
@@ -182,6 +183,7 @@ struct GemmParams {
     const int32_t* tile_start;  // [groups + 1] prefix of 128-row tiles per group
     __half* out;                // [rows][N]; MODE 0 in the chunk element order
     const int32_t* out_rows;    // MODE 1: output row of each tile row (null: the tile row itself)
+    int out_cap;                // rows of `out` (rows mapped past it are not written)
     uint32_t* ctrl;             // error word
 };
 
@@ -376,7 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_pgemm(GemmParams p) {
                     for (int i = 0; i < 8; ++i)
                         o[i] = h2_bits(__floats2half2_rn(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1])));
                 }
-                if (orow < T.r1) {
+                if (orow < T.r1 && drow < p.out_cap) {
                     uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
                     d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
                     d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
@@ -1049,11 +1051,36 @@ static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t*
 }
 
 // Routed experts: rows A (fp16, chunk order) gathered through tok_of_pos,
-// hidden H, outputs Y (rows = permuted positions, or `out_rows` order).
-static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const __half* a16, __half* y,
+// hidden H, outputs Y (y_rows rows: at the permuted positions, or in
+// `out_rows` order).  Q4_K experts take the TMA-fed GEMM (k_tgemm.cu), whose
+// activation tiles must be contiguous: the rows are first gathered in
+// position order into Y itself, which the down GEMM overwrites afterwards.
+static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const __half* a16, __half* y, int y_rows,
                              const int32_t* out_rows, cudaStream_t s) {
     const int d = P.d;
+    const int h_rows = P.T * P.k;  // capacity of H (one row per pair)
     cudaError_t e;
+    if (P.gate.type == P.up.type && tgemm_supported(P.gate.type, 0, P.F, d) &&
+        tgemm_supported(P.down.type, 1, d, P.F)) {
+        if ((e = launch_gather_rows(a16, B.tok_of_pos, P.offsets + P.E, y_rows, d, y, s)) != cudaSuccess) return e;
+        TgArgs g{};
+        g.mode = 0;
+        g.a16 = y;
+        g.a_rows = static_cast<uint64_t>(y_rows);
+        g.w0 = P.gate.p;
+        g.w1 = P.up.p;
+        g.K = d;
+        g.p = TgParams{P.F, d, P.E, P.F, P.offsets, B.tile_start, B.H, nullptr, h_rows, P.ctrl};
+        if ((e = launch_tgemm(g, s)) != cudaSuccess) return e;
+        TgArgs dn{};
+        dn.mode = 1;
+        dn.a16 = B.H;
+        dn.a_rows = static_cast<uint64_t>(h_rows);
+        dn.w0 = P.down.p;
+        dn.K = P.F;
+        dn.p = TgParams{d, P.F, P.E, d, P.offsets, B.tile_start, y, out_rows, y_rows, P.ctrl};
+        return launch_tgemm(dn, s);
+    }
     pf::GemmParams g{};
     g.a16 = a16;
     g.a_rows = B.tok_of_pos;
@@ -1068,6 +1095,7 @@ static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const 
     g.grp_start = P.offsets;
     g.tile_start = B.tile_start;
     g.out = B.H;
+    g.out_cap = h_rows;
     g.ctrl = P.ctrl;
     if ((e = launch_pgemm<0>(g, s)) != cudaSuccess) return e;
     pf::GemmParams dn{};
@@ -1083,6 +1111,7 @@ static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const 
     dn.tile_start = B.tile_start;
     dn.out = y;
     dn.out_rows = out_rows;
+    dn.out_cap = y_rows;
     dn.ctrl = P.ctrl;
     return launch_pgemm<1>(dn, s);
 }
@@ -1093,7 +1122,26 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
                                      const int32_t* inv_perm, cudaStream_t s) {
     const int d = P.d;
     cudaError_t e;
-    if (P.has_shared) {
+    if (P.has_shared && P.sgate.type == P.sup.type && tgemm_supported(P.sgate.type, 0, P.Fs, d) &&
+        tgemm_supported(P.sdown.type, 1, d, P.Fs)) {
+        TgArgs g{};
+        g.mode = 0;
+        g.a16 = B.X16;
+        g.a_rows = static_cast<uint64_t>(P.T);
+        g.w0 = P.sgate.p;
+        g.w1 = P.sup.p;
+        g.K = d;
+        g.p = TgParams{P.Fs, d, 1, P.Fs, B.sh_grp, B.sh_tiles, B.Hs, nullptr, P.T, P.ctrl};
+        if ((e = launch_tgemm(g, s)) != cudaSuccess) return e;
+        TgArgs dn{};
+        dn.mode = 1;
+        dn.a16 = B.Hs;
+        dn.a_rows = static_cast<uint64_t>(P.T);
+        dn.w0 = P.sdown.p;
+        dn.K = P.Fs;
+        dn.p = TgParams{d, P.Fs, 1, d, B.sh_grp, B.sh_tiles, B.Ys, nullptr, P.T, P.ctrl};
+        if ((e = launch_tgemm(dn, s)) != cudaSuccess) return e;
+    } else if (P.has_shared) {
         pf::GemmParams gs{};
         gs.a16 = B.X16;
         gs.w0 = P.sgate.p;
@@ -1107,6 +1155,7 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
         gs.grp_start = B.sh_grp;
         gs.tile_start = B.sh_tiles;
         gs.out = B.Hs;
+        gs.out_cap = P.T;
         gs.ctrl = P.ctrl;
         if ((e = launch_pgemm<0>(gs, s)) != cudaSuccess) return e;
         pf::GemmParams ds{};
@@ -1121,6 +1170,7 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
         ds.grp_start = B.sh_grp;
         ds.tile_start = B.sh_tiles;
         ds.out = B.Ys;
+        ds.out_cap = P.T;
         ds.ctrl = P.ctrl;
         if ((e = launch_pgemm<1>(ds, s)) != cudaSuccess) return e;
     }
@@ -1134,7 +1184,7 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     cudaError_t e;
     if ((e = pf_route(P, B, s)) != cudaSuccess) return e;
     if ((e = pf_dispatch(P.topk_idx, P.T, P.k, P.E, P.offsets, P.perm, P.inv_perm, B, s)) != cudaSuccess) return e;
-    if ((e = pf_routed(P, B, B.X16, B.Y, nullptr, s)) != cudaSuccess) return e;
+    if ((e = pf_routed(P, B, B.X16, B.Y, P.T * P.k, nullptr, s)) != cudaSuccess) return e;
     return pf_shared_combine(P, B, B.Y, P.inv_perm, s);
 }
 
@@ -1147,11 +1197,11 @@ cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStr
 // that number for every expert-sorted pair; outputs y [pairs][d] fp16 in that
 // order.
 cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
-                              const int32_t* qmap, int32_t* out_pos, __half* y, cudaStream_t s) {
+                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, cudaStream_t s) {
     cudaError_t e;
     if ((e = pf_dispatch(meta, P.T, P.k, P.E, P.offsets, P.perm, P.inv_perm, B, s, qmap, out_pos)) != cudaSuccess)
         return e;
-    return pf_routed(P, B, x16, y, out_pos, s);
+    return pf_routed(P, B, x16, y, y_rows, out_pos, s);
 }
 
 // Shared expert and combine of T local tokens; the routed outputs of pair

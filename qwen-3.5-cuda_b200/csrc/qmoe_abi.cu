@@ -16,7 +16,7 @@ bool prefill_supported(const DecodeParams& P);
 cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
-                              const int32_t* qmap, int32_t* out_pos, __half* y, cudaStream_t s);
+                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, cudaStream_t s);
 cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
                               const int32_t* pair_pos, cudaStream_t s);
 size_t ep_dispatch_scratch_bytes(int T, int G);
@@ -384,12 +384,12 @@ size_t qmoe_ep_rows_workspace_size(const qmoe_dims* D, int max_rows) {
     return ep_rows_layout(*D, max_rows).total;
 }
 
-int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n, void* y,
-                    void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n,
+                    int n_pairs, void* y, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     int st;
     if (!B || (st = check_dims(D))) return B ? st : QMOE_ERR_ARG;
-    if (n < 0) return QMOE_ERR_ARG;
-    if (n == 0) return QMOE_OK;
+    if (n < 0 || n_pairs < 0 || static_cast<int64_t>(n_pairs) > static_cast<int64_t>(n) * D->top_k) return QMOE_ERR_ARG;
+    if (n == 0 || n_pairs == 0) return QMOE_OK;
     if (!x16 || !meta || !y || !ws) return QMOE_ERR_ARG;
     if (!aligned16(x16) || !aligned16(y) || !aligned16(ws)) return QMOE_ERR_ALIGN;
     if (D->top_k > 8) return QMOE_ERR_UNSUPPORTED;
@@ -423,7 +423,7 @@ int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, co
     cudaError_t e = launch_ep_qmap(meta, n, D->top_k, reinterpret_cast<int32_t*>(w + L.qblk), qmap, s);
     if (e == cudaSuccess)
         e = launch_ep_experts(P, pb, static_cast<const __half*>(x16), meta, qmap,
-                              reinterpret_cast<int32_t*>(w + L.out_pos), static_cast<__half*>(y), s);
+                              reinterpret_cast<int32_t*>(w + L.out_pos), static_cast<__half*>(y), n_pairs, s);
     return cuda_status(e);
 }
 

@@ -24,7 +24,7 @@ NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler"
            "--expt-relaxed-constexpr", f"-I{CSRC}", f"-I{INCLUDE}"]
 # k_synth must not contract multiply-adds (bit-identical host/device synth)
 PER_FILE = {"k_synth.cu": ["-fmad=false"]}
-CU_SOURCES = ["k_decode.cu", "k_gemv.cu", "k_synth.cu", "k_dispatch.cu", "k_prefill.cu", "k_ep.cu", "qmoe_abi.cu"]
+CU_SOURCES = ["k_decode.cu", "k_gemv.cu", "k_synth.cu", "k_dispatch.cu", "k_prefill.cu", "k_tgemm.cu", "k_ep.cu", "qmoe_abi.cu"]
 CPP_SOURCES = ["synth_host.cpp"]
 
 

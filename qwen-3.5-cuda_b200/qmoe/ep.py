@@ -160,7 +160,7 @@ class CudaBackend:
             stream = torch.cuda.current_stream().cuda_stream
             _lib.check(_lib.lib().qmoe_ep_experts(
                 ctypes.byref(self.local_blk), ctypes.byref(self.local_dims), rows.data_ptr(), meta.data_ptr(), n,
-                y.data_ptr(), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts")
+                n_pairs, y.data_ptr(), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts")
         return y
 
     def combine(self, y, pair_pos, residual=None):

@@ -101,7 +101,7 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias):
         y = torch.empty((npairs, d), dtype=torch.float16, device="cuda")
         if nr:
             _lib.check(L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), send_rows[r0:r0 + nr].data_ptr(),
-                                         send_meta[r0:r0 + nr].data_ptr(), nr, y.data_ptr(), rws.data_ptr(),
+                                         send_meta[r0:r0 + nr].data_ptr(), nr, npairs, y.data_ptr(), rws.data_ptr(),
                                          rws_bytes, None), "ep_experts")
         chunks.append(y)
         r0 += nr
@@ -127,9 +127,12 @@ def test_ep_argument_checks(cuda):
     y = torch.empty_like(rows)
     meta = torch.zeros((16, 4), dtype=torch.int32, device="cuda")
     # zero rows is a no-op, too small a workspace is refused, decode-sized routing is refused
-    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), None, None, 0, None, None, 0, None) == _lib.QMOE_OK
-    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), meta.data_ptr(), 16, y.data_ptr(),
-                             rws.data_ptr(), 1024, None) == _lib.QMOE_ERR_WORKSPACE
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), None, None, 0, 0, None, None, 0, None) == _lib.QMOE_OK
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), meta.data_ptr(), 16, 16,
+                             y.data_ptr(), rws.data_ptr(), 1024, None) == _lib.QMOE_ERR_WORKSPACE
+    # more pairs than the rows' slots can hold is an argument error
+    assert L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), rows.data_ptr(), meta.data_ptr(), 16, 65,
+                             y.data_ptr(), rws.data_ptr(), rws_bytes, None) == _lib.QMOE_ERR_ARG
     ws_bytes = L.qmoe_workspace_size(ctypes.byref(dc), 64)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     x = torch.zeros((8, 512), dtype=torch.float32, device="cuda")
