@@ -599,7 +599,7 @@ __global__ void __launch_bounds__(256) k_perm_rows(const uint8_t* __restrict__ r
 namespace rt {
 constexpr int TT = 64, TE = 32, ROWS = TT + TE, NSTG = 4;
 template <int CH>
-constexpr int rs() { return 8 * CH + 4; }  // padded row stride in floats (rows land on distinct bank groups)
+__host__ __device__ constexpr int rs() { return 8 * CH + 4; }  // padded row stride in floats (rows land on distinct bank groups)
 template <int CH>
 constexpr size_t smem_bytes() { return static_cast<size_t>(NSTG) * ROWS * rs<CH>() * sizeof(float); }
 

@@ -54,7 +54,9 @@ constexpr int THREADS = (WARP_EPI + 4) * 32;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t IDESC = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 
-constexpr size_t smem_bytes() { return 1024 + OFF_BAR + 256; }
+constexpr int MAX_GROUPS = kMaxExperts;     // group tables staged in shared memory
+constexpr uint32_t OFF_TAB = OFF_BAR + 256;  // tile_start[groups + 1], grp_start[groups + 1]
+constexpr size_t smem_bytes() { return 1024 + OFF_TAB + 2 * (MAX_GROUPS + 1) * sizeof(int32_t); }
 
 // shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (tile bases are 1024-byte aligned)
@@ -104,7 +106,9 @@ __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint3
 // Sub-block h (0: low nibbles, 1: high) of group g of one Q4_K super-block
 // (raw row in shared memory) -> 32 fp16 values = chunks 4h..4h+3 of row r of
 // the operand slot (128-byte rows, chunk c stored at c ^ (r % 8)).
-__device__ __forceinline__ void dq_sub(uint32_t raw, int g, int h, uint32_t brow, int r) {
+template <int H>
+__device__ __forceinline__ void dq_sub(uint32_t raw, int g, uint32_t brow, int r) {
+    constexpr int h = H;
     const uint4 hd = lds128(raw);
     const uint4 q0 = lds128(raw + 16 + 32 * g);
     const uint4 q1 = lds128(raw + 32 + 32 * g);
@@ -129,19 +133,20 @@ __device__ __forceinline__ void dq_sub(uint32_t raw, int g, int h, uint32_t brow
 struct Tile {
     int g, mt, nt, r0, r1;
 };
-__device__ __forceinline__ Tile tile_of(const TgParams& p, int t, int nN) {
+// tile t -> (group, m tile, n tile, rows); ts / gs: the group tables in shared memory
+__device__ __forceinline__ Tile tile_of(const int32_t* ts, const int32_t* gs, int groups, int t, int nN) {
     Tile T;
     const int mi = t / nN;
     T.nt = t - mi * nN;
-    int lo = 0, hi = p.groups;  // largest g with tile_start[g] <= mi
+    int lo = 0, hi = groups;  // largest g with tile_start[g] <= mi
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (__ldg(p.tile_start + mid) <= mi) lo = mid; else hi = mid;
+        if (ts[mid] <= mi) lo = mid; else hi = mid;
     }
     T.g = lo;
-    T.mt = mi - __ldg(p.tile_start + lo);
-    T.r0 = __ldg(p.grp_start + lo) + T.mt * BM;
-    T.r1 = min(T.r0 + BM, __ldg(p.grp_start + lo + 1));
+    T.mt = mi - ts[lo];
+    T.r0 = gs[lo] + T.mt * BM;
+    T.r1 = min(T.r0 + BM, gs[lo + 1]);
     return T;
 }
 
@@ -160,11 +165,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
     uint64_t* acc_full = r_empty + NR;    // [2]
     uint64_t* acc_free = acc_full + 2;    // [2]
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acc_free + 2);
+    int32_t* s_ts = reinterpret_cast<int32_t*>(smem + OFF_TAB);
+    int32_t* s_gs = s_ts + MAX_GROUPS + 1;
     const uint32_t sbase = smem_u32(smem);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ncol = MODE == 0 ? BN / 2 : BN;  // output columns per tile
     const int nN = p.N / ncol, nKS = p.K / KS, nSB = p.K / SB_K;
     const int total = __ldg(p.tile_start + p.groups) * nN;
+    for (int i = tid; i <= p.groups; i += THREADS) {
+        s_ts[i] = __ldg(p.tile_start + i);
+        s_gs[i] = __ldg(p.grp_start + i);
+    }
 
     if (tid == 0) {
         for (int s = 0; s < NA; ++s) {
@@ -201,7 +212,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
             int step = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-                const Tile T = tile_of(p, t, nN);
+                const Tile T = tile_of(s_ts, s_gs, p.groups, t, nN);
                 for (int ks = 0; ks < nKS; ++ks, ++step) {
                     const int s = step % NA;
                     if (step >= NA && !(ok = mbar_wait(a_empty + s, ((step / NA) - 1) & 1, p.ctrl))) break;
@@ -218,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
             int step = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-                const Tile T = tile_of(p, t, nN);
+                const Tile T = tile_of(s_ts, s_gs, p.groups, t, nN);
                 for (int sb = 0; sb < nSB; ++sb, ++step) {
                     const int s = step % NR;
                     if (step >= NR && !(ok = mbar_wait(r_empty + s, ((step / NR) - 1) & 1, p.ctrl))) break;
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
     } else if (warp < WARP_MMA) {
         // ---------------- dequantisation ----------------
         const int i = tid - WARP_DQ * 32;  // 0..511
-        const int r = i >> 1, h = i & 1;   // weight row of the tile, sub-block of the slice
+        const int r = i & 255, h = i >> 8;  // weight row of the tile, sub-block of the slice (warp-uniform)
         int rstep = 0, bstep = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
@@ -249,7 +260,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
                 for (int g = 0; g < SB_K / KS; ++g, ++bstep) {
                     const int bs = bstep % NB;
                     if (bstep >= NB && !(ok = mbar_wait(b_empty + bs, ((bstep / NB) - 1) & 1, p.ctrl))) break;
-                    dq_sub(raw, g, h, sbase + OFF_B + bs * B_BYTES + r * 128, r);
+                    if (h == 0) dq_sub<0>(raw, g, sbase + OFF_B + bs * B_BYTES + r * 128, r);
+                    else dq_sub<1>(raw, g, sbase + OFF_B + bs * B_BYTES + r * 128, r);
                     fence_async_smem();  // generic stores -> visible to the tensor core
                     __syncwarp();
                     if (lane == 0) mbar_arrive(b_full + bs);
@@ -293,7 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 = tile rows
         int ti = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++ti) {
-            const Tile T = tile_of(p, t, nN);
+            const Tile T = tile_of(s_ts, s_gs, p.groups, t, nN);
             const int buf = ti & 1;
             if (!mbar_wait(acc_full + buf, (ti >> 1) & 1, p.ctrl)) break;
             tc_fence_after();
@@ -394,8 +406,10 @@ bool tgemm_supported(int wtype, int mode, int N, int K) {
     return wtype == T_Q4_K && K % tg::SB_K == 0 && N % (mode == 0 ? tg::BN / 2 : tg::BN) == 0 &&
            tmap_encoder() != nullptr;
 }
+static_assert(tg::smem_bytes() <= 227 * 1024, "k_tgemm shared memory");
 
 cudaError_t launch_tgemm(const TgArgs& a, cudaStream_t s) {
+    if (a.p.groups < 1 || a.p.groups > tg::MAX_GROUPS) return cudaErrorInvalidValue;
     CUtensorMap mA, mW0, mW1;
     const uint64_t wrow = static_cast<uint64_t>(a.K / tg::SB_K) * tg::SB_BYTES;
     const uint32_t wbox = a.mode == 0 ? tg::BN / 2 : tg::BN;
