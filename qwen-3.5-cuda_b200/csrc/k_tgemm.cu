@@ -103,31 +103,30 @@ __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint3
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
 
-// Sub-block h (0: low nibbles, 1: high) of group g of one Q4_K super-block
-// (raw row in shared memory) -> 32 fp16 values = chunks 4h..4h+3 of row r of
+// Sub-block H (0: low nibbles, 1: high) of group g of one Q4_K super-block
+// (raw row in shared memory) -> 32 fp16 values = chunks 4H..4H+3 of row r of
 // the operand slot (128-byte rows, chunk c stored at c ^ (r % 8)).
 template <int H>
 __device__ __forceinline__ void dq_sub(uint32_t raw, int g, uint32_t brow, int r) {
-    constexpr int h = H;
     const uint4 hd = lds128(raw);
     const uint4 q0 = lds128(raw + 16 + 32 * g);
     const uint4 q1 = lds128(raw + 32 + 32 * g);
     float sc, m;
-    kscale(hd.y, hd.z, hd.w, 2 * g + h, sc, m);
+    kscale(hd.y, hd.z, hd.w, 2 * g + H, sc, m);
     const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
     const __half2 a = __float2half2_rn(d * sc), nb = __float2half2_rn(-(dmin * m));
     const __half2 k1024 = __float2half2_rn(1024.0f);
-    const int sh = 4 * h;
+    const int sh = 4 * H;
     // half2(1024 + n(byte e), 1024 + n(byte e+2)): element order 0,2 / 1,3
     auto cvt = [&](uint32_t w) {
         const __half2 raw2 = bits_h2(((w >> sh) & 0x000F000Fu) | 0x64006400u);
         return h2_bits(__hfma2(__hsub2(raw2, k1024), a, nb));
     };
     const uint32_t x7 = static_cast<uint32_t>(r & 7);
-    sts128(brow + (((4 * h + 0) ^ x7) << 4), cvt(q0.x), cvt(q0.x >> 8), cvt(q0.y), cvt(q0.y >> 8));
-    sts128(brow + (((4 * h + 1) ^ x7) << 4), cvt(q0.z), cvt(q0.z >> 8), cvt(q0.w), cvt(q0.w >> 8));
-    sts128(brow + (((4 * h + 2) ^ x7) << 4), cvt(q1.x), cvt(q1.x >> 8), cvt(q1.y), cvt(q1.y >> 8));
-    sts128(brow + (((4 * h + 3) ^ x7) << 4), cvt(q1.z), cvt(q1.z >> 8), cvt(q1.w), cvt(q1.w >> 8));
+    sts128(brow + (((4 * H + 0) ^ x7) << 4), cvt(q0.x), cvt(q0.x >> 8), cvt(q0.y), cvt(q0.y >> 8));
+    sts128(brow + (((4 * H + 1) ^ x7) << 4), cvt(q0.z), cvt(q0.z >> 8), cvt(q0.w), cvt(q0.w >> 8));
+    sts128(brow + (((4 * H + 2) ^ x7) << 4), cvt(q1.x), cvt(q1.x >> 8), cvt(q1.y), cvt(q1.y >> 8));
+    sts128(brow + (((4 * H + 3) ^ x7) << 4), cvt(q1.z), cvt(q1.z >> 8), cvt(q1.w), cvt(q1.w >> 8));
 }
 
 struct Tile {
