@@ -10,7 +10,8 @@
 //   k_ep_hplace  positions: send row of (t, r) = rank offset + earlier blocks +
 //                earlier tokens of the block; the meta row (slot j -> local
 //                expert id or -1); pair_pos[t*k + j] = place of the pair in the
-//                returned outputs; then the block's warps copy the fp16 rows
+//                returned outputs; the source token of every send row
+//   k_ep_copy    the fp16 rows into the send buffer, all SMs
 // Receiving rank, from the meta rows of n received rows:
 //   k_ep_qcount / k_ep_qscan / k_ep_qmap
 //                the (row, slot) order number of every valid slot (-1 for the
@@ -83,8 +84,8 @@ __global__ void k_ep_hscan(int32_t* __restrict__ blk, int nb, int G, int32_t* __
 
 __global__ void __launch_bounds__(EPB) k_ep_hplace(const int32_t* __restrict__ idx, int T, int k, int eloc, int G,
                                                    const int32_t* __restrict__ blk, const int32_t* __restrict__ rank_off,
-                                                   const __half* __restrict__ x16, int d, __half* __restrict__ send_rows,
-                                                   int32_t* __restrict__ send_meta, int32_t* __restrict__ pair_pos) {
+                                                   int32_t* __restrict__ row_src, int32_t* __restrict__ send_meta,
+                                                   int32_t* __restrict__ pair_pos) {
     __shared__ int s_wrows[EPB / 32][kEpMaxRanks], s_wpairs[EPB / 32][kEpMaxRanks];
     __shared__ int2 s_copy[EPB * kEpMaxK];  // (source token, send row) of the block's rows
     __shared__ int s_ncopy;
@@ -155,13 +156,20 @@ __global__ void __launch_bounds__(EPB) k_ep_hplace(const int32_t* __restrict__ i
             if (j < k && (ids[j] < 0 || ep_rank_of(ids[j], eloc) >= G)) pair_pos[t * k + j] = -1;
     }
     __syncthreads();
-    // copy the block's rows: one warp per row, 16 bytes per lane and step
-    const int n = s_ncopy;
-    const int chunks = d / 8;
-    for (int i = warp; i < n; i += EPB / 32) {
-        const int2 cp = copies[i];
-        const uint4* src = reinterpret_cast<const uint4*>(x16 + static_cast<size_t>(cp.x) * d);
-        uint4* dst = reinterpret_cast<uint4*>(send_rows + static_cast<size_t>(cp.y) * d);
+    // the source token of every send row, for k_ep_copy
+    for (int i = threadIdx.x; i < s_ncopy; i += EPB) row_src[copies[i].y] = copies[i].x;
+}
+
+// send_rows[i] = x16[row_src[i]] for the n = counts[0..G) rows: one warp per
+// row, 16 bytes per lane and step, grid-stride over all SMs.
+__global__ void __launch_bounds__(256) k_ep_copy(const __half* __restrict__ x16, int d, const int32_t* __restrict__ row_src,
+                                                 const int32_t* __restrict__ counts, int G, __half* __restrict__ send_rows) {
+    int n = 0;
+    for (int r = 0; r < G; ++r) n += __ldg(counts + r);
+    const int lane = threadIdx.x & 31, chunks = d / 8;
+    for (int i = blockIdx.x * 8 + (threadIdx.x >> 5); i < n; i += gridDim.x * 8) {
+        const uint4* src = reinterpret_cast<const uint4*>(x16 + static_cast<size_t>(__ldg(row_src + i)) * d);
+        uint4* dst = reinterpret_cast<uint4*>(send_rows + static_cast<size_t>(i) * d);
         for (int c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
     }
 }
@@ -242,7 +250,9 @@ __global__ void __launch_bounds__(EPB) k_ep_qmap(const int32_t* __restrict__ met
 
 size_t ep_dispatch_scratch_bytes(int T, int G) {
     const size_t nb = (static_cast<size_t>(T) + EPB - 1) / EPB;
-    return align_up(nb * 2 * G * sizeof(int32_t), 256) + align_up(2 * G * sizeof(int32_t), 256);
+    const size_t rows = static_cast<size_t>(T) * (G < kEpMaxK ? G : kEpMaxK);
+    return align_up(nb * 2 * G * sizeof(int32_t), 256) + align_up(2 * G * sizeof(int32_t), 256) +
+           align_up(rows * sizeof(int32_t), 256);
 }
 
 bool ep_dispatch_supported(int k, int G) { return G >= 1 && G <= kEpMaxRanks && k >= 1 && k <= kEpMaxK; }
@@ -252,11 +262,17 @@ cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, c
                                void* scratch, cudaStream_t s) {
     const int nb = (T + EPB - 1) / EPB, eloc = E / G;
     int32_t* blk = static_cast<int32_t*>(scratch);
-    int32_t* rank_off = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) +
-                                                   align_up(static_cast<size_t>(nb) * 2 * G * sizeof(int32_t), 256));
+    const size_t o1 = align_up(static_cast<size_t>(nb) * 2 * G * sizeof(int32_t), 256);
+    int32_t* rank_off = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + o1);
+    int32_t* row_src = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + o1 +
+                                                  align_up(2 * G * sizeof(int32_t), 256));
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     k_ep_hcount<<<nb, EPB, 0, s>>>(idx, T, k, eloc, G, blk);
     k_ep_hscan<<<1, 64, 0, s>>>(blk, nb, G, counts, rank_off);
-    k_ep_hplace<<<nb, EPB, 0, s>>>(idx, T, k, eloc, G, blk, rank_off, x16, d, send_rows, send_meta, pair_pos);
+    k_ep_hplace<<<nb, EPB, 0, s>>>(idx, T, k, eloc, G, blk, rank_off, row_src, send_meta, pair_pos);
+    k_ep_copy<<<4 * sms, 256, 0, s>>>(x16, d, row_src, counts, G, send_rows);
     return cudaGetLastError();
 }
 
