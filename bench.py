@@ -434,9 +434,11 @@ def measure_ep(world, rank, dims):
     peak = _bf16_peak()
     reps = 10
     res = {"config": f"config5: T={T} tokens x d={d}, {E} Q4_K experts ({E // world} per GPU), top-{k}, "
-                     f"{world} GPU(s), one fp16 row per (token, rank) over NCCL all-to-all" if world > 1 else
+                     f"{world} GPU(s), one fp16 row per (token, rank) over NCCL all-to-all, outputs back by copy-engine "
+                     f"writes into the owning rank's buffer over NVLink (CUDA IPC)" if world > 1 else
                      f"config5 at 1 GPU: T={T} tokens x d={d}, {E} Q4_K experts, top-{k}, one block_forward",
            "n_gpus": world, "scaling": "strong", "routings": {}}
+    backends = []
     for routing in ("uniform", "zipf"):
         c = blk.c()
         if routing == "zipf":
@@ -458,7 +460,8 @@ def measure_ep(world, rank, dims):
             want_idx = ws[off:off + T * k * 4].view(torch.int32).view(T, k)[rank * Tl:(rank + 1) * Tl].clone()
             lb, ld = ep.local_block(c, dc, rank, world)
             be = ep.CudaBackend(c, lb, dc, ld, world, max_tokens=Tl, max_rows=2 * Tl)
-            moe = ep.ExpertParallelMoE(be, E, k, d)
+            moe = ep.ExpertParallelMoE(be, E, k, d, direct=True)
+            backends.append(be)
             got = moe.forward(x)
             idx = be.topk_idx()
             want = out_all[rank * Tl:(rank + 1) * Tl]
@@ -493,6 +496,12 @@ def measure_ep(world, rank, dims):
         res["routings"][routing] = entry
     res["peak"] = {"bf16_tflops": peak[0], "kind": peak[1]}
     res["expert_gflop"] = round(flop / 1e9, 1)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        for be in backends:
+            be.close()
+        dist.barrier()
     return res
 
 

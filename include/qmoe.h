@@ -224,6 +224,36 @@ QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max
 QMOE_API int qmoe_ep_experts(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
                      const int32_t* meta, int n_rows, int n_pairs, void* y_pairs, void* workspace,
                      size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Direct return of the expert outputs (expert parallelism over peer memory,
+ * e.g. NVLink): instead of y_pairs, the down GEMM's epilogue stores the output
+ * of received pair q (q in [pair_start[s], pair_start[s+1]) came from rank s)
+ * into rank s's return buffer dst[s] at row dst_row[s] + q - pair_start[s],
+ * i.e. where rank s's pair_pos expects it (dst_row[s] = the pairs rank s sends
+ * to the ranks before this one).  dst[s] is a peer pointer (qmoe_peer_open),
+ * this rank's own buffer for s = itself.  The caller orders the writes before
+ * rank s's qmoe_ep_combine (kernel completion, then any cross-rank barrier on
+ * the streams, e.g. a one-element NCCL all-reduce).  Q4_K experts only. */
+typedef struct qmoe_ep_return {
+    int32_t n_ranks;          /* G <= 32 */
+    int32_t pair_start[33];
+    void* dst[32];
+    int64_t dst_row[32];
+} qmoe_ep_return;
+QMOE_API int qmoe_ep_experts_return(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
+                            const int32_t* meta, int n_rows, const qmoe_ep_return* ret, void* workspace,
+                            size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Device memory another process on this node can map (CUDA IPC): allocate
+ * with a 64-byte handle to hand to the peers, open a peer's handle, close an
+ * opened mapping, free an allocation. */
+QMOE_API int qmoe_peer_alloc(size_t bytes, void** ptr, void* handle64);
+QMOE_API int qmoe_peer_open(const void* handle64, void** ptr);
+QMOE_API int qmoe_peer_close(void* ptr);
+QMOE_API int qmoe_peer_free(void* ptr);
+/* Stream-ordered device copy (one cudaMemcpyAsync; a peer pointer from
+ * qmoe_peer_open makes it a copy-engine transfer over NVLink). */
+QMOE_API int qmoe_copy_async(void* dst, const void* src, size_t bytes, qmoe_stream_t stream);
 QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs,
                      const int32_t* pair_pos, int T, const float* residual, float* out, void* workspace,
                      size_t workspace_bytes, qmoe_stream_t stream);

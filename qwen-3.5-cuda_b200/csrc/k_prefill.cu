@@ -1056,21 +1056,23 @@ static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t*
 // activation tiles must be contiguous: the rows are first gathered in
 // position order into Y itself, which the down GEMM overwrites afterwards.
 static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const __half* a16, __half* y, int y_rows,
-                             const int32_t* out_rows, cudaStream_t s) {
+                             const int32_t* out_rows, cudaStream_t s, const TgScatter* sc = nullptr,
+                             __half* xp = nullptr) {
     const int d = P.d;
     const int h_rows = P.T * P.k;  // capacity of H (one row per pair)
     cudaError_t e;
     if (P.gate.type == P.up.type && tgemm_supported(P.gate.type, 0, P.F, d) &&
         tgemm_supported(P.down.type, 1, d, P.F)) {
-        if ((e = launch_gather_rows(a16, B.tok_of_pos, P.offsets + P.E, y_rows, d, y, s)) != cudaSuccess) return e;
+        if (!xp) xp = y;  // the gathered rows live in Y until the down GEMM overwrites it
+        if ((e = launch_gather_rows(a16, B.tok_of_pos, P.offsets + P.E, y_rows, d, xp, s)) != cudaSuccess) return e;
         TgArgs g{};
         g.mode = 0;
-        g.a16 = y;
+        g.a16 = xp;
         g.a_rows = static_cast<uint64_t>(y_rows);
         g.w0 = P.gate.p;
         g.w1 = P.up.p;
         g.K = d;
-        g.p = TgParams{P.F, d, P.E, P.F, P.offsets, B.tile_start, B.H, nullptr, h_rows, P.ctrl};
+        g.p = TgParams{P.F, d, P.E, P.F, P.offsets, B.tile_start, B.H, nullptr, h_rows, P.ctrl, {}};
         if ((e = launch_tgemm(g, s)) != cudaSuccess) return e;
         TgArgs dn{};
         dn.mode = 1;
@@ -1078,9 +1080,11 @@ static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const 
         dn.a_rows = static_cast<uint64_t>(h_rows);
         dn.w0 = P.down.p;
         dn.K = P.F;
-        dn.p = TgParams{d, P.F, P.E, d, P.offsets, B.tile_start, y, out_rows, y_rows, P.ctrl};
+        dn.p = TgParams{d, P.F, P.E, d, P.offsets, B.tile_start, y, out_rows, y_rows, P.ctrl, {}};
+        if (sc) dn.p.sc = *sc;
         return launch_tgemm(dn, s);
     }
+    if (sc) return cudaErrorNotSupported;  // direct return needs the Q4_K GEMM
     pf::GemmParams g{};
     g.a16 = a16;
     g.a_rows = B.tok_of_pos;
@@ -1131,7 +1135,7 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
         g.w0 = P.sgate.p;
         g.w1 = P.sup.p;
         g.K = d;
-        g.p = TgParams{P.Fs, d, 1, P.Fs, B.sh_grp, B.sh_tiles, B.Hs, nullptr, P.T, P.ctrl};
+        g.p = TgParams{P.Fs, d, 1, P.Fs, B.sh_grp, B.sh_tiles, B.Hs, nullptr, P.T, P.ctrl, {}};
         if ((e = launch_tgemm(g, s)) != cudaSuccess) return e;
         TgArgs dn{};
         dn.mode = 1;
@@ -1139,7 +1143,7 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
         dn.a_rows = static_cast<uint64_t>(P.T);
         dn.w0 = P.sdown.p;
         dn.K = P.Fs;
-        dn.p = TgParams{d, P.Fs, 1, d, B.sh_grp, B.sh_tiles, B.Ys, nullptr, P.T, P.ctrl};
+        dn.p = TgParams{d, P.Fs, 1, d, B.sh_grp, B.sh_tiles, B.Ys, nullptr, P.T, P.ctrl, {}};
         if ((e = launch_tgemm(dn, s)) != cudaSuccess) return e;
     } else if (P.has_shared) {
         pf::GemmParams gs{};
@@ -1195,13 +1199,15 @@ cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStr
 // meta [n][k] (local expert id per slot or -1; P.k = k, P.E = local experts);
 // qmap [n*k] numbers the valid slots in (row, slot) order, out_pos receives
 // that number for every expert-sorted pair; outputs y [pairs][d] fp16 in that
-// order.
+// order, or (sc) straight into the owning ranks' return buffers; xp holds the
+// rows gathered in pair order.
 cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
-                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, cudaStream_t s) {
+                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, const TgScatter* sc,
+                              __half* xp, cudaStream_t s) {
     cudaError_t e;
     if ((e = pf_dispatch(meta, P.T, P.k, P.E, P.offsets, P.perm, P.inv_perm, B, s, qmap, out_pos)) != cudaSuccess)
         return e;
-    return pf_routed(P, B, x16, y, y_rows, out_pos, s);
+    return pf_routed(P, B, x16, y, y_rows, out_pos, s, sc, xp);
 }
 
 // Shared expert and combine of T local tokens; the routed outputs of pair

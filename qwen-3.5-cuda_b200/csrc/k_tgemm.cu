@@ -312,6 +312,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
             const uint32_t tl = tmem + buf * BN + (static_cast<uint32_t>(32 * quarter) << 16);
             const int drow = (p.out_rows && orow < T.r1) ? __ldg(p.out_rows + orow) : orow;
             __half* dst = p.out + static_cast<size_t>(drow) * p.N + T.nt * ncol;
+            bool to_peer = false;
+            if (MODE == 1 && p.sc.n_src > 0) {  // the rank the row came from, and its row there
+                int src = 0;
+                while (src + 1 < p.sc.n_src && drow >= p.sc.start[src + 1]) ++src;
+                to_peer = drow >= p.sc.start[src] && drow < p.sc.start[p.sc.n_src];
+                dst = p.sc.dst[src] + (static_cast<size_t>(p.sc.dst_row[src]) + (drow - p.sc.start[src])) * p.N +
+                      T.nt * ncol;
+            }
             for (int c0 = 0; c0 < ncol; c0 += 16) {
                 uint32_t a[16];
                 tmem_ld16(tl + c0, a);
@@ -340,12 +348,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_tgemm(const __grid_constant__ CU
                     for (int k = 0; k < 8; ++k)
                         o[k] = h2_bits(__floats2half2_rn(__uint_as_float(a[2 * k]), __uint_as_float(a[2 * k + 1])));
                 }
-                if (orow < T.r1 && drow < p.out_cap) {
+                if (orow < T.r1 && (MODE == 1 && p.sc.n_src > 0 ? to_peer : drow < p.out_cap)) {
                     uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
                     d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
                     d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
                 }
             }
+            if (MODE == 1 && p.sc.n_src > 0) __threadfence_system();  // peer stores performed before completion
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_free + buf);

@@ -5,6 +5,7 @@
 #include <cstring>
 #include "qmoe_dev.cuh"
 #include "qmoe_internal.h"
+#include "qmoe_tgemm.h"
 
 namespace qmoe {
 cudaError_t launch_router(const DecodeParams& P, cudaStream_t s);
@@ -16,7 +17,8 @@ bool prefill_supported(const DecodeParams& P);
 cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
-                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, cudaStream_t s);
+                              const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, const TgScatter* sc,
+                              __half* xp, cudaStream_t s);
 cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
                               const int32_t* pair_pos, cudaStream_t s);
 size_t ep_dispatch_scratch_bytes(int T, int G);
@@ -384,14 +386,15 @@ size_t qmoe_ep_rows_workspace_size(const qmoe_dims* D, int max_rows) {
     return ep_rows_layout(*D, max_rows).total;
 }
 
-int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n,
-                    int n_pairs, void* y, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+static int ep_experts_impl(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n,
+                           int n_pairs, void* y, const TgScatter* sc, void* ws, size_t ws_bytes,
+                           qmoe_stream_t stream) {
     int st;
     if (!B || (st = check_dims(D))) return B ? st : QMOE_ERR_ARG;
     if (n < 0 || n_pairs < 0 || static_cast<int64_t>(n_pairs) > static_cast<int64_t>(n) * D->top_k) return QMOE_ERR_ARG;
     if (n == 0 || n_pairs == 0) return QMOE_OK;
-    if (!x16 || !meta || !y || !ws) return QMOE_ERR_ARG;
-    if (!aligned16(x16) || !aligned16(y) || !aligned16(ws)) return QMOE_ERR_ALIGN;
+    if (!x16 || !meta || (!y && !sc) || !ws) return QMOE_ERR_ARG;
+    if (!aligned16(x16) || (y && !aligned16(y)) || !aligned16(ws)) return QMOE_ERR_ALIGN;
     if (D->top_k > 8) return QMOE_ERR_UNSUPPORTED;
     const uint64_t d = D->d_model, E = D->num_experts, F = D->expert_dim;
     if ((st = check_tensor(B->gate_exps, E * F * d, expert_type))) return st;
@@ -413,6 +416,9 @@ int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, co
     P.perm = reinterpret_cast<int32_t*>(w + L.perm);
     P.inv_perm = reinterpret_cast<int32_t*>(w + L.inv_perm);
     if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
+    if (sc && !(P.gate.type == P.up.type && tgemm_supported(P.gate.type, 0, P.F, P.d) &&
+                tgemm_supported(P.down.type, 1, P.d, P.F)))
+        return QMOE_ERR_UNSUPPORTED;
     PrefillBufs pb{};
     pb.tok_of_pos = reinterpret_cast<int32_t*>(w + L.tok_of_pos);
     pb.tile_start = reinterpret_cast<int32_t*>(w + L.tile_start);
@@ -423,8 +429,62 @@ int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, co
     cudaError_t e = launch_ep_qmap(meta, n, D->top_k, reinterpret_cast<int32_t*>(w + L.qblk), qmap, s);
     if (e == cudaSuccess)
         e = launch_ep_experts(P, pb, static_cast<const __half*>(x16), meta, qmap,
-                              reinterpret_cast<int32_t*>(w + L.out_pos), static_cast<__half*>(y), n_pairs, s);
+                              reinterpret_cast<int32_t*>(w + L.out_pos), static_cast<__half*>(y), n_pairs, sc,
+                              reinterpret_cast<__half*>(w + L.Xp), s);
     return cuda_status(e);
+}
+
+int qmoe_ep_experts(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n,
+                    int n_pairs, void* y, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    return ep_experts_impl(B, D, x16, meta, n, n_pairs, y, nullptr, ws, ws_bytes, stream);
+}
+
+int qmoe_ep_experts_return(const qmoe_block* B, const qmoe_dims* D, const void* x16, const int32_t* meta, int n,
+                           const qmoe_ep_return* ret, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    if (!ret || ret->n_ranks < 1 || ret->n_ranks > 32) return QMOE_ERR_ARG;
+    TgScatter sc{};
+    sc.n_src = ret->n_ranks;
+    for (int r = 0; r <= ret->n_ranks; ++r) {
+        sc.start[r] = ret->pair_start[r];
+        if (r > 0 && ret->pair_start[r] < ret->pair_start[r - 1]) return QMOE_ERR_ARG;
+    }
+    if (ret->pair_start[0] != 0) return QMOE_ERR_ARG;
+    for (int r = 0; r < ret->n_ranks; ++r) {
+        const bool has = ret->pair_start[r + 1] > ret->pair_start[r];
+        if (has && (!ret->dst[r] || !aligned16(ret->dst[r]) || ret->dst_row[r] < 0)) return QMOE_ERR_ARG;
+        sc.dst[r] = static_cast<__half*>(ret->dst[r]);
+        sc.dst_row[r] = ret->dst_row[r];
+    }
+    return ep_experts_impl(B, D, x16, meta, n, ret->pair_start[ret->n_ranks], nullptr, &sc, ws, ws_bytes, stream);
+}
+
+int qmoe_peer_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return QMOE_ERR_ARG;
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+    if (e != cudaSuccess && *ptr) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+    }
+    return cuda_status(e);
+}
+
+int qmoe_peer_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return QMOE_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int qmoe_peer_close(void* ptr) { return ptr ? cuda_status(cudaIpcCloseMemHandle(ptr)) : QMOE_ERR_ARG; }
+
+int qmoe_peer_free(void* ptr) { return ptr ? cuda_status(cudaFree(ptr)) : QMOE_ERR_ARG; }
+
+int qmoe_copy_async(void* dst, const void* src, size_t bytes, qmoe_stream_t stream) {
+    if (bytes == 0) return QMOE_OK;
+    if (!dst || !src) return QMOE_ERR_ARG;
+    return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos, int T,

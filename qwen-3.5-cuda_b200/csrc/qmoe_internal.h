@@ -115,9 +115,10 @@ inline WsLayout ws_layout(const qmoe_dims& D, int T) {
 
 // Workspace of qmoe_ep_experts for up to n received rows of k slots (the
 // expert-parallel receiver): dispatch of the (row, slot) pairs over the local
-// experts, the GEMM tile plan and the hidden vectors of the pairs.
+// experts, the GEMM tile plan, the rows gathered in pair order and the hidden
+// vectors of the pairs.
 struct EpRowsLayout {
-    size_t ctrl, offsets, perm, inv_perm, tok_of_pos, out_pos, qmap, qblk, tile_start, disp, H, total;
+    size_t ctrl, offsets, perm, inv_perm, tok_of_pos, out_pos, qmap, qblk, tile_start, disp, H, Xp, total;
 };
 inline EpRowsLayout ep_rows_layout(const qmoe_dims& D, int n) {
     EpRowsLayout L{};
@@ -135,6 +136,7 @@ inline EpRowsLayout ep_rows_layout(const qmoe_dims& D, int n) {
     L.tile_start = take(sizeof(int32_t) * (E + 1));
     L.disp = take(sizeof(int32_t) * E * ((static_cast<size_t>(n) + 63) / 64));
     L.H = take(2 * P * static_cast<size_t>(D.expert_dim));
+    L.Xp = take(2 * P * static_cast<size_t>(D.d_model));  // received rows gathered in pair order
     L.total = o;
     return L;
 }

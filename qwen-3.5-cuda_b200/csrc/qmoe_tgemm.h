@@ -7,6 +7,16 @@
 
 namespace qmoe {
 
+// MODE 1 outputs sent to the ranks that own the rows (expert parallelism):
+// row q of the received pairs, q in [start[s], start[s+1]), goes to
+// dst[s] + (dst_row[s] + q - start[s]) * N.  n_src = 0: rows go to `out`.
+struct TgScatter {
+    int n_src;
+    int32_t start[33];
+    __half* dst[32];
+    int64_t dst_row[32];
+};
+
 struct TgParams {
     int N, K;                   // output columns (F or d), reduction length
     int groups;                 // experts (1 for the shared expert)
@@ -17,6 +27,7 @@ struct TgParams {
     const int32_t* out_rows;    // output row of each A row (null: the same row)
     int out_cap;                // rows of `out` (rows mapped past it are not written)
     uint32_t* ctrl;             // error word
+    TgScatter sc;               // MODE 1 only
 };
 
 struct TgArgs {

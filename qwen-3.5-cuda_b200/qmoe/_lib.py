@@ -42,6 +42,11 @@ class QmoeBlock(ctypes.Structure):
                 ("shared_up", QmoeTensor), ("shared_down", QmoeTensor), ("expert_bias", c_void_p)]
 
 
+class QmoeEpReturn(ctypes.Structure):
+    _fields_ = [("n_ranks", c_int32), ("pair_start", c_int32 * 33), ("dst", c_void_p * 32),
+                ("dst_row", ctypes.c_int64 * 32)]
+
+
 # (name, restype, argtypes) for every symbol declared in include/qmoe.h
 SIGNATURES = [
     ("qmoe_abi_version", c_int, []),
@@ -70,6 +75,13 @@ SIGNATURES = [
     ("qmoe_ep_rows_workspace_size", c_size_t, [POINTER(QmoeDims), c_int]),
     ("qmoe_ep_experts", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_int, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),
+    ("qmoe_ep_experts_return", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int,
+                                       POINTER(QmoeEpReturn), c_void_p, c_size_t, c_void_p]),
+    ("qmoe_peer_alloc", c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    ("qmoe_peer_open", c_int, [c_void_p, POINTER(c_void_p)]),
+    ("qmoe_peer_close", c_int, [c_void_p]),
+    ("qmoe_peer_free", c_int, [c_void_p]),
+    ("qmoe_copy_async", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     ("qmoe_ep_combine", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),
     ("qmoe_block_kernel_count", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int]),

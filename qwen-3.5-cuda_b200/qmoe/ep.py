@@ -18,7 +18,14 @@ Per rank and call (T local tokens):
                rows and meta rows (all-to-all with those splits)
   4. experts   the rank's experts on the received rows (qmoe_ep_experts,
                tcgen05 grouped GEMMs), outputs in (row, slot) order
-  5. return    outputs back with the reverse all-to-all
+  5. return    outputs back with the reverse all-to-all -- or, with
+               direct=True, over peer memory (CUDA IPC mappings): the down
+               GEMM's epilogue stores this rank's own pairs straight into its
+               return buffer and the other ranks' pairs contiguously into a
+               local staging buffer (qmoe_ep_experts_return), the copy
+               engines push each staged chunk into its owner's return buffer
+               (one cudaMemcpyAsync per peer), and a one-element all-reduce
+               orders those writes before the combine
   6. combine   shared expert and the slot-ordered combine of the local tokens
                through pair_pos (qmoe_ep_combine)
 The exchange runs on torch.distributed (NCCL on GPUs, gloo in the CPU
@@ -43,7 +50,7 @@ def shard_bounds(E: int, world: int, rank: int) -> tuple[int, int]:
 class ExpertParallelMoE:
     """One MoE layer sharded over the ranks of `group` (torch.distributed)."""
 
-    def __init__(self, backend, E: int, k: int, d: int, group=None):
+    def __init__(self, backend, E: int, k: int, d: int, group=None, direct: bool = False):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
@@ -52,6 +59,39 @@ class ExpertParallelMoE:
         self.backend = backend
         self.E, self.k, self.d = E, k, d
         self.lo, self.hi = shard_bounds(E, self.world, self.rank)
+        self.direct = direct
+        if direct:
+            backend.setup_direct(self.dist, group, self.world, self.rank)
+
+    def gather_counts(self, counts):
+        """counts [2G] of every rank -> host matrix C[s] = rank s's counts."""
+        import torch
+        G = self.world
+        out = torch.empty(G * 2 * G, dtype=counts.dtype, device=counts.device)
+        self.dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
+        flat = out.tolist()
+        return [flat[s * 2 * G:(s + 1) * 2 * G] for s in range(G)]
+
+    def _forward_direct(self, x, residual):
+        be, G, me = self.backend, self.world, self.rank
+        be.route(x)
+        send_rows, send_meta, counts, pair_pos = be.dispatch(G)
+        C = self.gather_counts(counts)  # the one host synchronisation of the call
+        s_rows = C[me][:G]
+        r_rows = [C[s][me] for s in range(G)]
+        r_pairs = [C[s][G + me] for s in range(G)]
+        ns = sum(s_rows)
+        recv_rows = self._a2a(send_rows[:ns], s_rows, r_rows)
+        recv_meta = self._a2a(send_meta[:ns], s_rows, r_rows)
+        pair_start = [0]
+        for c in r_pairs:
+            pair_start.append(pair_start[-1] + c)
+        # rank s's buffer holds its pairs grouped by rank: this rank's chunk
+        # starts after the pairs s sends to the ranks before it
+        dst_row = [sum(C[s][G + r] for r in range(me)) for s in range(G)]
+        be.experts_return(recv_rows, recv_meta, pair_start, dst_row)
+        be.barrier()  # every rank's outputs for this rank have landed
+        return be.combine(be.returned(sum(C[me][G:])), pair_pos, residual)
 
     def _a2a(self, send, send_counts, recv_counts):
         import torch
@@ -73,6 +113,8 @@ class ExpertParallelMoE:
 
     def forward(self, x, residual=None):
         """x: [T, d] local tokens.  Returns out [T, d] (float32)."""
+        if self.direct:
+            return self._forward_direct(x, residual)
         be = self.backend
         be.route(x)
         send_rows, send_meta, counts, pair_pos = be.dispatch(self.world)
@@ -163,6 +205,92 @@ class CudaBackend:
                 n_pairs, y.data_ptr(), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts")
         return y
 
+    # ---- direct return over peer memory ----
+    def setup_direct(self, dist, group, world: int, rank: int) -> None:
+        """Allocate this rank's return buffer (one fp16 row per pair of its
+        tokens) as IPC-shareable memory and map every peer's."""
+        import torch
+        L = _lib.lib()
+        self.dist, self.group = dist, group
+        rows = (self.pair_pos.numel())  # max_tokens * k
+        self.ret_bytes = rows * self.dims.d_model * 2
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.check(L.qmoe_peer_alloc(self.ret_bytes, ctypes.byref(ptr), handle), "peer_alloc")
+        self.ret_ptr = ptr.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peer_ptrs = []
+        for s, h in enumerate(handles):
+            if s == rank:
+                self.peer_ptrs.append(self.ret_ptr)
+                continue
+            q = ctypes.c_void_p()
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            _lib.check(L.qmoe_peer_open(hb, ctypes.byref(q)), "peer_open")
+            self.peer_ptrs.append(q.value)
+        self.rank_ = rank
+        self.stage = None
+        self._flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def experts_return(self, rows, meta, pair_start, dst_row) -> None:
+        """This rank's experts on the received rows; the outputs of rank s's
+        pairs land in rank s's return buffer from row dst_row[s] on."""
+        import torch
+        n = rows.shape[0]
+        if n == 0:
+            return
+        if n > self.max_rows:
+            self._rows_ws(n)
+        L = _lib.lib()
+        row_bytes = self.dims.d_model * 2
+        n_pairs = pair_start[-1]
+        if self.stage is None or self.stage.shape[0] < n_pairs:
+            self.stage = torch.empty((n_pairs, self.dims.d_model), dtype=torch.float16, device="cuda")
+        ret = _lib.QmoeEpReturn()
+        ret.n_ranks = len(dst_row)
+        for i, v in enumerate(pair_start):
+            ret.pair_start[i] = v
+        for s, r0 in enumerate(dst_row):  # own pairs: final place; the others: staged in received order
+            own = s == self.rank_
+            ret.dst[s] = self.ret_ptr if own else self.stage.data_ptr()
+            ret.dst_row[s] = r0 if own else pair_start[s]
+        stream = torch.cuda.current_stream().cuda_stream
+        _lib.check(L.qmoe_ep_experts_return(
+            ctypes.byref(self.local_blk), ctypes.byref(self.local_dims), rows.data_ptr(), meta.data_ptr(), n,
+            ctypes.byref(ret), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts_return")
+        for s, r0 in enumerate(dst_row):
+            nb = (pair_start[s + 1] - pair_start[s]) * row_bytes
+            if s != self.rank_ and nb:
+                _lib.check(L.qmoe_copy_async(self.peer_ptrs[s] + r0 * row_bytes,
+                                             self.stage.data_ptr() + pair_start[s] * row_bytes, nb, stream),
+                           "copy_async")
+
+    def barrier(self) -> None:
+        """Stream-ordered barrier over the ranks (a one-element all-reduce):
+        the peers' return writes into this rank's buffer are complete."""
+        self.dist.all_reduce(self._flag, group=self.group)
+
+    def returned(self, n_pairs: int):
+        """This rank's return buffer as [n_pairs][d] fp16."""
+        import torch
+        if n_pairs == 0:
+            return torch.zeros((1, self.dims.d_model), dtype=torch.float16, device="cuda")
+        buf = torch.cuda.current_device()
+        t = _DevicePtr(self.ret_ptr, n_pairs * self.dims.d_model * 2, buf)
+        return torch.as_tensor(t, device="cuda").view(torch.float16).view(n_pairs, self.dims.d_model)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after the last call)."""
+        L = _lib.lib()
+        for s, ptr in enumerate(getattr(self, "peer_ptrs", [])):
+            if s != self.rank_:
+                L.qmoe_peer_close(ptr)
+        if getattr(self, "ret_ptr", None):
+            L.qmoe_peer_free(self.ret_ptr)
+            self.ret_ptr = None
+        self.peer_ptrs = []
+
     def combine(self, y, pair_pos, residual=None):
         import torch
         out = torch.empty((self.T, self.dims.d_model), dtype=torch.float32, device="cuda")
@@ -174,6 +302,15 @@ class CudaBackend:
             None if residual is None else residual.data_ptr(), out.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
             stream), "ep_combine")
         return out
+
+
+class _DevicePtr:
+    """A raw device allocation seen by torch through __cuda_array_interface__
+    (bytes, read-write); the memory stays owned by the caller."""
+
+    def __init__(self, ptr: int, nbytes: int, device: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
 
 
 def local_block(blk: "_lib.QmoeBlock", dims, rank: int, world: int) -> tuple["_lib.QmoeBlock", "_lib.QmoeDims"]:

@@ -84,6 +84,26 @@ class FakeBackend:
         y = rows.numpy()[r] * _scale(self.E)[self.lo + e][:, None] if n_pairs else np.zeros((0, D), np.float32)
         return torch.from_numpy(np.ascontiguousarray(y, dtype=np.float32))
 
+    # direct return: every rank's return buffer is a slice of one shared-memory
+    # array (standing in for the peer mappings of the GPU path)
+    def setup_direct(self, dist, group, world, rank):
+        from multiprocessing import shared_memory
+        self.dist, self.rank = dist, rank
+        self.shm = shared_memory.SharedMemory(name=self.shm_name)
+        self.bufs = np.ndarray((world, self.cap, D), dtype=np.float32, buffer=self.shm.buf)
+
+    def experts_return(self, rows, meta, pair_start, dst_row):
+        y = self.experts(rows, meta, pair_start[-1]).numpy()
+        for s in range(len(dst_row)):
+            q0, q1 = pair_start[s], pair_start[s + 1]
+            self.bufs[s, dst_row[s]:dst_row[s] + q1 - q0] = y[q0:q1]
+
+    def barrier(self):
+        self.dist.barrier()
+
+    def returned(self, n_pairs):
+        return torch.from_numpy(self.bufs[self.rank, :n_pairs].copy())
+
     def combine(self, y, pair_pos, residual=None):
         T = self.x.shape[0]
         yv, pp = y.numpy(), pair_pos.numpy()
@@ -95,14 +115,15 @@ class FakeBackend:
         return torch.from_numpy(out)
 
 
-def _worker(rank, world, port, E, token_counts, seed, q):
+def _worker(rank, world, port, E, token_counts, seed, q, shm_name=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         lo, hi = ep.shard_bounds(E, world, rank)
         be = FakeBackend(E, lo, seed)
-        moe = ep.ExpertParallelMoE(be, E, K, D)
+        be.shm_name, be.cap = shm_name, max(token_counts) * K
+        moe = ep.ExpertParallelMoE(be, E, K, D, direct=shm_name is not None)
         x = np.random.default_rng(100 + rank).standard_normal((token_counts[rank], D)).astype(np.float32)
         out = moe.forward(torch.from_numpy(x)).numpy()
         ref = _reference(x, E, seed)
@@ -111,17 +132,25 @@ def _worker(rank, world, port, E, token_counts, seed, q):
         dist.destroy_process_group()
 
 
-def _run(world, E, token_counts, seed=5):
+def _run(world, E, token_counts, seed=5, direct=False):
+    from multiprocessing import shared_memory
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, E, token_counts, seed, q)) for r in range(world)]
-    for p in ps:
-        p.start()
-    for p in ps:
-        p.join(120)
-    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
-    res = sorted(q.get() for _ in range(world))
+    shm = shared_memory.SharedMemory(create=True, size=world * max(token_counts) * K * D * 4) if direct else None
+    try:
+        ps = [ctx.Process(target=_worker, args=(r, world, port, E, token_counts, seed, q, shm.name if shm else None))
+              for r in range(world)]
+        for p in ps:
+            p.start()
+        for p in ps:
+            p.join(120)
+        assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+        res = sorted(q.get() for _ in range(world))
+    finally:
+        if shm is not None:
+            shm.close()
+            shm.unlink()
     return res
 
 
@@ -142,9 +171,10 @@ def test_shard_bounds():
         ep.shard_bounds(256, 3, 0)
 
 
+@pytest.mark.parametrize("direct", [False, True], ids=["all_to_all_return", "direct_return"])
 @pytest.mark.parametrize("world,E,tokens", [(2, 8, [13, 9]), (4, 16, [5, 0, 11, 3])])
-def test_exchange_matches_single_process(world, E, tokens):
-    res = _run(world, E, tokens)
+def test_exchange_matches_single_process(world, E, tokens, direct):
+    res = _run(world, E, tokens, direct=direct)
     for rank, err, shape, _ in res:
         assert shape == (tokens[rank], D)
         assert err < 1e-5, (rank, err)

@@ -59,8 +59,10 @@ def _reference(blk, x, residual):
     return out, idx
 
 
-@pytest.mark.parametrize("G,types,bias", [(2, synth.Q4K_TYPES, False), (8, synth.MIXED_TYPES, True)])
-def test_ep_shards_on_one_gpu(cuda, G, types, bias):
+@pytest.mark.parametrize("G,types,bias,direct", [(2, synth.Q4K_TYPES, False, False), (8, synth.MIXED_TYPES, True, False),
+                                                (4, synth.Q4K_TYPES, True, True)],
+                         ids=["g2_q4k", "g8_mixed_bias", "g4_q4k_direct_return"])
+def test_ep_shards_on_one_gpu(cuda, G, types, bias, direct):
     """Every rank of a G-way split on one GPU: the send layout bit-exact
     against tests/ep_plan_ref.py, each rank's chunk through its local experts,
     the chunks' outputs concatenated in rank order as the all-to-all returns
@@ -92,6 +94,8 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias):
     assert torch.equal(send_rows[:ns], x16[torch.from_numpy(tok).cuda()])
 
     chunks, r0 = [], 0
+    total = int((idx >= 0).sum())
+    y_direct = torch.full((total, d), float("nan"), dtype=torch.float16, device="cuda")
     for r in range(G):
         nr, npairs = int(cnt[r]), int(cnt[G + r])
         lb, ld = ep.local_block(full, dc, r, G)
@@ -99,13 +103,23 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias):
         rws = torch.full((rws_bytes,), 0xA5, dtype=torch.uint8, device="cuda")
         _lib.check(L.qmoe_workspace_init(rws.data_ptr(), rws_bytes, None))
         y = torch.empty((npairs, d), dtype=torch.float16, device="cuda")
-        if nr:
+        if nr and direct:
+            # rank r returns its outputs straight into the home buffer (one source rank here)
+            ret = _lib.QmoeEpReturn()
+            ret.n_ranks = 1
+            ret.pair_start[0], ret.pair_start[1] = 0, npairs
+            ret.dst[0] = y_direct.data_ptr()
+            ret.dst_row[0] = int(sum(int(cnt[G + q]) for q in range(r)))
+            _lib.check(L.qmoe_ep_experts_return(ctypes.byref(lb), ctypes.byref(ld), send_rows[r0:r0 + nr].data_ptr(),
+                                                send_meta[r0:r0 + nr].data_ptr(), nr, ctypes.byref(ret),
+                                                rws.data_ptr(), rws_bytes, None), "ep_experts_return")
+        elif nr:
             _lib.check(L.qmoe_ep_experts(ctypes.byref(lb), ctypes.byref(ld), send_rows[r0:r0 + nr].data_ptr(),
                                          send_meta[r0:r0 + nr].data_ptr(), nr, npairs, y.data_ptr(), rws.data_ptr(),
                                          rws_bytes, None), "ep_experts")
         chunks.append(y)
         r0 += nr
-    y_ret = torch.cat(chunks)
+    y_ret = y_direct if direct else torch.cat(chunks)
     assert y_ret.shape[0] == int((idx >= 0).sum())
     got = be.combine(y_ret, pair_pos, residual)
     torch.cuda.synchronize()
@@ -146,7 +160,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, t_local, q):
+def _nccl_worker(rank, world, port, t_local, q, direct):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -166,19 +180,24 @@ def _nccl_worker(rank, world, port, t_local, q):
         lb, ld = ep.local_block(full, dc, rank, world)
         be = ep.CudaBackend(full, lb, dc, ld, world, max_tokens=t_local, max_rows=t_local)
         _poison(be)
-        moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model)
+        moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model, direct=direct)
         got = moe.forward(x, res)
+        got = moe.forward(x, res)  # a second call reuses the return buffers
         idx = be.topk_idx()
         torch.cuda.synchronize()
         ids_equal = bool(torch.equal(idx, want_idx[sl]))
         max_err = float((got - want[sl]).abs().max())
         q.put((rank, ids_equal, max_err, bool(torch.equal(got, want[sl]))))
         dist.barrier()
+        torch.cuda.synchronize()
+        be.close()
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_nccl(cuda):
+@pytest.mark.parametrize("direct", [False, True], ids=["all_to_all_return", "direct_return"])
+def test_ep_nccl(cuda, direct):
     import torch
     import torch.multiprocessing as mp
     world = min(torch.cuda.device_count(), 8)
@@ -187,7 +206,7 @@ def test_ep_nccl(cuda):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_nccl_worker, args=(r, world, port, 160, q)) for r in range(world)]
+    ps = [ctx.Process(target=_nccl_worker, args=(r, world, port, 160, q, direct)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
