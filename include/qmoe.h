@@ -257,6 +257,15 @@ QMOE_API int qmoe_copy_async(void* dst, const void* src, size_t bytes, qmoe_stre
 QMOE_API int qmoe_ep_combine(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs,
                      const int32_t* pair_pos, int T, const float* residual, float* out, void* workspace,
                      size_t workspace_bytes, qmoe_stream_t stream);
+/* qmoe_ep_combine in two halves, so that the shared expert can run while the
+ * routed outputs are still travelling: qmoe_ep_shared (needs only the
+ * qmoe_ep_route workspace), then qmoe_ep_combine_routed (same arguments as
+ * qmoe_ep_combine). */
+QMOE_API int qmoe_ep_shared(const qmoe_block* blk, const qmoe_dims* dims, int T, void* workspace,
+                    size_t workspace_bytes, qmoe_stream_t stream);
+QMOE_API int qmoe_ep_combine_routed(const qmoe_block* blk, const qmoe_dims* dims, const void* y_pairs,
+                            const int32_t* pair_pos, int T, const float* residual, float* out, void* workspace,
+                            size_t workspace_bytes, qmoe_stream_t stream);
 
 /* Number of kernels one qmoe_block_forward call with these arguments launches
  * (for profiling and launch accounting); negative status on bad arguments. */

@@ -1122,8 +1122,7 @@ static cudaError_t pf_routed(const DecodeParams& P, const PrefillBufs& B, const 
 
 // Shared expert over all T tokens (rows of X16), then the combine of the
 // routed outputs Y (at inv_perm positions, or in pair order when null).
-static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B, const __half* Y,
-                                     const int32_t* inv_perm, cudaStream_t s) {
+static cudaError_t pf_shared(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) {
     const int d = P.d;
     cudaError_t e;
     if (P.has_shared && P.sgate.type == P.sup.type && tgemm_supported(P.sgate.type, 0, P.Fs, d) &&
@@ -1178,9 +1177,20 @@ static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B
         ds.ctrl = P.ctrl;
         if ((e = launch_pgemm<1>(ds, s)) != cudaSuccess) return e;
     }
-    k_pf_combine<<<P.T, 256, 0, s>>>(Y, B.Ys, inv_perm, P.topk_w, P.logits, P.residual, P.out, d, P.E, P.k,
+    return cudaSuccess;
+}
+
+static cudaError_t pf_combine(const DecodeParams& P, const PrefillBufs& B, const __half* Y, const int32_t* inv_perm,
+                              cudaStream_t s) {
+    k_pf_combine<<<P.T, 256, 0, s>>>(Y, B.Ys, inv_perm, P.topk_w, P.logits, P.residual, P.out, P.d, P.E, P.k,
                                      P.has_shared);
     return cudaGetLastError();
+}
+
+static cudaError_t pf_shared_combine(const DecodeParams& P, const PrefillBufs& B, const __half* Y,
+                                     const int32_t* inv_perm, cudaStream_t s) {
+    cudaError_t e = pf_shared(P, B, s);
+    return e != cudaSuccess ? e : pf_combine(P, B, Y, inv_perm, s);
 }
 
 // The whole block for T tokens through the prefill kernels.
@@ -1211,10 +1221,17 @@ cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const
 }
 
 // Shared expert and combine of T local tokens; the routed outputs of pair
-// (t, j) are row pair_pos[t*k + j] of y_pairs (-1: none).
+// (t, j) are row pair_pos[t*k + j] of y_pairs (-1: none).  The two halves
+// separately: the shared expert (needs only the routing call's workspace), the
+// combine (after the shared half).
 cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
                               const int32_t* pair_pos, cudaStream_t s) {
     return pf_shared_combine(P, B, y_pairs, pair_pos, s);
+}
+cudaError_t launch_ep_shared(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) { return pf_shared(P, B, s); }
+cudaError_t launch_ep_combine_routed(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
+                                     const int32_t* pair_pos, cudaStream_t s) {
+    return pf_combine(P, B, y_pairs, pair_pos, s);
 }
 
 }  // namespace qmoe

@@ -21,6 +21,9 @@ cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const
                               __half* xp, cudaStream_t s);
 cudaError_t launch_ep_combine(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
                               const int32_t* pair_pos, cudaStream_t s);
+cudaError_t launch_ep_shared(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
+cudaError_t launch_ep_combine_routed(const DecodeParams& P, const PrefillBufs& B, const __half* y_pairs,
+                                     const int32_t* pair_pos, cudaStream_t s);
 size_t ep_dispatch_scratch_bytes(int T, int G);
 bool ep_dispatch_supported(int k, int G);
 cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, const __half* x16, int d,
@@ -487,18 +490,39 @@ int qmoe_copy_async(void* dst, const void* src, size_t bytes, qmoe_stream_t stre
     return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos, int T,
-                    const float* residual, float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+static int ep_combine_impl(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos,
+                           int T, const float* residual, float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream,
+                           int part) {
     int st = check_common(B, D, T, ws, ws_bytes, 1 << 30);
     if (st) return st;
     if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
-    if (!y_pairs || !pair_pos || !out) return QMOE_ERR_ARG;
-    if (!aligned16(y_pairs)) return QMOE_ERR_ALIGN;
+    if (part != 1 && (!y_pairs || !pair_pos || !out)) return QMOE_ERR_ARG;
+    if (part != 1 && !aligned16(y_pairs)) return QMOE_ERR_ALIGN;
     if (ws_layout(*D, T).total > ws_bytes) return QMOE_ERR_WORKSPACE;
     DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
     if (!prefill_supported(P)) return QMOE_ERR_UNSUPPORTED;
-    return cuda_status(launch_ep_combine(P, prefill_bufs(*D, T, ws), static_cast<const __half*>(y_pairs), pair_pos,
-                                         reinterpret_cast<cudaStream_t>(stream)));
+    const PrefillBufs pb = prefill_bufs(*D, T, ws);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const __half* y = static_cast<const __half*>(y_pairs);
+    switch (part) {
+        case 1: return cuda_status(launch_ep_shared(P, pb, s));
+        case 2: return cuda_status(launch_ep_combine_routed(P, pb, y, pair_pos, s));
+        default: return cuda_status(launch_ep_combine(P, pb, y, pair_pos, s));
+    }
+}
+
+int qmoe_ep_combine(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos, int T,
+                    const float* residual, float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    return ep_combine_impl(B, D, y_pairs, pair_pos, T, residual, out, ws, ws_bytes, stream, 0);
+}
+
+int qmoe_ep_shared(const qmoe_block* B, const qmoe_dims* D, int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    return ep_combine_impl(B, D, nullptr, nullptr, T, nullptr, nullptr, ws, ws_bytes, stream, 1);
+}
+
+int qmoe_ep_combine_routed(const qmoe_block* B, const qmoe_dims* D, const void* y_pairs, const int32_t* pair_pos,
+                           int T, const float* residual, float* out, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    return ep_combine_impl(B, D, y_pairs, pair_pos, T, residual, out, ws, ws_bytes, stream, 2);
 }
 
 int qmoe_block_kernel_count(const qmoe_block* B, const qmoe_dims* D, int T) {

@@ -82,6 +82,9 @@ SIGNATURES = [
     ("qmoe_peer_close", c_int, [c_void_p]),
     ("qmoe_peer_free", c_int, [c_void_p]),
     ("qmoe_copy_async", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("qmoe_ep_shared", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int, c_void_p, c_size_t, c_void_p]),
+    ("qmoe_ep_combine_routed", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_void_p,
+                                       c_void_p, c_void_p, c_size_t, c_void_p]),
     ("qmoe_ep_combine", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),
     ("qmoe_block_kernel_count", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_int]),

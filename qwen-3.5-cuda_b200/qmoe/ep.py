@@ -90,8 +90,9 @@ class ExpertParallelMoE:
         # starts after the pairs s sends to the ranks before it
         dst_row = [sum(C[s][G + r] for r in range(me)) for s in range(G)]
         be.experts_return(recv_rows, recv_meta, pair_start, dst_row)
-        be.barrier()  # every rank's outputs for this rank have landed
-        return be.combine(be.returned(sum(C[me][G:])), pair_pos, residual)
+        # push the staged outputs, barrier (every rank's outputs for this rank
+        # have landed), shared expert meanwhile, combine
+        return be.finish(sum(C[me][G:]), pair_pos, residual)
 
     def _a2a(self, send, send_counts, recv_counts):
         import torch
@@ -231,6 +232,7 @@ class CudaBackend:
             self.peer_ptrs.append(q.value)
         self.rank_ = rank
         self.stage = None
+        self.side = torch.cuda.Stream()
         self._flag = torch.zeros(1, dtype=torch.int32, device="cuda")
 
     def experts_return(self, rows, meta, pair_start, dst_row) -> None:
@@ -259,17 +261,37 @@ class CudaBackend:
         _lib.check(L.qmoe_ep_experts_return(
             ctypes.byref(self.local_blk), ctypes.byref(self.local_dims), rows.data_ptr(), meta.data_ptr(), n,
             ctypes.byref(ret), self.rws.data_ptr(), self.rws_bytes, stream), "ep_experts_return")
-        for s, r0 in enumerate(dst_row):
-            nb = (pair_start[s + 1] - pair_start[s]) * row_bytes
-            if s != self.rank_ and nb:
-                _lib.check(L.qmoe_copy_async(self.peer_ptrs[s] + r0 * row_bytes,
-                                             self.stage.data_ptr() + pair_start[s] * row_bytes, nb, stream),
-                           "copy_async")
+        self.pushes = [(self.peer_ptrs[s] + r0 * row_bytes, self.stage.data_ptr() + pair_start[s] * row_bytes,
+                        (pair_start[s + 1] - pair_start[s]) * row_bytes)
+                       for s, r0 in enumerate(dst_row) if s != self.rank_ and pair_start[s + 1] > pair_start[s]]
 
-    def barrier(self) -> None:
-        """Stream-ordered barrier over the ranks (a one-element all-reduce):
-        the peers' return writes into this rank's buffer are complete."""
-        self.dist.all_reduce(self._flag, group=self.group)
+    def finish(self, n_pairs: int, pair_pos, residual=None):
+        """Push the staged outputs to their ranks (copy engines) and barrier on
+        a side stream while the shared expert runs on this stream; then the
+        combine of this rank's tokens from its return buffer."""
+        import torch
+        L = _lib.lib()
+        main = torch.cuda.current_stream()
+        ready = torch.cuda.Event()
+        ready.record(main)
+        with torch.cuda.stream(self.side):
+            self.side.wait_event(ready)
+            for dst, src, nb in getattr(self, "pushes", []):
+                _lib.check(L.qmoe_copy_async(dst, src, nb, self.side.cuda_stream), "copy_async")
+            self.dist.all_reduce(self._flag, group=self.group)
+            landed = torch.cuda.Event()
+            landed.record(self.side)
+        self.pushes = []
+        _lib.check(L.qmoe_ep_shared(ctypes.byref(self.blk), ctypes.byref(self.dims), self.T, self.ws.data_ptr(),
+                                    self.ws_bytes, main.cuda_stream), "ep_shared")
+        main.wait_event(landed)
+        out = torch.empty((self.T, self.dims.d_model), dtype=torch.float32, device="cuda")
+        y = self.returned(n_pairs)
+        _lib.check(L.qmoe_ep_combine_routed(
+            ctypes.byref(self.blk), ctypes.byref(self.dims), y.data_ptr(), pair_pos.data_ptr(), self.T,
+            None if residual is None else residual.data_ptr(), out.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+            main.cuda_stream), "ep_combine_routed")
+        return out
 
     def returned(self, n_pairs: int):
         """This rank's return buffer as [n_pairs][d] fp16."""

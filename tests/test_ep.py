@@ -93,16 +93,17 @@ class FakeBackend:
         self.bufs = np.ndarray((world, self.cap, D), dtype=np.float32, buffer=self.shm.buf)
 
     def experts_return(self, rows, meta, pair_start, dst_row):
-        y = self.experts(rows, meta, pair_start[-1]).numpy()
-        for s in range(len(dst_row)):
-            q0, q1 = pair_start[s], pair_start[s + 1]
-            self.bufs[s, dst_row[s]:dst_row[s] + q1 - q0] = y[q0:q1]
+        self.pending = (self.experts(rows, meta, pair_start[-1]).numpy(), pair_start, dst_row)
 
-    def barrier(self):
+    def finish(self, n_pairs, pair_pos, residual=None):
+        if getattr(self, "pending", None) is not None:
+            y, pair_start, dst_row = self.pending
+            for s in range(len(dst_row)):
+                q0, q1 = pair_start[s], pair_start[s + 1]
+                self.bufs[s, dst_row[s]:dst_row[s] + q1 - q0] = y[q0:q1]
+        self.pending = None
         self.dist.barrier()
-
-    def returned(self, n_pairs):
-        return torch.from_numpy(self.bufs[self.rank, :n_pairs].copy())
+        return self.combine(torch.from_numpy(self.bufs[self.rank, :n_pairs].copy()), pair_pos, residual)
 
     def combine(self, y, pair_pos, residual=None):
         T = self.x.shape[0]
