@@ -704,13 +704,43 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill (config 4) and mixed decode (config 3) lines")
+    ap.add_argument("--only", choices=["prefill", "config3", "ep"],
+                    help="run one extra measurement alone and print its object (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args.only)
     else:
         run_ours(args)
+
+
+def run_only(what):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qmoe import synth
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dims = synth.Dims()
+    if what == "prefill":
+        res = measure_prefill(synth.Block(dims, synth.Q4K_TYPES, seed=SEED, layer=0, device="cuda"), dims)
+    elif what == "config3":
+        res = measure_config3(dims)
+    else:
+        res = measure_ep(world, rank, dims)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({what: res}), flush=True)
 
 
 if __name__ == "__main__":
