@@ -815,12 +815,19 @@ __global__ void __launch_bounds__(256) k_pf_count(const int32_t* __restrict__ id
 __global__ void __launch_bounds__(256) k_pf_scan(int32_t* __restrict__ counts, int nb, int E, int32_t* __restrict__ offsets) {
     __shared__ int s_wsum[8];
     const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    constexpr int U = 16;  // loads issued ahead of the dependent stores
     int run = 0;
     if (e < E)
-        for (int b = 0; b < nb; ++b) {
-            const int c = counts[b * E + e];
-            counts[b * E + e] = run;
-            run += c;
+        for (int b0 = 0; b0 < nb; b0 += U) {
+            int c[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) c[j] = b0 + j < nb ? counts[(b0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+                if (b0 + j < nb) {
+                    counts[(b0 + j) * E + e] = run;
+                    run += c[j];
+                }
         }
     int inc = run;
 #pragma unroll
@@ -838,7 +845,14 @@ __global__ void __launch_bounds__(256) k_pf_scan(int32_t* __restrict__ counts, i
     const int off = base + inc - run;
     if (e < E) {
         offsets[e] = off;
-        for (int b = 0; b < nb; ++b) counts[b * E + e] += off;
+        for (int b0 = 0; b0 < nb; b0 += U) {
+            int c[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) c[j] = b0 + j < nb ? counts[(b0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+                if (b0 + j < nb) counts[(b0 + j) * E + e] = c[j] + off;
+        }
     }
     if (e == 0) offsets[E] = total;
 }
