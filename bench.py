@@ -395,6 +395,7 @@ def zipf_bias(E, k, d, sigma=0.02, s=ZIPF_S, seed=SEED + 4, sample=4096, iters=6
         cnt = np.bincount(idx.ravel(), minlength=E).astype(np.float64)
         b += 0.5 * (np.log(target) - np.log(np.maximum(cnt, 0.5)))
         b -= b.max()
+    zipf_bias.target = target / sample  # expected pairs per token and expert (the placement's load model)
     return b.astype(np.float32)
 
 
@@ -458,8 +459,15 @@ def measure_ep(world, rank, dims):
             p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_TOPK_IDX)
             off = p - ws.data_ptr()
             want_idx = ws[off:off + T * k * 4].view(torch.int32).view(T, k)[rank * Tl:(rank + 1) * Tl].clone()
-            lb, ld = ep.local_block(c, dc, rank, world)
-            be = ep.CudaBackend(c, lb, dc, ld, world, max_tokens=Tl, max_rows=2 * Tl)
+            pl = None
+            if routing == "zipf":  # experts placed to balance the expected (calibrated) per-rank load
+                pl = ep.balanced_placement(zipf_bias.target.tolist(), world)
+                lb, ld, keep = ep.local_block_placed(c, dc, ep.experts_of_rank(pl, world, rank))
+                entry["placement"] = "balanced by the calibrated Zipf(1.1) expert load"
+            else:
+                lb, ld = ep.local_block(c, dc, rank, world)
+                entry["placement"] = "contiguous"
+            be = ep.CudaBackend(c, lb, dc, ld, world, max_tokens=Tl, max_rows=2 * Tl, placement=pl)
             moe = ep.ExpertParallelMoE(be, E, k, d, direct=True)
             backends.append(be)
             got = moe.forward(x)

@@ -209,6 +209,10 @@ QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int
  *   qmoe_ep_combine   shared expert and combine of the T local tokens:
  *                     out[t] = residual[t] + sum_j w[t][j] y[pair_pos[t*k+j]]
  *                              + sigmoid(shared gate) * shared(x_in[t])
+ * placement (device int32 [E], optional): expert e lives on rank
+ * placement[e] / (E/G) as local expert placement[e] % (E/G) -- a permutation
+ * of 0..E-1 that balances expected load; NULL = contiguous shards (rank r owns
+ * experts r*E/G .. (r+1)*E/G - 1).
  * send_rows holds at most T * min(G, k) rows (send_meta the same number of
  * k-int rows); `scratch` comes from qmoe_ep_dispatch_scratch_size.  local_blk
  * holds the rank's slices of the expert tensors (router and shared tensors are
@@ -217,9 +221,9 @@ QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int
 QMOE_API int qmoe_ep_route(const qmoe_block* blk, const qmoe_dims* dims, const float* x, const float* norm_weight,
                    float eps, int T, void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 QMOE_API size_t qmoe_ep_dispatch_scratch_size(int T, int G);
-QMOE_API int qmoe_ep_dispatch(const qmoe_dims* dims, int T, int G, void* workspace, size_t workspace_bytes,
-                      void* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos, void* scratch,
-                      size_t scratch_bytes, qmoe_stream_t stream);
+QMOE_API int qmoe_ep_dispatch(const qmoe_dims* dims, int T, int G, const int32_t* placement, void* workspace,
+                      size_t workspace_bytes, void* send_rows, int32_t* send_meta, int32_t* counts,
+                      int32_t* pair_pos, void* scratch, size_t scratch_bytes, qmoe_stream_t stream);
 QMOE_API size_t qmoe_ep_rows_workspace_size(const qmoe_dims* local_dims, int max_rows);
 QMOE_API int qmoe_ep_experts(const qmoe_block* local_blk, const qmoe_dims* local_dims, const void* x16_rows,
                      const int32_t* meta, int n_rows, int n_pairs, void* y_pairs, void* workspace,

@@ -6,7 +6,7 @@
 # points).  oracle/ref_shim/qwen_ref_prelude.hpp is force-included to stand in
 # for the reference's cuda_utils.hpp, whose macros do not compile as shipped
 # (it also supplies the CUDA_CHECK that ops.cu uses without including it).
-# Usage: oracle/build_ref.sh [reference_root]   (default /root/reference)
+# Usage: oracle/build_ref.sh [reference_root]   (default: the development checkout)
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 ref="${1:-/root/reference}"

@@ -1,8 +1,8 @@
 // Expert-parallel exchange layout (no counterpart in the reference, which
 // runs the MoE block on one GPU, src/layer_moe.cpp:98-154).
 //
-// Sending rank, from the top-k of its T tokens (experts sharded contiguously,
-// Eloc = E / G per rank):
+// Sending rank, from the top-k of its T tokens (Eloc = E / G experts per
+// rank: contiguous shards, or any placement permutation):
 //   k_ep_hcount  per 256-token block and rank: rows (tokens with at least one
 //                expert on the rank) and pairs (token, slot) going there
 //   k_ep_hscan   exclusive scan of those over the blocks, per rank; totals and
@@ -30,8 +30,16 @@ constexpr int kEpMaxK = 8;  // top-k slots per token on this path
 
 __device__ __forceinline__ int ep_rank_of(int e, int eloc) { return e >= 0 ? e / eloc : -1; }
 
-__global__ void __launch_bounds__(EPB) k_ep_hcount(const int32_t* __restrict__ idx, int T, int k, int eloc, int G,
-                                                   int32_t* __restrict__ blk) {
+// Expert id as placed on the ranks: slot p = r*Eloc + local id on rank r
+// (placement: a permutation of the experts; null = contiguous shards).
+__device__ __forceinline__ int ep_placed(const int32_t* __restrict__ idx, const int32_t* __restrict__ placement,
+                                         int i) {
+    const int e = __ldg(idx + i);
+    return (placement && e >= 0) ? __ldg(placement + e) : e;
+}
+
+__global__ void __launch_bounds__(EPB) k_ep_hcount(const int32_t* __restrict__ idx, const int32_t* __restrict__ placement,
+                                                   int T, int k, int eloc, int G, int32_t* __restrict__ blk) {
     __shared__ int s_cnt[2 * kEpMaxRanks];
     if (threadIdx.x < 2 * G) s_cnt[threadIdx.x] = 0;
     __syncthreads();
@@ -39,7 +47,7 @@ __global__ void __launch_bounds__(EPB) k_ep_hcount(const int32_t* __restrict__ i
     if (t < T) {
         uint32_t mask = 0;
         for (int j = 0; j < k; ++j) {
-            const int r = ep_rank_of(__ldg(idx + t * k + j), eloc);
+            const int r = ep_rank_of(ep_placed(idx, placement, t * k + j), eloc);
             if (r >= 0 && r < G) {
                 mask |= 1u << r;
                 atomicAdd(s_cnt + G + r, 1);
@@ -82,7 +90,8 @@ __global__ void k_ep_hscan(int32_t* __restrict__ blk, int nb, int G, int32_t* __
     }
 }
 
-__global__ void __launch_bounds__(EPB) k_ep_hplace(const int32_t* __restrict__ idx, int T, int k, int eloc, int G,
+__global__ void __launch_bounds__(EPB) k_ep_hplace(const int32_t* __restrict__ idx, const int32_t* __restrict__ placement,
+                                                   int T, int k, int eloc, int G,
                                                    const int32_t* __restrict__ blk, const int32_t* __restrict__ rank_off,
                                                    int32_t* __restrict__ row_src, int32_t* __restrict__ send_meta,
                                                    int32_t* __restrict__ pair_pos) {
@@ -98,7 +107,7 @@ __global__ void __launch_bounds__(EPB) k_ep_hplace(const int32_t* __restrict__ i
     uint32_t mask = 0;
 #pragma unroll
     for (int j = 0; j < kEpMaxK; ++j) {
-        ids[j] = (live && j < k) ? __ldg(idx + t * k + j) : -1;
+        ids[j] = (live && j < k) ? ep_placed(idx, placement, t * k + j) : -1;
         const int r = ep_rank_of(ids[j], eloc);
         if (r >= 0 && r < G) mask |= 1u << r;
     }
@@ -257,9 +266,9 @@ size_t ep_dispatch_scratch_bytes(int T, int G) {
 
 bool ep_dispatch_supported(int k, int G) { return G >= 1 && G <= kEpMaxRanks && k >= 1 && k <= kEpMaxK; }
 
-cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, const __half* x16, int d,
-                               __half* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos,
-                               void* scratch, cudaStream_t s) {
+cudaError_t launch_ep_dispatch(const int32_t* idx, const int32_t* placement, int T, int k, int E, int G,
+                               const __half* x16, int d, __half* send_rows, int32_t* send_meta, int32_t* counts,
+                               int32_t* pair_pos, void* scratch, cudaStream_t s) {
     const int nb = (T + EPB - 1) / EPB, eloc = E / G;
     int32_t* blk = static_cast<int32_t*>(scratch);
     const size_t o1 = align_up(static_cast<size_t>(nb) * 2 * G * sizeof(int32_t), 256);
@@ -269,9 +278,9 @@ cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, c
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    k_ep_hcount<<<nb, EPB, 0, s>>>(idx, T, k, eloc, G, blk);
+    k_ep_hcount<<<nb, EPB, 0, s>>>(idx, placement, T, k, eloc, G, blk);
     k_ep_hscan<<<1, 64, 0, s>>>(blk, nb, G, counts, rank_off);
-    k_ep_hplace<<<nb, EPB, 0, s>>>(idx, T, k, eloc, G, blk, rank_off, row_src, send_meta, pair_pos);
+    k_ep_hplace<<<nb, EPB, 0, s>>>(idx, placement, T, k, eloc, G, blk, rank_off, row_src, send_meta, pair_pos);
     k_ep_copy<<<4 * sms, 256, 0, s>>>(x16, d, row_src, counts, G, send_rows);
     return cudaGetLastError();
 }

@@ -26,9 +26,9 @@ cudaError_t launch_ep_combine_routed(const DecodeParams& P, const PrefillBufs& B
                                      const int32_t* pair_pos, cudaStream_t s);
 size_t ep_dispatch_scratch_bytes(int T, int G);
 bool ep_dispatch_supported(int k, int G);
-cudaError_t launch_ep_dispatch(const int32_t* idx, int T, int k, int E, int G, const __half* x16, int d,
-                               __half* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos,
-                               void* scratch, cudaStream_t s);
+cudaError_t launch_ep_dispatch(const int32_t* idx, const int32_t* placement, int T, int k, int E, int G,
+                               const __half* x16, int d, __half* send_rows, int32_t* send_meta, int32_t* counts,
+                               int32_t* pair_pos, void* scratch, cudaStream_t s);
 cudaError_t launch_ep_qmap(const int32_t* meta, int n, int k, int32_t* qblk, int32_t* qmap, cudaStream_t s);
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
 int decode_num_sms();
@@ -364,9 +364,9 @@ size_t qmoe_ep_dispatch_scratch_size(int T, int G) {
     return ep_dispatch_scratch_bytes(T, G);
 }
 
-int qmoe_ep_dispatch(const qmoe_dims* D, int T, int G, void* ws, size_t ws_bytes, void* send_rows,
-                     int32_t* send_meta, int32_t* counts, int32_t* pair_pos, void* scratch, size_t scratch_bytes,
-                     qmoe_stream_t stream) {
+int qmoe_ep_dispatch(const qmoe_dims* D, int T, int G, const int32_t* placement, void* ws, size_t ws_bytes,
+                     void* send_rows, int32_t* send_meta, int32_t* counts, int32_t* pair_pos, void* scratch,
+                     size_t scratch_bytes, qmoe_stream_t stream) {
     int st;
     if ((st = check_dims(D))) return st;
     if (T <= kDecodeMaxT) return QMOE_ERR_UNSUPPORTED;
@@ -378,7 +378,7 @@ int qmoe_ep_dispatch(const qmoe_dims* D, int T, int G, void* ws, size_t ws_bytes
         return QMOE_ERR_WORKSPACE;
     const WsLayout L = ws_layout(*D, T);
     uint8_t* w = static_cast<uint8_t*>(ws);
-    return cuda_status(launch_ep_dispatch(reinterpret_cast<const int32_t*>(w + L.topk_idx), T, D->top_k,
+    return cuda_status(launch_ep_dispatch(reinterpret_cast<const int32_t*>(w + L.topk_idx), placement, T, D->top_k,
                                           D->num_experts, G, reinterpret_cast<const __half*>(w + L.X16), D->d_model,
                                           static_cast<__half*>(send_rows), send_meta, counts, pair_pos, scratch,
                                           reinterpret_cast<cudaStream_t>(stream)));

@@ -70,8 +70,8 @@ SIGNATURES = [
     ("qmoe_ep_route", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_float, c_int, c_void_p,
                               c_size_t, c_void_p]),
     ("qmoe_ep_dispatch_scratch_size", c_size_t, [c_int, c_int]),
-    ("qmoe_ep_dispatch", c_int, [POINTER(QmoeDims), c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
-                                 c_void_p, c_void_p, c_size_t, c_void_p]),
+    ("qmoe_ep_dispatch", c_int, [POINTER(QmoeDims), c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     ("qmoe_ep_rows_workspace_size", c_size_t, [POINTER(QmoeDims), c_int]),
     ("qmoe_ep_experts", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_int, c_int, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),

@@ -47,6 +47,36 @@ def shard_bounds(E: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+def balanced_placement(load, world: int) -> list:
+    """A placement of the experts on `world` ranks (E/world each) that evens
+    out the expected per-rank load: experts by decreasing load, each to the
+    least-loaded rank with room (greedy LPT).  Returns placement[e] = the
+    expert's slot r*(E/world) + local id."""
+    E = len(load)
+    n = E // world
+    if E % world:
+        raise ValueError(f"{E} experts cannot be split evenly over {world} ranks")
+    order = sorted(range(E), key=lambda e: (-float(load[e]), e))
+    rank_load, used = [0.0] * world, [0] * world
+    placement = [0] * E
+    for e in order:
+        r = min((q for q in range(world) if used[q] < n), key=lambda q: (rank_load[q], q))
+        placement[e] = r * n + used[r]
+        used[r] += 1
+        rank_load[r] += float(load[e])
+    return placement
+
+
+def experts_of_rank(placement, world: int, rank: int) -> list:
+    """Global ids of the experts placed on `rank`, in local-id order."""
+    n = len(placement) // world
+    out = [0] * n
+    for e, slot in enumerate(placement):
+        if slot // n == rank:
+            out[slot - rank * n] = e
+    return out
+
+
 class ExpertParallelMoE:
     """One MoE layer sharded over the ranks of `group` (torch.distributed)."""
 
@@ -133,9 +163,10 @@ class CudaBackend:
     this rank's slice of the expert tensors."""
 
     def __init__(self, blk, local_blk, dims, local_dims, world: int, max_tokens: int, max_rows: int,
-                 norm_weight=None, eps: float = 1e-6):
+                 norm_weight=None, eps: float = 1e-6, placement=None):
         import torch
         self.blk, self.local_blk = blk, local_blk
+        self.placement = None if placement is None else torch.tensor(placement, dtype=torch.int32, device="cuda")
         self.dims, self.local_dims = dims, local_dims
         self.norm_weight, self.eps = norm_weight, eps
         self.world = world
@@ -188,7 +219,8 @@ class CudaBackend:
         import torch
         stream = torch.cuda.current_stream().cuda_stream
         _lib.check(_lib.lib().qmoe_ep_dispatch(
-            ctypes.byref(self.dims), self.T, world, self.ws.data_ptr(), self.ws_bytes, self.send_rows.data_ptr(),
+            ctypes.byref(self.dims), self.T, world, None if self.placement is None else self.placement.data_ptr(),
+            self.ws.data_ptr(), self.ws_bytes, self.send_rows.data_ptr(),
             self.send_meta.data_ptr(), self.counts.data_ptr(), self.pair_pos.data_ptr(), self.scratch.data_ptr(),
             self.scratch_bytes, stream), "ep_dispatch")
         return self.send_rows, self.send_meta, self.counts, self.pair_pos[:self.T * self.dims.top_k]
@@ -298,8 +330,7 @@ class CudaBackend:
         import torch
         if n_pairs == 0:
             return torch.zeros((1, self.dims.d_model), dtype=torch.float16, device="cuda")
-        buf = torch.cuda.current_device()
-        t = _DevicePtr(self.ret_ptr, n_pairs * self.dims.d_model * 2, buf)
+        t = _DevicePtr(self.ret_ptr, n_pairs * self.dims.d_model * 2)
         return torch.as_tensor(t, device="cuda").view(torch.float16).view(n_pairs, self.dims.d_model)
 
     def close(self) -> None:
@@ -330,9 +361,35 @@ class _DevicePtr:
     """A raw device allocation seen by torch through __cuda_array_interface__
     (bytes, read-write); the memory stays owned by the caller."""
 
-    def __init__(self, ptr: int, nbytes: int, device: int):
+    def __init__(self, ptr: int, nbytes: int):
         self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
                                          "version": 3, "strides": None, "stream": None}
+
+
+def local_block_placed(blk: "_lib.QmoeBlock", dims, experts) -> tuple:
+    """The rank's experts (global ids, in local-id order) copied into
+    contiguous [E_loc][rows][K] tensors on this GPU, as qmoe_ep_experts
+    reads them.  Returns (block, dims, buffers to keep alive)."""
+    import torch
+    from .quant import calculate_tensor_bytes
+    n, d, F = len(experts), dims.d_model, dims.expert_dim
+    L = _lib.lib()
+    keep = []
+
+    def gather(t, rows, K):
+        per_expert = calculate_tensor_bytes(t.ggml_type, rows * K)
+        buf = torch.empty(n * per_expert, dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        for i, e in enumerate(experts):
+            _lib.check(L.qmoe_copy_async(buf.data_ptr() + i * per_expert, (t.data or 0) + e * per_expert, per_expert,
+                                         stream), "copy_async")
+        keep.append(buf)
+        return _lib.QmoeTensor(buf.data_ptr(), t.ggml_type, 0, n * rows * K)
+
+    lb = _lib.QmoeBlock(blk.router, gather(blk.gate_exps, F, d), gather(blk.up_exps, F, d),
+                        gather(blk.down_exps, d, F), blk.shared_gate_inp, blk.shared_gate, blk.shared_up,
+                        blk.shared_down, None)
+    return lb, _lib.QmoeDims(d, n, dims.top_k, F, dims.shared_dim), keep
 
 
 def local_block(blk: "_lib.QmoeBlock", dims, rank: int, world: int) -> tuple["_lib.QmoeBlock", "_lib.QmoeDims"]:

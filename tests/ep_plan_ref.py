@@ -8,16 +8,19 @@ from __future__ import annotations
 import numpy as np
 
 
-def dispatch_plan(idx: np.ndarray, E: int, G: int):
-    """idx [T][k] global expert ids (-1: failed token).  Returns
+def dispatch_plan(idx: np.ndarray, E: int, G: int, placement=None):
+    """idx [T][k] global expert ids (-1: failed token); placement[e] (optional)
+    = the expert's slot rank * (E/G) + local id, else contiguous shards.  Returns
     (send_tok [rows], send_meta [rows][k], counts [2G], pair_pos [T*k]):
     rows grouped by rank r = e // (E/G), token order inside a rank; the meta
-    row holds the expert id local to r per slot (-1 for slots elsewhere);
+    row holds the expert's local id on r per slot (-1 for slots elsewhere);
     counts = rows per rank then pairs per rank; pair_pos = the pair's place in
     the returned outputs (rank groups in rank order; inside a rank, (row, slot)
     order), -1 for invalid slots."""
     T, k = idx.shape
     eloc = E // G
+    if placement is not None:  # expert e lives at slot placement[e] = rank * eloc + local id
+        idx = np.where(idx >= 0, np.asarray(placement, dtype=np.int64)[np.maximum(idx, 0)], -1)
     send_tok, send_meta = [], []
     rows, pairs = [0] * G, [0] * G
     local = {}

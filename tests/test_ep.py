@@ -166,6 +166,20 @@ def test_dispatch_plan_layout():
     assert pair_pos.tolist() == [3, 0, 1, -1, -1, -1, 4, 2, 5]
 
 
+def test_dispatch_plan_with_placement():
+    # experts 0 and 4 are hot: placement puts them on different ranks
+    pl = ep.balanced_placement([10, 1, 1, 1, 9, 1, 1, 1], 2)
+    assert pl == [0, 5, 1, 6, 4, 2, 7, 3]
+    assert ep.experts_of_rank(pl, 2, 0) == [0, 2, 5, 7] and ep.experts_of_rank(pl, 2, 1) == [4, 1, 3, 6]
+    idx = np.array([[0, 4, 2], [7, 1, -1]], dtype=np.int32)
+    tok, meta, counts, pair_pos = ep_plan_ref.dispatch_plan(idx, 8, 2, pl)
+    # token 0: experts 0 (rank 0 local 0), 4 (rank 1 local 0), 2 (rank 0 local 1); token 1: 7 (rank 0 local 3), 1 (rank 1 local 1)
+    assert tok.tolist() == [0, 1, 0, 1]
+    assert meta.tolist() == [[0, -1, 1], [3, -1, -1], [-1, 0, -1], [-1, 1, -1]]
+    assert counts.tolist() == [2, 2, 3, 2]
+    assert pair_pos.tolist() == [0, 3, 1, 2, 4, -1]
+
+
 def test_shard_bounds():
     assert ep.shard_bounds(256, 8, 3) == (96, 128)
     with pytest.raises(ValueError):

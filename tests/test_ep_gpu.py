@@ -59,10 +59,12 @@ def _reference(blk, x, residual):
     return out, idx
 
 
-@pytest.mark.parametrize("G,types,bias,direct", [(2, synth.Q4K_TYPES, False, False), (8, synth.MIXED_TYPES, True, False),
-                                                (4, synth.Q4K_TYPES, True, True)],
-                         ids=["g2_q4k", "g8_mixed_bias", "g4_q4k_direct_return"])
-def test_ep_shards_on_one_gpu(cuda, G, types, bias, direct):
+@pytest.mark.parametrize("G,types,bias,direct,placed", [(2, synth.Q4K_TYPES, False, False, False),
+                                                       (8, synth.MIXED_TYPES, True, False, False),
+                                                       (4, synth.Q4K_TYPES, True, True, False),
+                                                       (8, synth.Q4K_TYPES, True, True, True)],
+                         ids=["g2_q4k", "g8_mixed_bias", "g4_q4k_direct_return", "g8_q4k_direct_balanced_placement"])
+def test_ep_shards_on_one_gpu(cuda, G, types, bias, direct, placed):
     """Every rank of a G-way split on one GPU: the send layout bit-exact
     against tests/ep_plan_ref.py, each rank's chunk through its local experts,
     the chunks' outputs concatenated in rank order as the all-to-all returns
@@ -78,13 +80,17 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias, direct):
 
     full, dc = blk.c(), dims.c()
     L = _lib.lib()
-    be = ep.CudaBackend(full, full, dc, dc, G, max_tokens=T, max_rows=T)
+    pl = None
+    if placed:  # balance the experts over the ranks by this batch's own load
+        load = np.bincount(want_idx.cpu().numpy().ravel(), minlength=dims.num_experts)
+        pl = ep.balanced_placement(load.tolist(), G)
+    be = ep.CudaBackend(full, full, dc, dc, G, max_tokens=T, max_rows=T, placement=pl)
     _poison(be)
     be.route(x)
     idx = be.topk_idx()
     assert torch.equal(idx, want_idx)
     send_rows, send_meta, counts, pair_pos = be.dispatch(G)
-    tok, meta, cnt, pp = ep_plan_ref.dispatch_plan(idx.cpu().numpy(), dims.num_experts, G)
+    tok, meta, cnt, pp = ep_plan_ref.dispatch_plan(idx.cpu().numpy(), dims.num_experts, G, pl)
     torch.cuda.synchronize()
     assert counts.cpu().numpy().tolist() == cnt.tolist()
     assert np.array_equal(pair_pos.cpu().numpy(), pp)
@@ -98,7 +104,10 @@ def test_ep_shards_on_one_gpu(cuda, G, types, bias, direct):
     y_direct = torch.full((total, d), float("nan"), dtype=torch.float16, device="cuda")
     for r in range(G):
         nr, npairs = int(cnt[r]), int(cnt[G + r])
-        lb, ld = ep.local_block(full, dc, r, G)
+        if placed:
+            lb, ld, keep = ep.local_block_placed(full, dc, ep.experts_of_rank(pl, G, r))
+        else:
+            lb, ld = ep.local_block(full, dc, r, G)
         rws_bytes = L.qmoe_ep_rows_workspace_size(ctypes.byref(ld), max(nr, 1))
         rws = torch.full((rws_bytes,), 0xA5, dtype=torch.uint8, device="cuda")
         _lib.check(L.qmoe_workspace_init(rws.data_ptr(), rws_bytes, None))
