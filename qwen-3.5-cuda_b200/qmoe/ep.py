@@ -47,6 +47,11 @@ def shard_bounds(E: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+class PeerMemoryUnavailable(RuntimeError):
+    """Raised on every rank alike when some rank could not allocate or map
+    the peer buffers of the direct return."""
+
+
 def balanced_placement(load, world: int) -> list:
     """A placement of the experts on `world` ranks (E/world each) that evens
     out the expected per-rank load: experts by decreasing load, each to the
@@ -91,7 +96,10 @@ class ExpertParallelMoE:
         self.lo, self.hi = shard_bounds(E, self.world, self.rank)
         self.direct = direct
         if direct:
-            backend.setup_direct(self.dist, group, self.world, self.rank)
+            try:
+                backend.setup_direct(self.dist, group, self.world, self.rank)
+            except PeerMemoryUnavailable:
+                self.direct = False  # on every rank alike: outputs come back by all-to-all
 
     def gather_counts(self, counts):
         """counts [2G] of every rank -> host matrix C[s] = rank s's counts."""
@@ -249,20 +257,28 @@ class CudaBackend:
         self.ret_bytes = rows * self.dims.d_model * 2
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * 64)()
-        _lib.check(L.qmoe_peer_alloc(self.ret_bytes, ctypes.byref(ptr), handle), "peer_alloc")
-        self.ret_ptr = ptr.value
+        failed = L.qmoe_peer_alloc(self.ret_bytes, ctypes.byref(ptr), handle) != _lib.QMOE_OK
+        self.ret_ptr = None if failed else ptr.value
         handles = [None] * world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.peer_ptrs = []
+        dist.all_gather_object(handles, None if failed else bytes(handle), group=group)
+        self.peer_ptrs, self.rank_ = [], rank
         for s, h in enumerate(handles):
             if s == rank:
                 self.peer_ptrs.append(self.ret_ptr)
                 continue
             q = ctypes.c_void_p()
-            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
-            _lib.check(L.qmoe_peer_open(hb, ctypes.byref(q)), "peer_open")
+            if h is None or L.qmoe_peer_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(q)) != _lib.QMOE_OK:
+                failed = True
+                q.value = None
             self.peer_ptrs.append(q.value)
-        self.rank_ = rank
+        # every rank learns whether all mappings exist, so that all of them
+        # take the same path (a rank that raised alone would leave the others
+        # waiting in the next collective)
+        ok = torch.tensor([0 if failed else 1], dtype=torch.int32, device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise PeerMemoryUnavailable("peer memory between the ranks could not be mapped")
         self.stage = None
         self.side = torch.cuda.Stream()
         self._flag = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -337,7 +353,7 @@ class CudaBackend:
         """Unmap the peers' buffers and free this rank's (after the last call)."""
         L = _lib.lib()
         for s, ptr in enumerate(getattr(self, "peer_ptrs", [])):
-            if s != self.rank_:
+            if s != self.rank_ and ptr:
                 L.qmoe_peer_close(ptr)
         if getattr(self, "ret_ptr", None):
             L.qmoe_peer_free(self.ret_ptr)
