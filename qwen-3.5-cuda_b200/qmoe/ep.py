@@ -15,7 +15,9 @@ Per rank and call (T local tokens):
                of every (token, slot) output in the returned buffer
   3. exchange  the per-rank counts (all-to-all, then the one host
                synchronisation of the call: NCCL needs the split sizes), then
-               rows and meta rows (all-to-all with those splits)
+               rows and meta rows (all-to-all with those splits; with
+               direct=True copy-engine writes into the peers' receive buffers
+               and one barrier)
   4. experts   the rank's experts on the received rows (qmoe_ep_experts,
                tcgen05 grouped GEMMs), outputs in (row, slot) order
   5. return    outputs back with the reverse all-to-all -- or, with
@@ -119,8 +121,11 @@ class ExpertParallelMoE:
         r_rows = [C[s][me] for s in range(G)]
         r_pairs = [C[s][G + me] for s in range(G)]
         ns = sum(s_rows)
-        recv_rows = self._a2a(send_rows[:ns], s_rows, r_rows)
-        recv_meta = self._a2a(send_meta[:ns], s_rows, r_rows)
+        if hasattr(be, "push_rows"):  # rows and meta rows over peer memory as well
+            recv_rows, recv_meta = be.push_rows(send_rows, send_meta, C)
+        else:
+            recv_rows = self._a2a(send_rows[:ns], s_rows, r_rows)
+            recv_meta = self._a2a(send_meta[:ns], s_rows, r_rows)
         pair_start = [0]
         for c in r_pairs:
             pair_start.append(pair_start[-1] + c)
@@ -247,30 +252,44 @@ class CudaBackend:
         return y
 
     # ---- direct return over peer memory ----
-    def setup_direct(self, dist, group, world: int, rank: int) -> None:
-        """Allocate this rank's return buffer (one fp16 row per pair of its
-        tokens) as IPC-shareable memory and map every peer's."""
-        import torch
+    def _shared_buffer(self, nbytes: int, world: int, rank: int):
+        """IPC-shareable device buffer of this rank and every peer's mapping
+        of theirs (index = rank; this rank's own pointer at its index; None
+        where an allocation or a mapping failed)."""
         L = _lib.lib()
-        self.dist, self.group = dist, group
-        rows = (self.pair_pos.numel())  # max_tokens * k
-        self.ret_bytes = rows * self.dims.d_model * 2
         ptr = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * 64)()
-        failed = L.qmoe_peer_alloc(self.ret_bytes, ctypes.byref(ptr), handle) != _lib.QMOE_OK
-        self.ret_ptr = None if failed else ptr.value
+        own = ptr.value if L.qmoe_peer_alloc(nbytes, ctypes.byref(ptr), handle) == _lib.QMOE_OK else None
         handles = [None] * world
-        dist.all_gather_object(handles, None if failed else bytes(handle), group=group)
-        self.peer_ptrs, self.rank_ = [], rank
+        self.dist.all_gather_object(handles, None if own is None else bytes(handle), group=self.group)
+        ptrs = []
         for s, h in enumerate(handles):
             if s == rank:
-                self.peer_ptrs.append(self.ret_ptr)
+                ptrs.append(own)
                 continue
             q = ctypes.c_void_p()
             if h is None or L.qmoe_peer_open((ctypes.c_uint8 * 64).from_buffer_copy(h), ctypes.byref(q)) != _lib.QMOE_OK:
-                failed = True
                 q.value = None
-            self.peer_ptrs.append(q.value)
+            ptrs.append(q.value)
+        if own is not None:
+            self._owned.append(own)
+        self._mapped += [q for s, q in enumerate(ptrs) if s != rank and q]
+        return ptrs
+
+    def setup_direct(self, dist, group, world: int, rank: int) -> None:
+        """IPC-shareable buffers mapped by every peer: this rank's return
+        buffer (one fp16 row per pair of its tokens) and its receive buffers
+        for rows and meta rows (one row per (token, rank) of every rank)."""
+        import torch
+        self.dist, self.group, self.rank_ = dist, group, rank
+        self._owned, self._mapped = [], []
+        d, k = self.dims.d_model, self.dims.top_k
+        self.peer_ptrs = self._shared_buffer(self.pair_pos.numel() * d * 2, world, rank)
+        self.ret_ptr = self.peer_ptrs[rank]
+        self.recv_cap = world * self.pair_pos.numel() // k  # rows: every rank's tokens once
+        self.peer_rows = self._shared_buffer(self.recv_cap * d * 2, world, rank)
+        self.peer_meta = self._shared_buffer(self.recv_cap * k * 4, world, rank)
+        failed = any(p is None for p in self.peer_ptrs + self.peer_rows + self.peer_meta)
         # every rank learns whether all mappings exist, so that all of them
         # take the same path (a rank that raised alone would leave the others
         # waiting in the next collective)
@@ -282,6 +301,33 @@ class CudaBackend:
         self.stage = None
         self.side = torch.cuda.Stream()
         self._flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def push_rows(self, send_rows, send_meta, C):
+        """Rows and meta rows to every rank's receive buffers with the copy
+        engines (this rank's chunk for rank r lands after the chunks of the
+        ranks before it), then a barrier; returns this rank's received rows."""
+        import torch
+        L = _lib.lib()
+        G, me = len(C), self.rank_
+        d, k = self.dims.d_model, self.dims.top_k
+        stream = torch.cuda.current_stream().cuda_stream
+        src = 0
+        for r in range(G):
+            n = C[me][r]
+            if n:
+                at = sum(C[s][r] for s in range(me))
+                if at + n > self.recv_cap:
+                    raise ValueError("expert-parallel receive buffer too small")
+                _lib.check(L.qmoe_copy_async(self.peer_rows[r] + at * d * 2, send_rows.data_ptr() + src * d * 2,
+                                             n * d * 2, stream), "copy_async")
+                _lib.check(L.qmoe_copy_async(self.peer_meta[r] + at * k * 4, send_meta.data_ptr() + src * k * 4,
+                                             n * k * 4, stream), "copy_async")
+            src += n
+        self.dist.all_reduce(self._flag, group=self.group)  # every chunk for this rank has landed
+        n_recv = sum(C[s][me] for s in range(G))
+        rows = torch.as_tensor(_DevicePtr(self.peer_rows[me], max(n_recv, 1) * d * 2), device="cuda")
+        meta = torch.as_tensor(_DevicePtr(self.peer_meta[me], max(n_recv, 1) * k * 4), device="cuda")
+        return (rows.view(torch.float16).view(-1, d)[:n_recv], meta.view(torch.int32).view(-1, k)[:n_recv])
 
     def experts_return(self, rows, meta, pair_start, dst_row) -> None:
         """This rank's experts on the received rows; the outputs of rank s's
@@ -352,13 +398,12 @@ class CudaBackend:
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after the last call)."""
         L = _lib.lib()
-        for s, ptr in enumerate(getattr(self, "peer_ptrs", [])):
-            if s != self.rank_ and ptr:
-                L.qmoe_peer_close(ptr)
-        if getattr(self, "ret_ptr", None):
-            L.qmoe_peer_free(self.ret_ptr)
-            self.ret_ptr = None
-        self.peer_ptrs = []
+        for ptr in getattr(self, "_mapped", []):
+            L.qmoe_peer_close(ptr)
+        for ptr in getattr(self, "_owned", []):
+            L.qmoe_peer_free(ptr)
+        self._mapped, self._owned, self.peer_ptrs = [], [], []
+        self.ret_ptr = None
 
     def combine(self, y, pair_pos, residual=None):
         import torch

@@ -90,7 +90,24 @@ class FakeBackend:
         from multiprocessing import shared_memory
         self.dist, self.rank = dist, rank
         self.shm = shared_memory.SharedMemory(name=self.shm_name)
+        n_ret, n_rows = world * self.cap * D, world * self.rcap * D
         self.bufs = np.ndarray((world, self.cap, D), dtype=np.float32, buffer=self.shm.buf)
+        self.rows_in = np.ndarray((world, self.rcap, D), dtype=np.float32, buffer=self.shm.buf, offset=4 * n_ret)
+        self.meta_in = np.ndarray((world, self.rcap, K), dtype=np.int32, buffer=self.shm.buf,
+                                  offset=4 * (n_ret + n_rows))
+
+    def push_rows(self, send_rows, send_meta, C):
+        G, me = len(C), self.rank
+        src = 0
+        for r in range(G):
+            n = C[me][r]
+            at = sum(C[s][r] for s in range(me))
+            self.rows_in[r, at:at + n] = send_rows.numpy()[src:src + n]
+            self.meta_in[r, at:at + n] = send_meta.numpy()[src:src + n]
+            src += n
+        self.dist.barrier()
+        n_recv = sum(C[s][me] for s in range(G))
+        return (torch.from_numpy(self.rows_in[me, :n_recv].copy()), torch.from_numpy(self.meta_in[me, :n_recv].copy()))
 
     def experts_return(self, rows, meta, pair_start, dst_row):
         self.pending = (self.experts(rows, meta, pair_start[-1]).numpy(), pair_start, dst_row)
@@ -123,7 +140,7 @@ def _worker(rank, world, port, E, token_counts, seed, q, shm_name=None):
     try:
         lo, hi = ep.shard_bounds(E, world, rank)
         be = FakeBackend(E, lo, seed)
-        be.shm_name, be.cap = shm_name, max(token_counts) * K
+        be.shm_name, be.cap, be.rcap = shm_name, max(token_counts) * K, sum(token_counts)
         moe = ep.ExpertParallelMoE(be, E, K, D, direct=shm_name is not None)
         x = np.random.default_rng(100 + rank).standard_normal((token_counts[rank], D)).astype(np.float32)
         out = moe.forward(torch.from_numpy(x)).numpy()
@@ -138,7 +155,8 @@ def _run(world, E, token_counts, seed=5, direct=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    shm = shared_memory.SharedMemory(create=True, size=world * max(token_counts) * K * D * 4) if direct else None
+    size = world * (max(token_counts) * K * D + sum(token_counts) * (D + K)) * 4
+    shm = shared_memory.SharedMemory(create=True, size=size) if direct else None
     try:
         ps = [ctx.Process(target=_worker, args=(r, world, port, E, token_counts, seed, q, shm.name if shm else None))
               for r in range(world)]
