@@ -10,13 +10,15 @@ MoE half of a decoder layer as model.cpp:208-211 runs it -- RMSNorm of the
 residual stream, MoE block, residual add -- with the norm and the add fused
 into the block's kernels, so block l+1 reads block l's output and the 40
 blocks run in sequence like in the model.  Metric: microseconds per token per MoE block
-(lower is better); ``value`` is whole-job: time / (steps * 40 * n_gpus).
+(lower is better); ``value`` = device time / (steps * 40) on each GPU, max
+over ranks; the ``aggregate`` object gives the whole job's throughput.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 (torchrun, one rank per GPU): the headline decode line runs
-independent replicas of the same decode stream (decode does not shard);
-max-over-ranks device time.  The path that shards is prefill: the
+independent replicas of the same decode stream (decode does not shard:
+replicas only); max-over-ranks device time per GPU, aggregate tokens/s over
+all GPUs.  The path that shards is prefill: the
 ``ep_prefill`` object runs T=16384 tokens through one
 block with the experts split over the N GPUs and NCCL all-to-all between
 them; at N = 1 it is the same block on one GPU.
@@ -67,13 +69,11 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_from_profiles():
-    """DRAM bytes (read + write) of one k_experts launch from the committed ncu summary."""
-    p = ROOT / "profiles" / "k_experts_decode_q4k.md"
-    if not p.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", p.read_text())
-    return int(m.group(1)) if m else None
+# DRAM bytes (read + write) of one k_experts launch, from an ncu capture of the
+# same kernel on the same workload shape (dram__bytes_read.sum +
+# dram__bytes_write.sum; the capture command is in
+# profiles/k_experts_decode_q4k.md).  Imported, not measured by this run.
+EXPERT_TRAFFIC_BYTES = 16_061_184
 
 
 class ClockSampler(threading.Thread):
@@ -256,18 +256,23 @@ def run_ours(args):
         ms, ems, kernel_us = float(t[0]), float(t[1]), float(t[2])
     del g
 
-    per_block_us = ms * 1e3 / (args.steps * L)          # one GPU
-    value = ms * 1e3 / (args.steps * L * world)         # whole job
-    e2e = ems * 1e3 / (args.steps * L * world)
+    # decode does not shard: N GPUs run N independent replicas of the decode
+    # stream, so the time per block and token is per GPU (max over ranks) and
+    # the job's throughput is N times one replica's
+    per_block_us = ms * 1e3 / (args.steps * L)
+    value = per_block_us
+    e2e = ems * 1e3 / (args.steps * L)
     peak, peak_kind = _peaks()
     achieved = EXPERT_BYTES / (kernel_us * 1e-6) / 1e9
     block_achieved = BLOCK_BYTES / (per_block_us * 1e-6) / 1e9
-    traffic = _traffic_from_profiles()
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K; x ~ N(0,1))",
+        "aggregate": {"tokens_per_s": round(world * args.steps / (ms * 1e-3), 1),
+                      "block_tokens_per_s": round(world * args.steps * L / (ms * 1e-3), 1),
+                      "note": "all replicas together; value is the per-GPU time per block and token"},
         "config": {"workload": WORKLOAD, "tokens_per_step": 1, "layers": L, "parallelism": f"replicas{world}",
                    "l2": "inputs larger than L2: ~722 MB of distinct weights touched per step vs 126 MB L2",
                    "launch": f"one CUDA graph per step ({kernels_per_block} kernels per block)"},
@@ -281,12 +286,15 @@ def run_ours(args):
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": EXPERT_BYTES,
                      "avg_launch_us": round(kernel_us, 3),
-                     "traffic": traffic,
+                     "traffic": EXPERT_TRAFFIC_BYTES,
+                     "traffic_source": "imported: ncu capture of k_experts (profiles/k_experts_decode_q4k.md)",
                      "block": {"algorithmic_bytes": BLOCK_BYTES, "us": round(per_block_us, 3),
                                "achieved": round(block_achieved, 1), "frac": round(block_achieved / peak, 4)}},
     }
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"], line["parity"] = cpu_baseline(args, blocks, inputs, dims, dc, ws, nws)
+        line["parity"] = decode_parity(blocks, inputs, dims, dc, ws, nws, 3)
+        line["cpu_baseline"] = cpu_baseline(args)
+        line["ref_gpu"] = ref_gpu_baseline(blocks, inputs, dims, steps=4)
     if world == 1 and not args.no_extra:
         line["prefill"] = measure_prefill(blocks[0], dims)
         line["config3"] = measure_config3(dims)
@@ -314,13 +322,14 @@ def measure_prefill(blk, dims):
 
     from qmoe import _lib
 
+    from qmoe import synth
+
     T = PREFILL_T
     dc = dims.c()
-    bias = _zipf_bias(dims)
+    bias, bias_h, _ = _zipf_bias(dims)
     c = blk.c()
     c.expert_bias = bias.data_ptr()
-    g = torch.Generator(device="cuda").manual_seed(SEED + 5)
-    x = torch.randn(T, dims.d_model, generator=g, device="cuda", dtype=torch.float32)
+    x = synth.inputs(T, dims.d_model, seed=SEED + 5, tag=4)
     n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
     ws = torch.empty(n, dtype=torch.uint8, device="cuda")
     _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
@@ -342,9 +351,15 @@ def measure_prefill(blk, dims):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
     st, flags, _ = _check_errors(_lib, ws, dc)
-    p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_OFFSETS)
-    off = p - ws.data_ptr()
-    counts = np.diff(ws[off:off + 4 * (dims.num_experts + 1)].cpu().numpy().view(np.int32))
+    E, k = dims.num_experts, dims.top_k
+    got = {"logits": _ws_view(_lib, ws, dc, T, _lib.WS_LOGITS, T * (E + 1), np.float32).reshape(T, E + 1)[:, :E],
+           "idx": _ws_view(_lib, ws, dc, T, _lib.WS_TOPK_IDX, T * k, np.int32).reshape(T, k),
+           "w": _ws_view(_lib, ws, dc, T, _lib.WS_TOPK_W, T * k, np.float32).reshape(T, k),
+           "offsets": _ws_view(_lib, ws, dc, T, _lib.WS_OFFSETS, E + 1, np.int32),
+           "perm": _ws_view(_lib, ws, dc, T, _lib.WS_PERM, T * k, np.int32),
+           "out": out.cpu().numpy()}
+    counts = np.diff(got["offsets"])
+    parity = _oracle_parity(blk, dims, x.cpu().numpy(), got, bias_h)
     k, F, d = dims.top_k, dims.expert_dim, dims.d_model
     flop = 2.0 * T * k * 3 * F * d + 2.0 * T * 3 * dims.shared_dim * d  # routed + shared expert products
     tflops = flop / (us * 1e-6) / 1e12
@@ -358,51 +373,21 @@ def measure_prefill(blk, dims):
                          "note": "whole block (router, top-k, dispatch, GEMMs, combine) against dense bf16 peak"},
             "routing": {"experts_hit": int((counts > 0).sum()), "max_per_expert": int(counts.max()),
                         "mean_per_hit_expert": round(float(counts[counts > 0].mean()), 1)},
+            "parity": parity,
             "error_flags": flags}
 
 
 EP_T = 16384
 
 
-def zipf_bias(E, k, d, sigma=0.02, s=ZIPF_S, seed=SEED + 4, sample=4096, iters=60):
-    """Per-expert router logit bias under which the expert hit histogram
-    follows Zipf(s): expert of popularity rank r (a seeded permutation) gets a
-    share proportional to r^-s of the T*k pairs, capped at one pair per token
-    (the overflow of the capped head spread over the rest).  Calibrated on a
-    seeded sample of the benchmark's input distribution (x ~ N(0,1), router
-    rows ~ N(0, sigma^2)): a damped fixed-point iteration on
-    log(target count) - log(sample count).  Deterministic; about a second of
-    host time."""
-    import numpy as np
-    rng = np.random.default_rng(seed)
-    W = (rng.standard_normal((E, d)) * sigma).astype(np.float32)
-    X = rng.standard_normal((sample, d)).astype(np.float32)
-    logits = X @ W.T
-    ranks = rng.permutation(E) + 1
-    z = np.arange(1, E + 1, dtype=np.float64) ** -s
-    z = z / z.sum() * sample * k
-    for _ in range(64):
-        over = np.clip(z - sample, 0, None).sum()
-        z = np.minimum(z, sample)
-        free = z < sample
-        if over <= 0 or not free.any():
-            break
-        z[free] += over * z[free] / z[free].sum()
-    target = np.minimum(z[ranks - 1], sample - 0.5)
-    b = -s * np.log(ranks) * 0.5
-    for _ in range(iters):
-        idx = np.argpartition(-(logits + b[None, :]), k, axis=1)[:, :k]
-        cnt = np.bincount(idx.ravel(), minlength=E).astype(np.float64)
-        b += 0.5 * (np.log(target) - np.log(np.maximum(cnt, 0.5)))
-        b -= b.max()
-    zipf_bias.target = target / sample  # expected pairs per token and expert (the placement's load model)
-    return b.astype(np.float32)
-
-
 def _zipf_bias(dims):
+    """The calibrated Zipf(1.1) router bias on the device, and the expected
+    pairs per token of each expert (the placement's load model)."""
     import torch
-    b = zipf_bias(dims.num_experts, dims.top_k, dims.d_model)
-    return torch.tensor(b, dtype=torch.float32, device="cuda")
+
+    from qmoe import synth
+    b, target = synth.zipf_bias(dims.num_experts, dims.top_k, dims.d_model, s=ZIPF_S, seed=SEED + 4)
+    return torch.tensor(b, dtype=torch.float32, device="cuda"), b, target
 
 
 def measure_ep(world, rank, dims):
@@ -414,6 +399,7 @@ def measure_ep(world, rank, dims):
     block on all T tokens once and checks that its routing is bit-identical
     and its output equal.  Time: CUDA events around repeated calls, max over
     ranks; tokens/s counts all T tokens (total work fixed: strong scaling)."""
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -426,7 +412,7 @@ def measure_ep(world, rank, dims):
     g = torch.Generator(device="cuda").manual_seed(SEED + 8)
     x_all = torch.randn(T, d, generator=g, device="cuda", dtype=torch.float32)
     x = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
-    zipf = _zipf_bias(dims)
+    zipf, zipf_h, zipf_target = _zipf_bias(dims)
     n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
     ws = torch.empty(n, dtype=torch.uint8, device="cuda")
     _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
@@ -453,15 +439,24 @@ def measure_ep(world, rank, dims):
         one_gpu()
         torch.cuda.synchronize()
         entry = {}
+        bias_h = zipf_h if routing == "zipf" else None
         if world == 1:
             run = one_gpu
+            got = {"logits": _ws_view(_lib, ws, dc, T, _lib.WS_LOGITS, T * (E + 1), np.float32).reshape(T, E + 1)[:, :E],
+                   "idx": _ws_view(_lib, ws, dc, T, _lib.WS_TOPK_IDX, T * k, np.int32).reshape(T, k),
+                   "w": _ws_view(_lib, ws, dc, T, _lib.WS_TOPK_W, T * k, np.float32).reshape(T, k),
+                   "offsets": _ws_view(_lib, ws, dc, T, _lib.WS_OFFSETS, E + 1, np.int32),
+                   "perm": _ws_view(_lib, ws, dc, T, _lib.WS_PERM, T * k, np.int32),
+                   "out": out_all.cpu().numpy()}
+            entry["parity"] = _oracle_parity(blk, dims, x_all.cpu().numpy(), got, bias_h, n_spread=48, n_cold=4,
+                                             per_cold=2, every_expert=False)
         else:
             p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, _lib.WS_TOPK_IDX)
             off = p - ws.data_ptr()
             want_idx = ws[off:off + T * k * 4].view(torch.int32).view(T, k)[rank * Tl:(rank + 1) * Tl].clone()
             pl = None
             if routing == "zipf":  # experts placed to balance the expected (calibrated) per-rank load
-                pl = ep.balanced_placement(zipf_bias.target.tolist(), world)
+                pl = ep.balanced_placement(zipf_target.tolist(), world)
                 lb, ld, keep = ep.local_block_placed(c, dc, ep.experts_of_rank(pl, world, rank))
                 entry["placement"] = "balanced by the calibrated Zipf(1.1) expert load"
             else:
@@ -476,7 +471,17 @@ def measure_ep(world, rank, dims):
             chk = torch.tensor([0.0 if torch.equal(idx, want_idx) else 1.0, float((got - want).abs().max())],
                                dtype=torch.float64, device="cuda")
             dist.all_reduce(chk, op=dist.ReduceOp.MAX)
-            entry["parity"] = {"ids_bit_identical_to_1gpu": chk[0].item() == 0.0, "max_abs_diff_vs_1gpu": chk[1].item()}
+            orc_rep = _ep_oracle_parity(blk, dims, x.cpu().numpy(), idx.cpu().numpy(), got.cpu().numpy(), bias_h,
+                                        world)
+            ok = torch.tensor([orc_rep["max_abs_err"], orc_rep["max_rel_err"], float(orc_rep["n_outside"]),
+                               0.0 if orc_rep["ids_bit_exact"] else 1.0], dtype=torch.float64, device="cuda")
+            dist.all_reduce(ok, op=dist.ReduceOp.MAX)
+            entry["parity"] = {"ids_bit_identical_to_1gpu": chk[0].item() == 0.0, "max_abs_diff_vs_1gpu": chk[1].item(),
+                               "oracle": {"ids_bit_exact": ok[3].item() == 0.0, "max_abs_err": ok[0].item(),
+                                          "max_rel_err": ok[1].item(), "max_n_outside_per_rank": int(ok[2].item()),
+                                          "within_tol": ok[3].item() == 0.0 and ok[2].item() == 0.0,
+                                          "sample": "every rank: routing of its T/N tokens, outputs of a sample "
+                                                    f"of ~{orc_rep['sample_tokens']} of them"}}
 
             def run():
                 moe.forward(x)
@@ -511,6 +516,24 @@ def measure_ep(world, rank, dims):
             be.close()
         dist.barrier()
     return res
+
+
+def _ep_oracle_parity(blk, dims, x_local, idx_local, out_local, bias_h, world):
+    """One rank's share of the expert-parallel parity: its tokens' expert ids
+    against the oracle's routing, and the outputs of a sample of them."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    from qmoe import synth
+    orc.set_threads(max(1, (os.cpu_count() or 1) // world))
+    _, idx, _ = orc.route(blk.host_bytes("router"), blk.types["router"], x_local, dims.num_experts, dims.top_k,
+                          bias_h)
+    sample = orc.pick_sample(idx, dims.num_experts, n_spread=16, n_cold=2, per_cold=1, every_expert=False)
+    want = orc.moe_forward({n: blk.host_bytes(n) for n in synth.TENSORS}, blk.types, dims, x_local[sample], bias_h)
+    rep = orc.tolerance_report(out_local[sample], want["out"])
+    rep["ids_bit_exact"] = bool(np.array_equal(idx, idx_local))
+    rep["sample_tokens"] = int(sample.size)
+    return rep
 
 
 def measure_config3(dims):
@@ -575,6 +598,31 @@ def _check_errors(_lib, ws, dc):
     return st, int(err[0]), int(err[1])
 
 
+def _ws_view(_lib, ws, dc, T, which, count, dtype):
+    import numpy as np
+    p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), T, which)
+    off = p - ws.data_ptr()
+    return ws[off:off + count * np.dtype(dtype).itemsize].cpu().numpy().view(dtype)
+
+
+def _oracle_parity(blk, dims, x_host, got, bias_h, threads=None, **sample_kw):
+    """orc.check_batch on the host cores: routing of every token bit-exact,
+    outputs of a sample of tokens within tolerance (not timed)."""
+    from oracle import oracle as orc
+    from qmoe import synth
+    orc.set_threads(threads or os.cpu_count() or 1)
+    sample = None
+    if sample_kw:
+        logits, idx, _ = orc.route(blk.host_bytes("router"), blk.types["router"], x_host, dims.num_experts,
+                                   dims.top_k, bias_h)
+        sample = orc.pick_sample(idx, dims.num_experts, **sample_kw)
+    t0 = time.perf_counter()
+    res = orc.check_batch({n: blk.host_bytes(n) for n in synth.TENSORS}, blk.types, dims, x_host, got, bias_h,
+                          sample=sample)
+    res["check_s"] = round(time.perf_counter() - t0, 1)
+    return res
+
+
 def _ws_array(_lib, ws, dc, which, count, dtype):
     import numpy as np
     p = _lib.lib().qmoe_ws_view(ws.data_ptr(), ctypes.byref(dc), 1, which)
@@ -582,23 +630,126 @@ def _ws_array(_lib, ws, dc, which, count, dtype):
     return ws[off:off + count * np.dtype(dtype).itemsize].cpu().numpy().view(dtype)
 
 
-def cpu_baseline(args, blocks, inputs, dims, dc, ws, nws):
+def cpu_info() -> dict:
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": model, "nproc": os.cpu_count()}
+
+
+class CpuStack:
+    """The config-2 stack's weights on the host for the CPU legs, generated
+    lazily (router and shared expert per layer, a routed expert's three
+    matrices when a token first selects it) by the oracle's copy of the host
+    generator -- the same bytes the GPU arm generates on the device."""
+
+    def __init__(self):
+        import numpy as np
+
+        from qmoe import synth
+        from qmoe.quant import calculate_tensor_bytes
+        self.np, self.synth = np, synth
+        self.dims = synth.Dims()
+        self.types = synth.Q4K_TYPES
+        self.tb = calculate_tensor_bytes
+        self.cache = {}
+        self.pool = self._inputs()
+
+    def _inputs(self):
+        from oracle import oracle as orc
+        d = self.dims.d_model
+        b = self.np.empty(POOL * d * 4, dtype=self.np.uint8)
+        orc.synth_fill(b, 0, 0, POOL * d, SEED, self.synth.input_stream_id(2), 1.0)
+        return b.view(self.np.float32).reshape(POOL, d)
+
+    def _fill(self, name, layer, first, n, dst):
+        from oracle import oracle as orc
+        sid = self.synth.stream_id(layer, self.synth.TENSORS.index(name) + 1)
+        orc.synth_fill(dst, int(self.types[name]), first, n, SEED, sid, self.synth.WEIGHT_SIGMA)
+
+    def layer(self, layer):
+        if layer not in self.cache:
+            t = {}
+            for n in self.synth.TENSORS:
+                t[n] = self.np.zeros(self.tb(self.types[n], self.dims.elements(n)), dtype=self.np.uint8)
+            for n in ("router", "shared_gate_inp", "shared_gate", "shared_up", "shared_down"):
+                self._fill(n, layer, 0, self.dims.elements(n), t[n])
+            self.cache[layer] = (t, set())
+            if len(self.cache) > 4:
+                self.cache.pop(next(iter(self.cache)))
+        return self.cache[layer]
+
+    def prepare(self, step):
+        """Weights of block (step mod 40) with the experts its token selects, and the token."""
+        from oracle import oracle as orc
+        d, E, k, F = self.dims.d_model, self.dims.num_experts, self.dims.top_k, self.dims.expert_dim
+        layer = step % N_LAYERS
+        x = self.pool[(step // N_LAYERS) % POOL]
+        t, have = self.layer(layer)
+        logits = orc.gemv(t["router"], 0, E * d, x, E, d)
+        ids, _ = orc.topk(logits, k)
+        bpe = self.tb(self.types["gate_exps"], F * d)
+        for e in ids.tolist():
+            if e not in have:
+                for n in ("gate_exps", "up_exps", "down_exps"):
+                    self._fill(n, layer, e * F * d, F * d, t[n][e * bpe:(e + 1) * bpe])
+                have.add(e)
+        return t, x
+
+    def time_blocks(self, steps, warmup, threads):
+        """Microseconds per block and token of the oracle on `threads` host threads."""
+        from oracle import oracle as orc
+        orc.set_threads(threads)
+        for i in range(warmup):
+            t, x = self.prepare(i)
+            orc.moe_forward(t, self.types, self.dims, x)
+        secs = 0.0
+        for i in range(steps):
+            t, x = self.prepare(warmup + i)
+            t0 = time.perf_counter()
+            res = orc.moe_forward(t, self.types, self.dims, x)
+            secs += time.perf_counter() - t0
+            assert res["status"][0] == 0
+        return secs / steps * 1e6
+
+
+def cpu_baseline(args):
     """The oracle (C restatement of the reference MoE path) on the host cores
-    over a bounded sample, plus a parity gate on the same sample."""
+    over a bounded sample: all host threads and one thread."""
+    threads = os.cpu_count() or 1
+    st = CpuStack()
+    n_all, n_one = max(4, args.cpu_layers), 2
+    v_all = st.time_blocks(n_all, 2, threads)
+    v_one = st.time_blocks(n_one, 1, 1)
+    sample = (f"{n_all} MoE blocks x 1 token after 2 warm-up blocks (layer = step mod 40 of the config-2 stack), "
+              "oracle/qmoe_oracle.c, OpenMP over output rows")
+    return {"value": round(v_all, 1), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+            "single_thread": {"value": round(v_one, 1), "unit": UNIT, "cores": 1,
+                              "sample": f"{n_one} MoE blocks x 1 token after 1 warm-up block"},
+            "cpu": cpu_info()}
+
+
+def decode_parity(blocks, inputs, dims, dc, ws, nws, n_blocks):
+    """The product's decode output of the first n_blocks layers of the stack
+    (one token, the residual stream as in the timed run) against the oracle:
+    expert ids bit-exact, outputs within max-abs 1e-3 / rel 1e-2."""
     import numpy as np
     import torch
 
     from oracle import oracle as orc
     from qmoe import _lib, synth
 
-    threads = os.cpu_count() or 1
-    orc.set_threads(threads)
-    S = min(args.cpu_layers, len(blocks))
+    orc.set_threads(os.cpu_count() or 1)
     x = inputs[0:1].clone()
     out = torch.empty_like(x)
-    secs, ids_ok, max_err, within = 0.0, True, 0.0, True
+    ids_ok, max_abs, max_rel, within = True, 0.0, 0.0, True
     gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")
-    for l in range(S):
+    for l in range(n_blocks):
         c = blocks[l].c()
         _lib.check(_lib.lib().qmoe_block_forward_prenorm(ctypes.byref(c), ctypes.byref(dc), x.data_ptr(),
                                                          gamma.data_ptr(), EPS, out.data_ptr(), 1, ws.data_ptr(),
@@ -606,98 +757,88 @@ def cpu_baseline(args, blocks, inputs, dims, dc, ws, nws):
         torch.cuda.synchronize()
         gid = _ws_array(_lib, ws, dc, _lib.WS_TOPK_IDX, dims.top_k, np.int32)
         xin = _ws_array(_lib, ws, dc, _lib.WS_INPUT, dims.d_model, np.float32)  # rmsnorm(r) as the block saw it
-        host = {n: blocks[l].host_bytes(n) for n in synth.TENSORS}
-        t0 = time.perf_counter()
-        res = orc.moe_forward(host, blocks[l].types, dims, xin)
-        secs += time.perf_counter() - t0
-        got = out.cpu().numpy()
-        want = x.cpu().numpy() + res["out"]
+        res = orc.moe_forward({n: blocks[l].host_bytes(n) for n in synth.TENSORS}, blocks[l].types, dims, xin)
+        rep = orc.tolerance_report(out.cpu().numpy(), x.cpu().numpy() + res["out"])
         ids_ok &= bool(np.array_equal(gid, res["idx"][0]))
-        max_err = max(max_err, float(np.max(np.abs(got - want))))
-        within &= bool(np.all(np.isclose(got, want, atol=1e-3, rtol=1e-2)))
+        max_abs, max_rel = max(max_abs, rep["max_abs_err"]), max(max_rel, rep["max_rel_err"])
+        within &= rep["within_tol"]
         x = out.clone()  # the residual stream, as in the timed run
-    cpu = {"value": round(secs / S * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
-           "sample": f"{S} MoE blocks x 1 token (layers 0..{S - 1} of the config-2 stack, step 0), "
-                     "oracle/qmoe_oracle.c, OpenMP over output rows"}
-    parity = {"blocks": S, "ids_bit_exact": ids_ok, "max_abs_err": max_err, "within_tol": within,
-              "tol": "max-abs 1e-3 / rel 1e-2"}
-    return cpu, parity
+    return {"blocks": n_blocks, "ids_bit_exact": ids_ok, "max_abs_err": max_abs, "max_rel_err": max_rel,
+            "within_tol": within and ids_ok, "tol": "per element |err| <= 1e-3 or |err|/|want| <= 1e-2"}
+
+
+def ref_gpu_baseline(blocks, inputs, dims, steps):
+    """The reference's own GPU path (oracle/_ref: MoeLayer::forward and its
+    kernels compiled unmodified for sm_100a, with rmsnorm_forward and
+    residual_add around it as model.cpp:207-211 runs them) over the same 40
+    layers of weights, one token at a time, CUDA events around the steps.
+    MoeLayer::forward synchronises the stream inside every call, as shipped."""
+    import torch
+
+    from oracle import oracle as orc
+    if not orc.ref_available():
+        return {"unavailable": "oracle/_ref/libqwenref.so not built (the reference tree was absent at build time)"}
+    from qmoe import synth
+    L = orc.ref_lib()
+    L.ref_stack_create.restype = ctypes.c_void_p
+    L.ref_stack_create.argtypes = [ctypes.c_int] * 6 + [ctypes.c_void_p] * 3
+    L.ref_stack_forward.restype = ctypes.c_int
+    L.ref_stack_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                                    ctypes.c_void_p]
+    L.ref_stack_destroy.argtypes = [ctypes.c_void_p]
+    nl = len(blocks)
+    ptrs = (ctypes.c_void_p * (8 * nl))(*[b.t[n].device_ptr for b in blocks for n in synth.TENSORS])
+    tys = (ctypes.c_int * (8 * nl))(*[int(b.types[n]) for b in blocks for n in synth.TENSORS])
+    nel = (ctypes.c_uint64 * (8 * nl))(*[dims.elements(n) for b in blocks for n in synth.TENSORS])
+    h = L.ref_stack_create(nl, dims.d_model, dims.num_experts, dims.top_k, dims.expert_dim, dims.shared_dim,
+                           ptrs, tys, nel)
+    if not h:
+        return {"unavailable": "reference stack set-up failed: " + L.ref_last_error().decode()}
+    gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")
+    x = inputs[0:1].clone()
+    s = torch.cuda.current_stream().cuda_stream
+    try:
+        for i in range(3):
+            x.copy_(inputs[i:i + 1])
+            if L.ref_stack_forward(h, x.data_ptr(), gamma.data_ptr(), EPS, s):
+                raise RuntimeError(L.ref_last_error().decode())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            x.copy_(inputs[i % POOL:i % POOL + 1])
+            if L.ref_stack_forward(h, x.data_ptr(), gamma.data_ptr(), EPS, s):
+                raise RuntimeError(L.ref_last_error().decode())
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    finally:
+        L.ref_stack_destroy(h)
+    return {"us_per_block": round(ms * 1e3 / (steps * nl), 2), "ms_per_step": round(ms / steps, 4),
+            "steps": steps, "layers": nl,
+            "what": "reference MoeLayer::forward (+ rmsnorm_forward, residual_add) built from the reference sources "
+                    "for sm_100a (oracle/_ref), same weights and tokens, one token per step"}
 
 
 # ---------------------------------------------------------------------------
 # reference arm: the reference's CPU path (oracle port), rank 0 only
 # ---------------------------------------------------------------------------
 def run_reference(args):
-    import numpy as np
-
-    from oracle import oracle as orc
-    from qmoe import _lib, synth
-    from qmoe.quant import GgmlType, calculate_tensor_bytes
-
     world, rank, _ = _dist()
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    orc.set_threads(threads)
-    dims = synth.Dims()
-    d, E, k, F, Fs = dims.d_model, dims.num_experts, dims.top_k, dims.expert_dim, dims.shared_dim
-    types = synth.Q4K_TYPES
-    pool = synth.inputs(POOL, d, seed=SEED, tag=2, device="cpu")
-    layer_cache = {}
-
-    def fill_range(name, layer, first, n, dst):
-        sid = synth.stream_id(layer, synth.TENSORS.index(name) + 1)
-        _lib.check(_lib.lib().qmoe_synth_fill_host_range(dst.ctypes.data, int(types[name]), first, n, SEED, sid,
-                                                         synth.WEIGHT_SIGMA))
-
-    def layer_tensors(layer):
-        if layer not in layer_cache:
-            t = {}
-            for n in synth.TENSORS:
-                nb = calculate_tensor_bytes(types[n], dims.elements(n))
-                t[n] = np.zeros(nb, dtype=np.uint8)  # lazily backed; only filled slices are touched
-            for n in ("router", "shared_gate_inp", "shared_gate", "shared_up", "shared_down"):
-                fill_range(n, layer, 0, dims.elements(n), t[n])
-            layer_cache[layer] = (t, set())
-            if len(layer_cache) > 4:
-                layer_cache.pop(next(iter(layer_cache)))
-        return layer_cache[layer]
-
-    def prepare(step):
-        layer = step % N_LAYERS
-        x = pool[(step // N_LAYERS) % POOL]
-        t, have = layer_tensors(layer)
-        logits = orc.gemv(t["router"], 0, E * d, x, E, d)
-        ids, _ = orc.topk(logits, k)
-        for e in ids.tolist():
-            if e in have:
-                continue
-            bpe = calculate_tensor_bytes(GgmlType.Q4_K, F * d)
-            for n in ("gate_exps", "up_exps", "down_exps"):
-                fill_range(n, layer, e * F * d, F * d, t[n][e * bpe:(e + 1) * bpe])
-            have.add(e)
-        return t, x
-
-    for i in range(args.warmup):
-        t, x = prepare(i)
-        orc.moe_forward(t, types, dims, x)
-    secs = 0.0
-    for i in range(args.steps):
-        t, x = prepare(args.warmup + i)
-        t0 = time.perf_counter()
-        res = orc.moe_forward(t, types, dims, x)
-        secs += time.perf_counter() - t0
-        assert res["status"][0] == 0
-    value = secs / args.steps * 1e6
-    sample = (f"{args.steps} MoE blocks x 1 token (layer = step mod 40) of the config-2 stack; "
-              "only the routed experts' bytes are generated; oracle/qmoe_oracle.c, OpenMP over output rows")
+    value = CpuStack().time_blocks(args.steps, args.warmup, threads)
+    sample = (f"{args.steps} MoE blocks x 1 token after {args.warmup} warm-up blocks (layer = step mod 40) of the "
+              "config-2 stack; only the routed experts' bytes are generated; oracle/qmoe_oracle.c, OpenMP over "
+              "output rows")
     line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value / 1e3, 3),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": {"workload": WORKLOAD, "tokens_per_step": 1, "layers": 1,
                                            "parallelism": "cpu"},
             "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": sample},
+                             "sample": sample, "cpu": cpu_info()},
             "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -6,10 +6,14 @@
 # points).  oracle/ref_shim/qwen_ref_prelude.hpp is force-included to stand in
 # for the reference's cuda_utils.hpp, whose macros do not compile as shipped
 # (it also supplies the CUDA_CHECK that ops.cu uses without including it).
-# Usage: oracle/build_ref.sh [reference_root]   (default: the development checkout)
+# Usage: oracle/build_ref.sh <reference_root>
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-ref="${1:-/root/reference}"
+if [ $# -lt 1 ]; then
+  echo "usage: $0 <reference_root>" >&2
+  exit 2
+fi
+ref="$1"
 if [ ! -f "$ref/src/layer_moe.cpp" ]; then
   echo "reference tree not found at $ref; skipping" >&2
   exit 0

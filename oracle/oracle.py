@@ -16,6 +16,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libqwenref.so"
+SYNTH_LIB = HERE / "libsynth_host.so"
 
 TENSORS = ["router", "gate_exps", "up_exps", "down_exps", "shared_gate_inp", "shared_gate", "shared_up",
            "shared_down"]
@@ -54,6 +55,9 @@ def lib() -> ctypes.CDLL:
         L.or_moe_forward_batch.argtypes = [POINTER(OrBlock), c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                            c_void_p]
+        L.or_route_batch.restype = None
+        L.or_route_batch.argtypes = [c_void_p, c_int, c_uint64, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                     c_void_p, c_void_p, c_void_p]
         L.or_dispatch.restype = c_int
         L.or_dispatch.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]
         L.or_rmsnorm.restype = None
@@ -110,6 +114,42 @@ def topk(logits: np.ndarray, k: int):
     return idx, w
 
 
+def route(router: np.ndarray, ggml_type: int, x: np.ndarray, E: int, k: int, bias: np.ndarray | None = None):
+    """Router logits (+ bias) and top-k of every row of x: (logits[T][E], idx[T][k], w[T][k])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, d = x.shape
+    router = np.ascontiguousarray(router)
+    logits = np.zeros((T, E), dtype=np.float32)
+    idx = np.zeros((T, k), dtype=np.int32)
+    w = np.zeros((T, k), dtype=np.float32)
+    bp = None
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, dtype=np.float32)
+        bp = _p(bias)
+    lib().or_route_batch(_p(router), int(ggml_type), E * d, bp, d, E, k, T, _p(x), _p(logits), _p(idx), _p(w))
+    return logits, idx, w
+
+
+def tolerance_report(got: np.ndarray, want: np.ndarray, atol: float = 1e-3, rtol: float = 1e-2) -> dict:
+    """Output error against the oracle under the two bounds "max-abs atol /
+    rel rtol": an element passes when its absolute error is at most atol or
+    its relative error at most rtol.  Reports the largest absolute error,
+    the largest relative error among elements with |want| >= atol / rtol
+    (where the relative bound is the binding one), and the element count
+    outside both bounds."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    diff = np.abs(got - want)
+    mag = np.abs(want)
+    big = mag >= atol / rtol
+    bad = ~((diff <= atol) | (diff <= rtol * mag))
+    bad |= ~np.isfinite(got)
+    return {"max_abs_err": float(diff.max()) if diff.size else 0.0,
+            "max_rel_err": float((diff[big] / mag[big]).max()) if big.any() else 0.0,
+            "n_outside": int(bad.sum()), "n": int(diff.size), "within_tol": not bool(bad.any()),
+            "tol": f"per element |err| <= {atol:g} or |err|/|want| <= {rtol:g}"}
+
+
 def moe_forward(tensors: dict, types: dict, dims, x: np.ndarray, bias: np.ndarray | None = None):
     """tensors: name -> uint8 numpy payload; dims: object with d_model,
     num_experts, top_k, expert_dim, shared_dim.  Returns a dict."""
@@ -154,6 +194,34 @@ def dispatch(idx: np.ndarray, E: int):
 
 
 # ---------------------------------------------------------------------------
+# Seeded synthetic bytes on the host (oracle/libsynth_host.so: the product's
+# host generator compiled on its own), for CPU legs that must not load the
+# product library.
+# ---------------------------------------------------------------------------
+_synth = None
+
+
+def synth_lib() -> ctypes.CDLL:
+    global _synth
+    if _synth is None:
+        if not SYNTH_LIB.exists():
+            build()
+        L = ctypes.CDLL(str(SYNTH_LIB))
+        L.qmoe_synth_fill_host_range.restype = c_int
+        L.qmoe_synth_fill_host_range.argtypes = [c_void_p, ctypes.c_uint32, c_uint64, c_uint64, c_uint64, c_uint64,
+                                                 c_float]
+        _synth = L
+    return _synth
+
+
+def synth_fill(dst: np.ndarray, ggml_type: int, first: int, n: int, seed: int, stream_id: int, sigma: float) -> None:
+    """Elements [first, first + n) of the seeded stream, encoded as ggml_type, into dst (uint8)."""
+    st = synth_lib().qmoe_synth_fill_host_range(_p(dst), int(ggml_type), first, n, seed, stream_id, sigma)
+    if st:
+        raise RuntimeError(f"synth_fill status {st}")
+
+
+# ---------------------------------------------------------------------------
 # The reference's own CUDA path (oracle/_ref/libqwenref.so), GPU box only.
 # ---------------------------------------------------------------------------
 _ref = None
@@ -192,3 +260,60 @@ def ref_moe_forward(dims, ptrs: list, types: list, nelem: list, x_ptr: int, out_
                                    x_ptr, out_ptr, P, Ty, N, stream)
     if st:
         raise RuntimeError("reference MoE path failed: " + ref_lib().ref_last_error().decode())
+
+
+# ---------------------------------------------------------------------------
+# Parity of a large batch (prefill sizes): routing of every token, outputs of
+# a sample of tokens.
+# ---------------------------------------------------------------------------
+def pick_sample(idx: np.ndarray, E: int, n_spread: int = 128, n_cold: int = 8, per_cold: int = 4,
+                every_expert: bool = True) -> np.ndarray:
+    """Token rows for the output check of a large batch: up to `per_cold`
+    tokens of each of the `n_cold` least-hit experts that are hit, the first
+    token of every hit expert (with `every_expert`), `n_spread` evenly spaced
+    tokens, and the first and last token.  The most-hit experts are in the sample through the
+    spread (under Zipf routing nearly every token holds the hottest one)."""
+    T = idx.shape[0]
+    valid = (idx >= 0) & (idx < E)
+    counts = np.bincount(idx[valid].ravel(), minlength=E)
+    hit = np.nonzero(counts)[0]
+    rows = set([0, T - 1])
+    rows.update(np.linspace(0, T - 1, num=min(n_spread, T), dtype=np.int64).tolist())
+    for e in hit[np.argsort(counts[hit], kind="stable")][:n_cold]:
+        rows.update(np.nonzero((idx == e).any(axis=1))[0][:per_cold].tolist())
+    if every_expert:
+        for e in hit:
+            rows.add(int(np.nonzero((idx == e).any(axis=1))[0][0]))
+    return np.array(sorted(rows), dtype=np.int64)
+
+
+def check_batch(tensors: dict, types: dict, dims, x: np.ndarray, got: dict, bias: np.ndarray | None = None,
+                sample: np.ndarray | None = None, atol: float = 1e-3, rtol: float = 1e-2) -> dict:
+    """Checks one block call of T tokens against the oracle.  got: device
+    results as numpy -- "logits" [T][E], "idx"/"w" [T][k], "offsets" [E+1],
+    "perm" [valid pairs], "out" [T][d] (out may be None).  Routing (logits
+    bit-exact, ids and selection order, permutation) is checked on every
+    token; outputs on `sample` (default: pick_sample of the oracle's ids)."""
+    E, k = dims.num_experts, dims.top_k
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    logits, idx, w = route(tensors["router"], types["router"], x, E, k, bias)
+    offs, perm, _ = dispatch(idx, E)
+    res = {"tokens": int(x.shape[0]),
+           "logits_bit_exact": bool(np.array_equal(np.asarray(got["logits"], np.float32).view(np.uint32),
+                                                   logits.view(np.uint32))),
+           "ids_bit_exact": bool(np.array_equal(got["idx"], idx)),
+           "weights_max_rel_err": float(np.max(np.abs(got["w"] - w) / np.maximum(np.abs(w), 1e-30))),
+           "offsets_bit_exact": bool(np.array_equal(got["offsets"], offs)),
+           "perm_bit_exact": bool(np.array_equal(np.asarray(got["perm"])[:perm.size], perm))}
+    if got.get("out") is not None:
+        if sample is None:
+            sample = pick_sample(idx, E)
+        want = moe_forward(tensors, types, dims, x[sample], bias)
+        rep = tolerance_report(np.asarray(got["out"])[sample], want["out"], atol, rtol)
+        rep["sample_tokens"] = int(sample.size)
+        rep["oracle_status_ok"] = bool(np.all(want["status"] == 0))
+        res["out"] = rep
+    res["routing_ok"] = (res["logits_bit_exact"] and res["ids_bit_exact"] and res["offsets_bit_exact"]
+                         and res["perm_bit_exact"] and res["weights_max_rel_err"] <= 2e-6)
+    res["within_tol"] = res["routing_ok"] and (res.get("out") is None or res["out"]["within_tol"])
+    return res

@@ -22,6 +22,7 @@
  *   - or_rmsnorm            src/cuda/ops.cu:25-65 (pre-MoE norm, model.cpp:208);
  *                           the reference scales by rsqrtf, a hardware
  *                           approximation, here 1/sqrtf (within 2 ulp)
+ *   - or_route_batch        layer_moe.cpp:98-99 + moe.cu:7-52 for T tokens
  *   - or_dispatch           no counterpart in the reference (single token);
  *                           stable counting sort of (token, slot) pairs by
  *                           expert, key order (expert, token, slot).
@@ -56,6 +57,16 @@ enum {
 };
 
 static int g_threads = 1;
+
+/* 1 inside a parallel region of this file (the token-parallel batch entry
+ * points), where the row-parallel GEMV runs on the calling thread alone. */
+static int or_in_parallel(void) {
+#ifdef _OPENMP
+    return omp_in_parallel();
+#else
+    return 0;
+#endif
+}
 
 OR_EXPORT void or_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
 OR_EXPORT int or_max_threads(void) {
@@ -190,7 +201,7 @@ OR_EXPORT int or_gemv(const uint8_t* w, int type, uint64_t num_elements, const f
     if (!w) return OR_ERR_ARG;
     if (!or_type_supported(type)) return OR_ERR_TYPE;
     if (M <= 0 || K <= 0 || element_offset + (uint64_t)M * (uint64_t)K > num_elements) return OR_ERR_SHAPE;
-#pragma omp parallel for num_threads(g_threads) if (g_threads > 1 && M >= 64) schedule(static)
+#pragma omp parallel for num_threads(g_threads) if (g_threads > 1 && M >= 64 && !or_in_parallel()) schedule(static)
     for (int row = 0; row < M; ++row)
         y[row] = or_gemv_row(w, type, x, K, element_offset + (uint64_t)row * (uint64_t)K);
     return OR_OK;
@@ -351,23 +362,46 @@ done:
     return st;
 }
 
-/* T tokens, one after another (the reference has no batched path: a batch is
- * T independent calls of MoeLayer::forward).  Returns the first error code;
- * status[t] (optional) receives each token's code. */
+/* Router logits (+ optional bias) and top-k of T tokens (layer_moe.cpp:98-99,
+ * moe.cu:7-52), the tokens in parallel (each token's arithmetic is the
+ * single-token order above, so the result does not depend on the threads).
+ * logits[T][E], idx/wts[T][k]. */
+OR_EXPORT void or_route_batch(const uint8_t* router, int type, uint64_t num_elements, const float* bias,
+                              int d, int E, int k, int T, const float* x, float* logits, int* idx, float* wts) {
+#pragma omp parallel for num_threads(g_threads) if (g_threads > 1 && T > 1) schedule(dynamic, 8)
+    for (int t = 0; t < T; ++t) {
+        float* lg = logits + (size_t)t * E;
+        or_gemv(router, type, num_elements, x + (size_t)t * d, lg, E, d, 0);
+        if (bias)
+            for (int e = 0; e < E; ++e) lg[e] = lg[e] + bias[e];
+        or_topk(lg, idx + (size_t)t * k, wts + (size_t)t * k, E, k);
+    }
+}
+
+/* T tokens (the reference has no batched path: a batch is T independent
+ * calls of MoeLayer::forward).  With more than one thread and T > 1 the
+ * tokens run in parallel, each with the single-token arithmetic, so the
+ * results are the same as one after another.  Returns the first error code
+ * in token order; status[t] (optional) receives each token's code. */
 OR_EXPORT int or_moe_forward_batch(const or_block* W, int d, int E, int k, int F, int Fs, int T,
                                    const float* x, float* out, int* idx, float* wts, int* status,
                                    float* logits_out, float* h_out, float* hs_out, float* sgate_out) {
     int first = OR_OK;
+    int* codes = (int*)malloc(sizeof(int) * (size_t)(T > 0 ? T : 1));
+#pragma omp parallel for num_threads(g_threads) if (g_threads > 1 && T > 1) schedule(dynamic, 1)
     for (int t = 0; t < T; ++t) {
-        int st = or_moe_forward(W, d, E, k, F, Fs, x + (size_t)t * d, out + (size_t)t * d,
+        codes[t] = or_moe_forward(W, d, E, k, F, Fs, x + (size_t)t * d, out + (size_t)t * d,
                                 idx + (size_t)t * k, wts + (size_t)t * k,
                                 logits_out ? logits_out + (size_t)t * E : NULL,
                                 h_out ? h_out + (size_t)t * k * F : NULL,
                                 hs_out ? hs_out + (size_t)t * Fs : NULL,
                                 sgate_out ? sgate_out + t : NULL);
-        if (status) status[t] = st;
-        if (st != OR_OK && first == OR_OK) first = st;
     }
+    for (int t = 0; t < T; ++t) {
+        if (status) status[t] = codes[t];
+        if (codes[t] != OR_OK && first == OR_OK) first = codes[t];
+    }
+    free(codes);
     return first;
 }
 

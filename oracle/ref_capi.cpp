@@ -6,6 +6,8 @@
 #include "matmul_q4.hpp"
 #include "ops.hpp"
 #include <cstring>
+#include <stdexcept>
+#include <vector>
 #include <exception>
 #include <string>
 
@@ -91,6 +93,70 @@ int ref_moe_forward(int d, int E, int k, int F, int Fs, int T, const float* x, f
         ctx.synchronize();
         return 0;
     } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+// A stack of L MoE layers run the way model.cpp:207-211 runs the MoE half of
+// each decoder layer (rmsnorm_forward -> MoeLayer::forward -> residual_add),
+// for timing the reference's own GPU path.  The layers are created once
+// (MoeLayer::init allocates its buffers); tensors: 8 per layer as in
+// ref_moe_forward, layer-major.
+struct RefStack {
+    int L = 0, d = 0;
+    qwen::ModelConfig cfg;
+    std::vector<qwen::QuantTensor> t;
+    std::vector<qwen::MoeLayer*> layers;
+    float *normed = nullptr, *moe_out = nullptr;
+};
+
+void* ref_stack_create(int L, int d, int E, int k, int F, int Fs, const void* const* ptrs, const int* types,
+                       const unsigned long long* nelem) {
+    try {
+        RefStack* s = new RefStack();
+        s->L = L;
+        s->d = d;
+        s->cfg.d_model = d;
+        s->cfg.num_experts = E;
+        s->cfg.num_experts_per_tok = k;
+        s->cfg.moe_intermediate_dim = F;
+        s->cfg.shared_expert_dim = Fs;
+        static const char* names[8] = {"ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps",
+                                       "ffn_gate_inp_shexp", "ffn_gate_shexp", "ffn_up_shexp", "ffn_down_shexp"};
+        for (int l = 0; l < L; ++l) {
+            for (int i = 0; i < 8; ++i) s->t.push_back(make_tensor(names[i], ptrs[8 * l + i], types[8 * l + i], nelem[8 * l + i]));
+            s->layers.push_back(new qwen::MoeLayer());
+            s->layers.back()->init(s->cfg, l);
+        }
+        if (cudaMalloc(&s->normed, sizeof(float) * d) != cudaSuccess ||
+            cudaMalloc(&s->moe_out, sizeof(float) * d) != cudaSuccess)
+            throw std::runtime_error("ref_stack_create: cudaMalloc failed");
+        return s;
+    } catch (const std::exception& e) { g_last_error = e.what(); return nullptr; }
+}
+
+// One token through the stack: x (device F32[d], the residual stream) is
+// updated in place; norm_w = the post-attention norm weight (F32[d]).
+int ref_stack_forward(void* handle, float* x, const float* norm_w, float eps, void* stream) {
+    try {
+        RefStack* s = static_cast<RefStack*>(handle);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        qwen::CudaContext ctx(st);
+        for (int l = 0; l < s->L; ++l) {
+            const qwen::QuantTensor* t = &s->t[8 * l];
+            qwen::rmsnorm_forward(x, norm_w, s->normed, s->d, eps, st);
+            s->layers[l]->forward(s->normed, s->moe_out, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[7], ctx);
+            qwen::residual_add(x, s->moe_out, x, s->d, st);
+        }
+        return 0;
+    } catch (const std::exception& e) { g_last_error = e.what(); return 1; }
+}
+
+void ref_stack_destroy(void* handle) {
+    RefStack* s = static_cast<RefStack*>(handle);
+    if (!s) return;
+    for (auto* l : s->layers) delete l;
+    cudaFree(s->normed);
+    cudaFree(s->moe_out);
+    delete s;
 }
 
 }  // extern "C"

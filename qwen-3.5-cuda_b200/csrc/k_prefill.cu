@@ -136,21 +136,25 @@ __device__ __forceinline__ uint4 pack_chunk(const float (&v)[8]) {
 // Two chunks (16 values) of one sub-block of a Q4_K row from a producer
 // thread's staged raw bytes: the block header (d, dmin, 12 scale bytes) and
 // 16 qs bytes of the 64-element group; sub-block j uses the low (j even) or
-// high nibbles.  value = d*sc*q - dmin*m (matmul_q4.cu:76-96), evaluated in
-// fp16 as (q*(d*sc)) - dmin*m after an exact nibble-to-half conversion.
+// high nibbles.  value = d*sc*q - dmin*m (matmul_q4.cu:76-96), rounded to
+// fp16 once as ((q - 8) * sc) * d + (8*d*sc - dmin*m): the first product is an
+// exact fp16 integer, d the block's own fp16 scale, one fused half2
+// multiply-add rounds the sum (the same evaluation as the TMA GEMM's).
 __device__ __forceinline__ void dq_q4k_raw(uint32_t raw, int j, uint4 (&out)[2]) {
     const uint4 hd = lds128(raw);
     const uint4 q = lds128(raw + 16);
     float sc, m;
     kscale(hd.y, hd.z, hd.w, j, sc, m);
     const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
-    const __half2 a = __float2half2_rn(d * sc), nb = __float2half2_rn(-(dmin * m));
-    const __half2 k1024 = __float2half2_rn(1024.0f);
+    const __half2 d2 = bits_h2((hd.x & 0xFFFFu) * 0x00010001u);
+    const __half2 sc2 = __float2half2_rn(sc);
+    const __half2 c2 = __float2half2_rn(fmaf(8.0f * d, sc, -(dmin * m)));
+    const __half2 k1032 = __float2half2_rn(1032.0f);
     const int sh = (j & 1) * 4;
     // half2(1024 + n(byte e), 1024 + n(byte e+2)) from one word: element order 0,2 / 1,3
     auto cvt = [&](uint32_t w) {
         const __half2 raw2 = bits_h2(((w >> sh) & 0x000F000Fu) | 0x64006400u);
-        return h2_bits(__hfma2(__hsub2(raw2, k1024), a, nb));
+        return h2_bits(__hfma2(__hmul2(__hsub2(raw2, k1032), sc2), d2, c2));
     };
     out[0] = make_uint4(cvt(q.x), cvt(q.x >> 8), cvt(q.y), cvt(q.y >> 8));
     out[1] = make_uint4(cvt(q.z), cvt(q.z >> 8), cvt(q.w), cvt(q.w >> 8));

@@ -106,6 +106,15 @@ __device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint3
 // Sub-block H (0: low nibbles, 1: high) of group g of one Q4_K super-block
 // (raw row in shared memory) -> 32 fp16 values = chunks 4H..4H+3 of row r of
 // the operand slot (128-byte rows, chunk c stored at c ^ (r % 8)).
+//
+// The value d*sc*q - dmin*m (matmul_q4.cu:76-96) is rounded to fp16 once:
+// written as ((q - 8) * sc) * d + (8*d*sc - dmin*m), the first product is an
+// integer of at most 504 in magnitude (exact in fp16), d is the block's own
+// fp16 scale, and one fused half2 multiply-add rounds the sum.  The constant
+// c = 8*d*sc - dmin*m (computed in F32) is about half a quantisation step, so
+// its own fp16 rounding is small.  (Rounding d*sc and dmin*m to fp16 first
+// and applying them to q doubles the error of the products, and the error is
+// shared by the sub-block's 32 weights and every token.)
 template <int H>
 __device__ __forceinline__ void dq_sub(uint32_t raw, int g, uint32_t brow, int r) {
     const uint4 hd = lds128(raw);
@@ -114,13 +123,15 @@ __device__ __forceinline__ void dq_sub(uint32_t raw, int g, uint32_t brow, int r
     float sc, m;
     kscale(hd.y, hd.z, hd.w, 2 * g + H, sc, m);
     const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
-    const __half2 a = __float2half2_rn(d * sc), nb = __float2half2_rn(-(dmin * m));
-    const __half2 k1024 = __float2half2_rn(1024.0f);
+    const __half2 d2 = bits_h2((hd.x & 0xFFFFu) * 0x00010001u);  // the fp16 d, both halves
+    const __half2 sc2 = __float2half2_rn(sc);                     // integer 0..63: exact
+    const __half2 c2 = __float2half2_rn(fmaf(8.0f * d, sc, -(dmin * m)));
+    const __half2 k1032 = __float2half2_rn(1032.0f);
     const int sh = 4 * H;
     // half2(1024 + n(byte e), 1024 + n(byte e+2)): element order 0,2 / 1,3
     auto cvt = [&](uint32_t w) {
         const __half2 raw2 = bits_h2(((w >> sh) & 0x000F000Fu) | 0x64006400u);
-        return h2_bits(__hfma2(__hsub2(raw2, k1024), a, nb));
+        return h2_bits(__hfma2(__hmul2(__hsub2(raw2, k1032), sc2), d2, c2));
     };
     const uint32_t x7 = static_cast<uint32_t>(r & 7);
     sts128(brow + (((4 * H + 0) ^ x7) << 4), cvt(q0.x), cvt(q0.x >> 8), cvt(q0.y), cvt(q0.y >> 8));

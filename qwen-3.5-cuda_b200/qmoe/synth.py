@@ -135,3 +135,38 @@ def inputs(n_tokens: int, d: int, seed: int, tag: int = 0, device: str = "cuda")
     b = torch.empty(n * 4, dtype=torch.uint8, device=device)
     fill(b, GgmlType.F32, n, seed, input_stream_id(tag), 1.0)
     return b.view(torch.float32).view(n_tokens, d)
+
+
+def zipf_bias(E: int, k: int, d: int, s: float = 1.1, seed: int = 1238, sigma: float = WEIGHT_SIGMA,
+              sample: int = 4096, iters: int = 60):
+    """Per-expert router logit bias under which the expert hit histogram
+    follows Zipf(s) (benchmark configs 4 and 5): the expert of popularity rank
+    r (a seeded permutation) gets a share proportional to r^-s of the T*k
+    pairs, capped at one pair per token (the capped head's overflow spread
+    over the rest).  Calibrated on a seeded sample of the benchmark's input
+    distribution (x ~ N(0,1), router rows ~ N(0, sigma^2)) by a damped
+    fixed-point iteration on log(target count) - log(sample count).
+    Deterministic; about a second of host time.  Returns (bias F32[E],
+    expected pairs per token of each expert)."""
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((E, d)) * sigma).astype(np.float32)
+    X = rng.standard_normal((sample, d)).astype(np.float32)
+    logits = X @ W.T
+    ranks = rng.permutation(E) + 1
+    z = np.arange(1, E + 1, dtype=np.float64) ** -s
+    z = z / z.sum() * sample * k
+    for _ in range(64):
+        over = np.clip(z - sample, 0, None).sum()
+        z = np.minimum(z, sample)
+        free = z < sample
+        if over <= 0 or not free.any():
+            break
+        z[free] += over * z[free] / z[free].sum()
+    target = np.minimum(z[ranks - 1], sample - 0.5)
+    b = -s * np.log(ranks) * 0.5
+    for _ in range(iters):
+        idx = np.argpartition(-(logits + b[None, :]), k, axis=1)[:, :k]
+        cnt = np.bincount(idx.ravel(), minlength=E).astype(np.float64)
+        b += 0.5 * (np.log(target) - np.log(np.maximum(cnt, 0.5)))
+        b -= b.max()
+    return b.astype(np.float32), target / sample
