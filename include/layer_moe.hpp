@@ -25,8 +25,10 @@ public:
     void free_buffers();
 
     // out[d_model] = MoE(x[d_model]) for one token (device pointers), enqueued on
-    // ctx.stream() without synchronising.  Routing errors are recorded on the
-    // device; check_routing() reports them with the reference's exceptions.
+    // ctx.stream() without synchronising.  Errors of a call are recorded on the
+    // device and in a host-mapped word; the next forward() throws them
+    // (std::runtime_error, the reference's messages for routing errors) after
+    // re-initialising the workspace, and check_routing() reports them at once.
     void forward(const float* x, float* out, const QuantTensor& router, const QuantTensor& eg,
                  const QuantTensor& eu, const QuantTensor& ed, const QuantTensor& sgate,
                  const QuantTensor& sg, const QuantTensor& su, const QuantTensor& sd, const CudaContext& ctx);
@@ -41,6 +43,10 @@ private:
     qmoe_dims dims_{};
     void* ws_ = nullptr;
     size_t ws_bytes_ = 0;
+    uint32_t* err_host_ = nullptr;  // host-mapped error word of the kernels (qmoe_workspace_set_error_sink)
+    uint32_t* err_dev_ = nullptr;   // its device address
+
+    void throw_flags(uint32_t flags, const CudaContext* ctx);
 };
 
 }  // namespace qwen

@@ -156,9 +156,11 @@ QMOE_API int qmoe_dispatch(const int32_t* topk_idx, int T, int k, int E,
  * Its scratch is a fixed array inside the library, 32 KiB per device, which
  * limits it to num_experts <= 256; larger E returns QMOE_ERR_UNSUPPORTED.
  * Nothing has to start at zero: every call clears the scratch it uses.
- * The first call on a device looks up the scratch's address with that device
- * current (cudaGetSymbolAddress); make that first call before capturing a
- * stream.  All calls on a device share the scratch, so two calls that
+ * Every call looks up the scratch's address in the current device context
+ * (cudaGetSymbolAddress, a host-side query that allocates nothing); make the
+ * first call on a device before capturing a stream, since the library's
+ * module is loaded on that device by the first call.  All calls on a device
+ * share the scratch, so two calls that
  * overlap in time race: order them on one stream, or synchronise between
  * streams. */
 QMOE_API int qmoe_dispatch_noalloc(const int32_t* topk_idx, int T, int k, int E,
@@ -303,8 +305,30 @@ QMOE_API int qmoe_check_errors(void* workspace, const qmoe_dims* dims, uint32_t*
 QMOE_API int qmoe_trace_enable(uint64_t* device_buffer, size_t bytes);
 QMOE_API size_t qmoe_trace_bytes(void);
 
-/* Clears the workspace control words (call once after allocating it). */
+/* Clears the workspace control words (call once after allocating it, and
+ * again after a call reported QMOE_ERR_TIMEOUT).  It also removes an error
+ * sink (below). */
 QMOE_API int qmoe_workspace_init(void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* Registers a host-mapped 32-bit word (a device-accessible pointer from
+ * cudaHostAlloc(..., cudaHostAllocMapped) + cudaHostGetDevicePointer) into
+ * which the kernels OR the same error flags they record in the workspace
+ * (1 routing, 2 weights not normalised, 4 timed-out wait, 8 misaligned copy).
+ * The host can then notice a failed call by reading that word, without
+ * synchronising the stream -- the reference throws from MoeLayer::forward
+ * after a stream synchronisation (src/layer_moe.cpp:106-124); the shim in
+ * this library throws at its next forward instead.  NULL removes the sink.
+ * Stream-ordered; qmoe_workspace_init clears it. */
+QMOE_API int qmoe_workspace_set_error_sink(void* workspace, uint32_t* sink, qmoe_stream_t stream);
+
+/* Test hook for the bounded grid-barrier wait of the fused decode kernel (no
+ * counterpart in the reference): later launches wait at most `wait_ns`
+ * nanoseconds (0 restores the default, 200 ms) and wait for
+ * `phantom_arrivals` extra CTAs that never arrive (0 = normal operation;
+ * > 0 makes the wait run out, so a test can check that the kernel returns
+ * and reports QMOE_ERR_TIMEOUT instead of hanging).  Process-wide; not for
+ * use while other threads launch. */
+QMOE_API int qmoe_debug_grid_barrier(uint64_t wait_ns, int phantom_arrivals);
 
 /* Synthetic tensors for tests and benchmarks: elements sigma*N(0,1) from a
  * counter-based stream (seed, stream_id), encoded as `ggml_type`.  The device

@@ -206,7 +206,7 @@ __device__ void topk_and_schedule(const DecodeParams& P, int* sched, float* w_ou
         uint32_t flag;
         select_token(P.logits + t * LS, E, k, lane, my_idx, wj, flag);
         if (publish && flag && lane == 0) {
-            atomicOr(P.ctrl + CTRL_ERROR, flag);
+            raise_error(P.ctrl, flag);
             atomicMin(P.ctrl + CTRL_ERR_TOKEN, static_cast<uint32_t>(t));
         }
         if (lane < k) {
@@ -887,6 +887,8 @@ struct FxLayout {
     int gnst, gsub, dnst, Rd, nvec;
     uint32_t half_bytes, dstage;
     uint32_t off_sched, off_xs, off_hb, off_w, off_sg, off_res, off_yb, off_gu, off_dn;
+    uint64_t wait_ns;  // bound of the grid barrier's wait
+    int phantom;       // extra arrivals the barrier waits for (0; > 0 only to test the bounded wait)
 };
 
 __device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* p) {
@@ -1142,12 +1144,13 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
         unsigned long long* ctr = reinterpret_cast<unsigned long long*>(P.ctrl + CTRL_GRID_CTR);
         uint64_t old;
         asm volatile("atom.add.acq_rel.gpu.u64 %0, [%1], %2;" : "=l"(old) : "l"(ctr), "l"(1ull) : "memory");
-        const uint64_t target = (old / static_cast<uint64_t>(G) + 1u) * static_cast<uint64_t>(G);
+        const uint64_t target = (old / static_cast<uint64_t>(G) + 1u) * static_cast<uint64_t>(G) +
+                                static_cast<uint64_t>(L.phantom);
         if (old + 1u != target) {
             const uint64_t t0 = gtimer();
             while (ld_acquire_u64(ctr) < target) {
-                if (gtimer() - t0 > kGridWaitNs) {
-                    atomicOr(P.ctrl + CTRL_ERROR, EF_TIMEOUT);
+                if (gtimer() - t0 > L.wait_ns) {
+                    raise_error(P.ctrl, EF_TIMEOUT);
                     break;
                 }
                 __nanosleep(32);
@@ -1416,8 +1419,20 @@ cudaError_t launch_gateup(const DecodeParams& P, cudaStream_t s) {
 }
 
 // ---- fused expert kernel ----
+// Bound of the fused kernel's grid-barrier wait and extra arrivals it waits
+// for (qmoe_debug_grid_barrier; defaults kGridWaitNs and 0).
+static uint64_t g_grid_wait_ns = kGridWaitNs;
+static int g_grid_phantom = 0;
+
+void set_grid_barrier_limits(uint64_t wait_ns, int phantom) {
+    g_grid_wait_ns = wait_ns ? wait_ns : kGridWaitNs;
+    g_grid_phantom = phantom > 0 ? phantom : 0;
+}
+
 static bool plan_fused(const DecodeParams& P, FxLayout& L, size_t& smem, int& grid) {
     DevCache& dc = dev_cache();
+    L.wait_ns = g_grid_wait_ns;
+    L.phantom = g_grid_phantom;
     if (dc.sms <= 0 || dc.smem_optin <= 0) return false;  // no usable device
     if (P.F % ITEM_ROWS || P.Fs % ITEM_ROWS) return false;
     grid = dc.sms;
@@ -1484,11 +1499,25 @@ static FxKern pick_fused(int tr, int ts, int dr, int ds) {
     return nullptr;
 }
 
+// The fused kernel's grid barrier needs every CTA resident at once: it is
+// used only when the device supports cooperative launches and its occupancy
+// holds the whole grid (it is then launched cooperatively, so the driver
+// refuses rather than runs it when the SMs are not available).
+static bool fused_fits(FxKern kern, size_t smem, int grid) {
+    int dev = 0, coop = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) return false;
+    if (set_smem(kern, smem) != cudaSuccess) return false;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FX_THREADS, smem) != cudaSuccess) return false;
+    return per_sm * dev_cache().sms >= grid;
+}
+
 bool fused_supported(const DecodeParams& P) {
     FxLayout L;
     size_t smem;
     int grid;
-    return pick_fused(P.gate.type, P.sgate.type, P.down.type, P.sdown.type) && plan_fused(P, L, smem, grid);
+    FxKern kern = pick_fused(P.gate.type, P.sgate.type, P.down.type, P.sdown.type);
+    return kern && plan_fused(P, L, smem, grid) && fused_fits(kern, smem, grid);
 }
 
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s) {
@@ -1499,7 +1528,21 @@ cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s) {
     if (!kern || !plan_fused(P, L, smem, grid)) return cudaErrorInvalidValue;
     cudaError_t e = set_smem(kern, smem);
     if (e != cudaSuccess) return e;
-    return launch(kern, grid, FX_THREADS, smem, s, P, L);
+    // cooperative: all CTAs are resident together (the grid barrier's
+    // requirement) or the launch is refused
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(FX_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dev_cache().pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, P, L);
 }
 
 cudaError_t launch_down(const DecodeParams& P, cudaStream_t s) {

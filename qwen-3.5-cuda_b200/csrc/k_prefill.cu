@@ -771,7 +771,7 @@ __global__ void __launch_bounds__(256) k_topk_many(const float* __restrict__ log
     uint32_t flag;
     select_token(logits + static_cast<size_t>(t) * (E + 1), E, k, lane, my_idx, wj, flag);
     if (flag && lane == 0) {
-        atomicOr(ctrl + CTRL_ERROR, flag);
+        raise_error(ctrl, flag);
         atomicMin(ctrl + CTRL_ERR_TOKEN, static_cast<uint32_t>(t));
     }
     if (lane < k) {

@@ -1,7 +1,6 @@
 // extern "C" entry points of include/qmoe.h: argument checks (the reference's
 // host-side exceptions become status codes), workspace layout, launches.
 #include <algorithm>
-#include <atomic>
 #include <cstring>
 #include "qmoe_dev.cuh"
 #include "qmoe_internal.h"
@@ -31,6 +30,7 @@ cudaError_t launch_ep_dispatch(const int32_t* idx, const int32_t* placement, int
                                int32_t* pair_pos, void* scratch, cudaStream_t s);
 cudaError_t launch_ep_qmap(const int32_t* meta, int n, int k, int32_t* qblk, int32_t* qmap, cudaStream_t s);
 cudaError_t launch_experts(const DecodeParams& P, cudaStream_t s);
+void set_grid_barrier_limits(uint64_t wait_ns, int phantom);
 int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
                         cudaStream_t s);
@@ -41,6 +41,10 @@ cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets,
                             int32_t* table, cudaStream_t s);
 size_t dispatch_scratch_bytes(int E);
 cudaError_t dispatch_noalloc_scratch(int32_t** p);
+
+__global__ void k_set_sink(uint32_t* ctrl, unsigned long long sink) {
+    *reinterpret_cast<unsigned long long*>(ctrl + CTRL_SINK) = sink;
+}
 
 __global__ void k_ws_init(uint32_t* ctrl) {
     const int i = threadIdx.x;
@@ -265,6 +269,19 @@ int qmoe_workspace_init(void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     return cuda_status(cudaGetLastError());
 }
 
+int qmoe_workspace_set_error_sink(void* ws, uint32_t* sink, qmoe_stream_t stream) {
+    if (!ws) return QMOE_ERR_WORKSPACE;
+    k_set_sink<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint32_t*>(ws), static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(sink)));
+    return cuda_status(cudaGetLastError());
+}
+
+int qmoe_debug_grid_barrier(uint64_t wait_ns, int phantom_arrivals) {
+    if (phantom_arrivals < 0) return QMOE_ERR_ARG;
+    set_grid_barrier_limits(wait_ns, phantom_arrivals);
+    return QMOE_OK;
+}
+
 int qmoe_router_topk(const qmoe_block* B, const qmoe_dims* D, const float* x, int T, int32_t* topk_idx,
                      float* topk_w, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
     int st = check_common(B, D, T, ws, ws_bytes, kDecodeMaxT);
@@ -285,22 +302,16 @@ int qmoe_dispatch(const int32_t* idx, int T, int k, int E, int32_t* offsets, int
                                        reinterpret_cast<cudaStream_t>(stream)));
 }
 
-// Address of the fixed dispatch scratch on each device, looked up on the
-// first call made with that device current.
-static std::atomic<int32_t*> g_noalloc_scratch[64];
-
 int qmoe_dispatch_noalloc(const int32_t* idx, int T, int k, int E, int32_t* offsets, int32_t* perm,
                           int32_t* inv_perm, qmoe_stream_t stream) {
     if (!idx || !offsets || !perm || T <= 0 || k <= 0 || E <= 0) return QMOE_ERR_ARG;
     if (E > kNoAllocMaxExperts) return QMOE_ERR_UNSUPPORTED;  // the fixed scratch holds E <= 256
     if (static_cast<int64_t>(T) * k > (1ll << 30)) return QMOE_ERR_UNSUPPORTED;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QMOE_ERR_CUDA;
-    int32_t* table = g_noalloc_scratch[dev].load(std::memory_order_acquire);
-    if (!table) {
-        if (dispatch_noalloc_scratch(&table) != cudaSuccess || !table) return QMOE_ERR_CUDA;
-        g_noalloc_scratch[dev].store(table, std::memory_order_release);
-    }
+    // the scratch array's device address in the current context, looked up on
+    // every call (a host-side query, no allocation): a cached address would
+    // be stale after cudaDeviceReset or in another context of the device
+    int32_t* table = nullptr;
+    if (dispatch_noalloc_scratch(&table) != cudaSuccess || !table) return QMOE_ERR_CUDA;
     return cuda_status(launch_dispatch(idx, T * k, E, offsets, perm, inv_perm, table,
                                        reinterpret_cast<cudaStream_t>(stream)));
 }

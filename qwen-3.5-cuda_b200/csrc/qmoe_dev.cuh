@@ -25,8 +25,18 @@ enum : int {
     CTRL_N_ACTIVE = 3,   // number of experts with >= 1 routed pair
     CTRL_N_PAIRS = 4,    // number of valid pairs
     CTRL_GRID_CTR = 6,   // words 6-7: 64-bit arrival count of the fused expert kernel's grid barrier
+    CTRL_SINK = 8,       // words 8-9: device address of a host-mapped error word (0 = none)
     CTRL_WORDS = 64
 };
+
+// Records error flags in the workspace error word and, when the caller has
+// registered one (qmoe_workspace_set_error_sink), in its host-mapped word, so
+// that a host can notice an error without synchronising the stream.
+__device__ __forceinline__ void raise_error(uint32_t* ctrl, uint32_t flag) {
+    atomicOr(ctrl + CTRL_ERROR, flag);
+    const unsigned long long sink = *reinterpret_cast<volatile unsigned long long*>(ctrl + CTRL_SINK);
+    if (sink) atomicOr_system(reinterpret_cast<unsigned int*>(sink), flag);
+}
 
 // ---------------------------------------------------------------------------
 // Small math / bit helpers
@@ -99,7 +109,7 @@ constexpr uint32_t kWaitLimit = 1u << 14;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* ctrl) {
     for (uint32_t i = 0; i < kWaitLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-    if (ctrl) atomicOr(ctrl + CTRL_ERROR, EF_TIMEOUT);
+    if (ctrl) raise_error(ctrl, EF_TIMEOUT);
     return false;
 }
 
@@ -115,7 +125,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
                                          uint32_t* ctrl) {
     if (((smem_u32(smem_dst) | static_cast<uint32_t>(reinterpret_cast<uintptr_t>(gmem_src)) | bytes) & 15u) != 0) {
-        if (ctrl) atomicOr(ctrl + CTRL_ERROR, EF_ALIGN);
+        if (ctrl) raise_error(ctrl, EF_ALIGN);
         return;
     }
     asm volatile(

@@ -96,6 +96,8 @@ SIGNATURES = [
     ("qmoe_trace_enable", c_int, [c_void_p, c_size_t]),
     ("qmoe_trace_bytes", c_size_t, []),
     ("qmoe_workspace_init", c_int, [c_void_p, c_size_t, c_void_p]),
+    ("qmoe_workspace_set_error_sink", c_int, [c_void_p, c_void_p, c_void_p]),
+    ("qmoe_debug_grid_barrier", c_int, [c_uint64, c_int]),
     ("qmoe_synth_fill", c_int, [c_void_p, c_uint32, c_uint64, c_uint64, c_uint64, c_float, c_void_p]),
     ("qmoe_synth_fill_host", c_int, [c_void_p, c_uint32, c_uint64, c_uint64, c_uint64, c_float]),
     ("qmoe_synth_fill_host_range", c_int, [c_void_p, c_uint32, c_uint64, c_uint64, c_uint64, c_uint64, c_float]),

@@ -115,11 +115,28 @@ class ExpertParallelMoE:
         flat = out.tolist()
         return [flat[s * 2 * G:(s + 1) * 2 * G] for s in range(G)]
 
+    def _route_dispatch(self, x):
+        """route + dispatch, or -- when this rank's batch exceeds the planned
+        size -- counts of -1, so that every rank learns of the error from the
+        count exchange that follows (no rank raises alone and leaves the
+        others waiting in a collective)."""
+        import torch
+        be, G = self.backend, self.world
+        if x.shape[0] > be.max_tokens:
+            return None, None, torch.full((2 * G,), -1, dtype=torch.int32, device=x.device), None
+        be.route(x)
+        return be.dispatch(G)
+
+    @staticmethod
+    def _check_counts(rows):
+        if any(c < 0 for row in rows for c in row):
+            raise ValueError("expert-parallel forward: a rank's batch exceeds the planned max_tokens")
+
     def _forward_direct(self, x, residual):
         be, G, me = self.backend, self.world, self.rank
-        be.route(x)
-        send_rows, send_meta, counts, pair_pos = be.dispatch(G)
+        send_rows, send_meta, counts, pair_pos = self._route_dispatch(x)
         C = self.gather_counts(counts)  # the one host synchronisation of the call
+        self._check_counts(C)
         s_rows = C[me][:G]
         r_rows = [C[s][me] for s in range(G)]
         r_pairs = [C[s][G + me] for s in range(G)]
@@ -166,9 +183,9 @@ class ExpertParallelMoE:
         if self.direct:
             return self._forward_direct(x, residual)
         be = self.backend
-        be.route(x)
-        send_rows, send_meta, counts, pair_pos = be.dispatch(self.world)
+        send_rows, send_meta, counts, pair_pos = self._route_dispatch(x)
         s_rows, s_pairs, r_rows, r_pairs = self.exchange_counts(counts)
+        self._check_counts([s_rows, s_pairs, r_rows, r_pairs])
         ns = sum(s_rows)
         recv_rows = self._a2a(send_rows[:ns], s_rows, r_rows)
         recv_meta = self._a2a(send_meta[:ns], s_rows, r_rows)
@@ -189,6 +206,7 @@ class CudaBackend:
         self.dims, self.local_dims = dims, local_dims
         self.norm_weight, self.eps = norm_weight, eps
         self.world = world
+        self.max_tokens = max_tokens
         L = _lib.lib()
         k, d = dims.top_k, dims.d_model
         self.ws_bytes = L.qmoe_workspace_size(ctypes.byref(dims), max_tokens)
@@ -322,8 +340,10 @@ class CudaBackend:
             n = C[me][r]
             if n:
                 at = sum(C[s][r] for s in range(me))
-                if at + n > self.recv_cap:
-                    raise ValueError("expert-parallel receive buffer too small")
+                # holds by construction: a rank sends each of its <= max_tokens
+                # tokens to a rank at most once, and the buffer has room for
+                # every rank's max_tokens rows
+                assert at + n <= self.recv_cap, "expert-parallel receive buffer too small"
                 _lib.check(L.qmoe_copy_async(self.peer_rows[r] + at * d * 2, send_rows.data_ptr() + src * d * 2,
                                              n * d * 2, stream), "copy_async")
                 _lib.check(L.qmoe_copy_async(self.peer_meta[r] + at * k * 4, send_meta.data_ptr() + src * k * 4,

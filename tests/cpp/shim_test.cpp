@@ -184,6 +184,37 @@ int main() {
     layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx);
     layer.check_routing(ctx);
 
+    // without check_routing: the next forward() throws the earlier call's error
+    // (host-mapped error word, no synchronisation inside forward), and the one
+    // after it works again
+    layer.forward(dnan, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx);
+    CUDA_CHECK(cudaStreamSynchronize(ctx.stream()));  // the kernels have run
+    expect_throw([&] { layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx); },
+                 "invalid/non-finite MoE routing result in layer 3");
+    layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx);
+    layer.check_routing(ctx);
+    CUDA_CHECK(cudaMemcpy(y.data(), dy, sizeof(float) * d, cudaMemcpyDeviceToHost));
+    bad = 0;
+    for (int i = 0; i < d; ++i) bad += close(y[i], want[i]) ? 0 : 1;
+    CHECK(bad == 0, "after a reported error: %d of %d MoE outputs outside tolerance", bad, d);
+
+    // a grid-barrier wait that runs out (the test hook makes the fused decode
+    // kernel wait for one CTA that never arrives, for 1 ms): the kernel
+    // returns, the next forward() reports the timeout, and after it the layer
+    // computes correctly again
+    CHECK(qmoe_debug_grid_barrier(1000000ull, 1) == QMOE_OK, "debug hook");
+    layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx);
+    CUDA_CHECK(cudaStreamSynchronize(ctx.stream()));
+    CHECK(qmoe_debug_grid_barrier(0, 0) == QMOE_OK, "debug hook reset");
+    expect_throw([&] { layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx); },
+                 "MoE layer 3: device-side wait timed out");
+    layer.forward(dx, dy, router.q, eg.q, eu.q, ed.q, sgate.q, sg.q, su.q, sd.q, ctx);
+    layer.check_routing(ctx);
+    CUDA_CHECK(cudaMemcpy(y.data(), dy, sizeof(float) * d, cudaMemcpyDeviceToHost));
+    bad = 0;
+    for (int i = 0; i < d; ++i) bad += close(y[i], want[i]) ? 0 : 1;
+    CHECK(bad == 0, "after a barrier timeout: %d of %d MoE outputs outside tolerance", bad, d);
+
     std::printf(g_fail ? "shim_test: %d failures\n" : "shim_test: all checks passed\n", g_fail);
     return g_fail ? 1 : 0;
 }

@@ -61,8 +61,9 @@ class FakeBackend:
     """route / dispatch / experts / combine with the semantics of the
     qmoe_ep_* calls, on the host."""
 
-    def __init__(self, E: int, lo: int, seed: int):
+    def __init__(self, E: int, lo: int, seed: int, max_tokens: int = 1 << 20):
         self.E, self.lo, self.seed = E, lo, seed
+        self.max_tokens = max_tokens
         self.received = 0
 
     def route(self, x):
@@ -133,24 +134,28 @@ class FakeBackend:
         return torch.from_numpy(out)
 
 
-def _worker(rank, world, port, E, token_counts, seed, q, shm_name=None):
+def _worker(rank, world, port, E, token_counts, seed, q, shm_name=None, max_tokens=1 << 20):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         lo, hi = ep.shard_bounds(E, world, rank)
-        be = FakeBackend(E, lo, seed)
+        be = FakeBackend(E, lo, seed, max_tokens)
         be.shm_name, be.cap, be.rcap = shm_name, max(token_counts) * K, sum(token_counts)
         moe = ep.ExpertParallelMoE(be, E, K, D, direct=shm_name is not None)
         x = np.random.default_rng(100 + rank).standard_normal((token_counts[rank], D)).astype(np.float32)
-        out = moe.forward(torch.from_numpy(x)).numpy()
+        try:
+            out = moe.forward(torch.from_numpy(x)).numpy()
+        except ValueError as err:  # every rank must see a batch-size error, none may hang
+            q.put((rank, "error", str(err), 0))
+            return
         ref = _reference(x, E, seed)
         q.put((rank, float(np.abs(out - ref).max()) if out.size else 0.0, out.shape, be.received))
     finally:
         dist.destroy_process_group()
 
 
-def _run(world, E, token_counts, seed=5, direct=False):
+def _run(world, E, token_counts, seed=5, direct=False, max_tokens=1 << 20):
     from multiprocessing import shared_memory
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -158,7 +163,8 @@ def _run(world, E, token_counts, seed=5, direct=False):
     size = world * (max(token_counts) * K * D + sum(token_counts) * (D + K)) * 4
     shm = shared_memory.SharedMemory(create=True, size=size) if direct else None
     try:
-        ps = [ctx.Process(target=_worker, args=(r, world, port, E, token_counts, seed, q, shm.name if shm else None))
+        ps = [ctx.Process(target=_worker,
+                          args=(r, world, port, E, token_counts, seed, q, shm.name if shm else None, max_tokens))
               for r in range(world)]
         for p in ps:
             p.start()
@@ -218,3 +224,13 @@ def test_exchange_matches_single_process(world, E, tokens, direct):
         idx, _ = _routing(x, E, 5)
         total_valid += int((idx >= 0).sum())
     assert sum(r[3] for r in res) == total_valid
+
+
+@pytest.mark.parametrize("direct", [False, True], ids=["all_to_all_return", "direct_return"])
+def test_oversized_batch_fails_on_every_rank(direct):
+    # rank 1 holds more tokens than the backends were planned for: it must not
+    # route, and both ranks must raise together instead of one waiting in a
+    # collective for the other
+    res = _run(2, 8, [4, 9], direct=direct, max_tokens=8)
+    assert [r[1] for r in res] == ["error", "error"], res
+    assert all("max_tokens" in r[2] for r in res)

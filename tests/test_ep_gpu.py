@@ -39,6 +39,21 @@ def _poison(be):
     _lib.check(_lib.lib().qmoe_workspace_init(be.rws.data_ptr(), be.rws_bytes, None))
 
 
+def _poison_peer(be, dist):
+    """Fill this rank's IPC receive and return buffers (direct return) with the
+    same pattern, then wait for every rank: a call can only pass if its own
+    pushes and copies landed, not by reading a previous call's data."""
+    import torch
+    if getattr(be, "peer_ptrs", None) is None:
+        return
+    me, d, k = be.rank_, be.dims.d_model, be.dims.top_k
+    for ptr, n in ((be.peer_ptrs[me], be.pair_pos.numel() * d * 2), (be.peer_rows[me], be.recv_cap * d * 2),
+                   (be.peer_meta[me], be.recv_cap * k * 4)):
+        torch.as_tensor(ep._DevicePtr(ptr, n), device="cuda").fill_(0xA5)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+
 def _reference(blk, x, residual):
     """1-GPU prefill block: out and the top-k ids of every token."""
     import torch
@@ -180,23 +195,27 @@ def _nccl_worker(rank, world, port, t_local, q, direct):
         dims = synth.Dims()
         blk = synth.Block(dims, synth.Q4K_TYPES, seed=SEED)          # the same bytes on every rank
         T = t_local * world
-        x_all = synth.inputs(T, dims.d_model, seed=23, tag=5)
-        r_all = synth.inputs(T, dims.d_model, seed=24, tag=6)
-        want, want_idx = _reference(blk, x_all, r_all)
         sl = slice(rank * t_local, (rank + 1) * t_local)
-        x, res = x_all[sl].contiguous(), r_all[sl].contiguous()
         full, dc = blk.c(), dims.c()
         lb, ld = ep.local_block(full, dc, rank, world)
         be = ep.CudaBackend(full, lb, dc, ld, world, max_tokens=t_local, max_rows=t_local)
         _poison(be)
         moe = ep.ExpertParallelMoE(be, dims.num_experts, dims.top_k, dims.d_model, direct=direct)
-        got = moe.forward(x, res)
-        got = moe.forward(x, res)  # a second call reuses the return buffers
-        idx = be.topk_idx()
-        torch.cuda.synchronize()
-        ids_equal = bool(torch.equal(idx, want_idx[sl]))
-        max_err = float((got - want[sl]).abs().max())
-        q.put((rank, ids_equal, max_err, bool(torch.equal(got, want[sl]))))
+        results = []
+        # two calls with different tokens: the second reuses the exchange and
+        # return buffers, which are poisoned again before it
+        for call, (xs, rs) in enumerate(((23, 24), (31, 32))):
+            x_all = synth.inputs(T, dims.d_model, seed=xs, tag=5)
+            r_all = synth.inputs(T, dims.d_model, seed=rs, tag=6)
+            want, want_idx = _reference(blk, x_all, r_all)
+            x, res = x_all[sl].contiguous(), r_all[sl].contiguous()
+            _poison_peer(be, dist)
+            got = moe.forward(x, res)
+            idx = be.topk_idx()
+            torch.cuda.synchronize()
+            results.append((bool(torch.equal(idx, want_idx[sl])), float((got - want[sl]).abs().max()),
+                            bool(torch.equal(got, want[sl]))))
+        q.put((rank, results))
         dist.barrier()
         torch.cuda.synchronize()
         be.close()
@@ -205,13 +224,24 @@ def _nccl_worker(rank, world, port, t_local, q, direct):
         dist.destroy_process_group()
 
 
+def _worlds():
+    """2 ranks (rows pushed over peer memory when direct) and every GPU of the
+    box up to 8 (rows by NCCL all-to-all above two ranks)."""
+    try:
+        import torch
+        n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:  # noqa: BLE001
+        n = 0
+    return sorted({2, min(n, 8)}) if n >= 2 else [2]
+
+
+@pytest.mark.parametrize("world", _worlds())
 @pytest.mark.parametrize("direct", [False, True], ids=["all_to_all_return", "direct_return"])
-def test_ep_nccl(cuda, direct):
+def test_ep_nccl(cuda, direct, world):
     import torch
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 8)
-    if world < 2:
-        pytest.skip("needs at least two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -221,7 +251,8 @@ def test_ep_nccl(cuda, direct):
     for p in ps:
         p.join(300)
     assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
-    for rank, ids_equal, max_err, exact in sorted(q.get() for _ in range(world)):
-        assert ids_equal, rank
-        assert max_err <= 1e-3, (rank, max_err)
-        assert exact, (rank, max_err)
+    for rank, results in sorted(q.get() for _ in range(world)):
+        for call, (ids_equal, max_err, exact) in enumerate(results):
+            assert ids_equal, (rank, call)
+            assert max_err <= 1e-3, (rank, call, max_err)
+            assert exact, (rank, call, max_err)
