@@ -12,6 +12,8 @@
  * Reference interfaces replaced (sahan974/qwen-3.5-cuda, file:line):
  *   qmoe_type_supported   include/matmul_q4.hpp:10   matmul_type_supported
  *   qmoe_gemv             include/matmul_q4.hpp:13-21 matmul_dispatch
+ *   qmoe_gemv_exact       src/cuda/matmul_q4.cu:140-167 gemv_kernel (same
+ *                         operation order, bit-identical output)
  *   qmoe_dequant_row      include/matmul_q4.hpp:24-30 dequantize_row
  *   qmoe_router_topk      src/layer_moe.cpp:98-99     router GEMV + moe_topk
  *                         (src/cuda/moe.cu:7-57), plus the host checks of
@@ -25,6 +27,9 @@
  *                         moe_add, moe_shared_add, final copy)
  *   qmoe_block_forward    src/layer_moe.cpp:82-155   MoeLayer::forward, for
  *                         T >= 1 tokens at once
+ *   qmoe_stack_forward    src/model.cpp:193-212 layer loop (MoE halves, rmsnorm
+ *                         :208 and residual_add :211 fused), for T tokens at
+ *                         once instead of src/main.cpp:391-393's one per call
  *   qmoe_workspace_size   src/layer_moe.cpp:51-78    MoeLayer::init buffers
  */
 #ifndef QMOE_H
@@ -58,7 +63,8 @@ enum qmoe_status {
     QMOE_ERR_CUDA = 7,           /* CUDA runtime / launch error */
     QMOE_ERR_ROUTING = 10,       /* device error word: invalid or non-finite routing (layer_moe.cpp:116-118) */
     QMOE_ERR_NOT_NORMALIZED = 11,/* device error word: route weights not normalised (layer_moe.cpp:122-124) */
-    QMOE_ERR_TIMEOUT = 12        /* device error word: a bounded device-side wait gave up */
+    QMOE_ERR_TIMEOUT = 12,       /* device error word: a bounded device-side wait gave up */
+    QMOE_ERR_COMM = 13           /* collective communication (NCCL) error: include/qmoe_ep.h */
 };
 
 /* Non-owning view of one GGUF tensor on the device (reference QuantTensor,
@@ -118,8 +124,20 @@ QMOE_API const char* qmoe_status_string(int status);
  * (F32, F16, BF16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K), else 0. */
 QMOE_API int qmoe_type_supported(uint32_t ggml_type);
 
-/* y[M] = rows [element_offset/K, element_offset/K + M) of W times x[K]. */
+/* y[M] = rows [element_offset/K, element_offset/K + M) of W times x[K].
+ * Q4_K / Q5_K / Q6_K / Q8_0 rows with K = 256 * 2^j <= 4096 (and x 16-byte
+ * aligned) stream through shared memory with bulk copies and are decoded a
+ * 64-element unit at a time against 24-bit fixed-point planes of x: F32-level
+ * accuracy (~2^-22 relative), but not the reference's summation order.  Other
+ * types and shapes take the qmoe_gemv_exact path. */
 QMOE_API int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, int K,
+              uint64_t element_offset, qmoe_stream_t stream);
+
+/* The same product in the reference GEMV's exact F32 operation order
+ * (src/cuda/matmul_q4.cu:140-167: per-thread FMA chains over k = t + 256 i,
+ * then the warp and block shuffle trees), one warp per row: bit-identical to
+ * the reference kernel's output. */
+QMOE_API int qmoe_gemv_exact(const qmoe_tensor* w, const float* x, float* y, int M, int K,
               uint64_t element_offset, qmoe_stream_t stream);
 
 /* out[cols] = elements [row*cols, row*cols + cols) of W, dequantised to F32. */
@@ -291,6 +309,21 @@ QMOE_API int qmoe_block_forward(const qmoe_block* blk, const qmoe_dims* dims, co
 QMOE_API int qmoe_block_forward_prenorm(const qmoe_block* blk, const qmoe_dims* dims, const float* resid,
                                         const float* norm_weight, float eps, float* out, int T,
                                         void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
+
+/* The MoE halves of n_layers decoder layers for a batch of T tokens, in
+ * layer order (the multi-token form of the layer loop of src/model.cpp:193-212,
+ * which the reference runs one token at a time from src/main.cpp:391-393):
+ * for l = 0..n_layers-1:  resid <- resid + MoE_l(rmsnorm(resid) * norm_weights[l])
+ * (qmoe_block_forward_prenorm per layer; T > 8 takes the tensor-core path).
+ * `blocks` and `norm_weights` are host arrays of n_layers entries (device
+ * pointers inside); resid [T][d] is updated in place; tmp is device scratch of
+ * the same size; one workspace serves every layer (stream-ordered).  The token
+ * mixing that model.cpp runs between the MoE halves is the caller's: call this
+ * once per layer (n_layers = 1) with the mixer between, or for a run of
+ * consecutive MoE halves. */
+QMOE_API int qmoe_stack_forward(const qmoe_block* blocks, const float* const* norm_weights, int n_layers,
+                                const qmoe_dims* dims, float eps, float* resid, float* tmp, int T,
+                                void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 
 /* Waits for `stream`, reads the device error word of `workspace` into
  * err[0..1] (flags, first failing token) and clears it.  Returns the status

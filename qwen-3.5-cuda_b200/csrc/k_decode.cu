@@ -31,11 +31,18 @@ namespace qmoe {
 
 constexpr unsigned FULL = 0xffffffffu;
 
-// Phase timestamp (one thread per CTA) when a trace buffer is registered.
+// Phase timestamp (one thread per CTA) when a trace buffer is registered:
+// %globaltimer ns, or with QMOE_TRACE_CLOCK the SM's cycle counter (exact
+// durations inside one CTA; not comparable across SMs).
+#ifdef QMOE_TRACE_CLOCK
+#define QMOE_TRACE_NOW() static_cast<uint64_t>(clock64())
+#else
+#define QMOE_TRACE_NOW() gtimer()
+#endif
 #define QMOE_TRACE(P, kind, ev)                                                                          \
     do {                                                                                                 \
         if ((P).trace && blockIdx.x < kTraceCtas)                                                        \
-            (P).trace[((kind) * kTraceCtas + blockIdx.x) * kTraceEvents + (ev)] = gtimer();             \
+            (P).trace[((kind) * kTraceCtas + blockIdx.x) * kTraceEvents + (ev)] = QMOE_TRACE_NOW();     \
     } while (0)
 
 // ---------------------------------------------------------------------------
@@ -136,38 +143,6 @@ __device__ __forceinline__ void load_input(float4 (&xr)[CH][2], const DecodePara
 }
 
 __device__ __forceinline__ int router_esize(int type) { return type == T_F32 ? 4 : 2; }
-
-// 24-bit planes (qmoe_dev.cuh) of four consecutive elements e0..e0+3 per lane,
-// where the 8 lanes 8m..8m+7 of a warp hold one 32-block: block maximum over
-// the 8 lanes, 16-run sums over 4 lanes, one 32-bit store per plane.
-__device__ __forceinline__ void write_planes4(float4 v, uint8_t* base, int K, int e0, int lane) {
-    uint32_t ab = max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
-                      max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu));
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) ab = max(ab, __shfl_xor_sync(FULL, ab, o));
-    float s16 = (v.x + v.y) + (v.z + v.w);
-    s16 += __shfl_xor_sync(FULL, s16, 1);
-    s16 += __shfl_xor_sync(FULL, s16, 2);
-    const bool bad = ab >= 0x7F800000u;
-    const uint32_t eb = ab >> 23;
-    int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
-    sh = sh > 126 ? 126 : sh;
-    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
-    float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-    if (bad) scale = __uint_as_float(0x7FC00000u);
-    const uint32_t X0 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.x * mul));
-    const uint32_t X1 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.y * mul));
-    const uint32_t X2 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.z * mul));
-    const uint32_t X3 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.w * mul));
-    const uint32_t w0 = (X0 & 255u) | ((X1 & 255u) << 8) | ((X2 & 255u) << 16) | ((X3 & 255u) << 24);
-    const uint32_t w1 = ((X0 >> 8) & 255u) | (((X1 >> 8) & 255u) << 8) | (((X2 >> 8) & 255u) << 16) | (((X3 >> 8) & 255u) << 24);
-    const uint32_t w2 = ((X0 >> 16) & 255u) | (((X1 >> 16) & 255u) << 8) | (((X2 >> 16) & 255u) << 16) | (((X3 >> 16) & 255u) << 24);
-    const uint32_t o = pswz(static_cast<uint32_t>(e0));
-    *reinterpret_cast<uint32_t*>(base + o) = w0;
-    *reinterpret_cast<uint32_t*>(base + K + o) = w1;
-    *reinterpret_cast<uint32_t*>(base + 2 * K + o) = w2;
-    if ((lane & 3) == 0) reinterpret_cast<float2*>(base + 3 * K)[e0 >> 4] = make_float2(scale, s16);
-}
 
 // Top-k + softmax + validation for every token (select_token, one warp per
 // token), then the permutation and the packed schedule.  Runs in the router's
@@ -372,14 +347,6 @@ __global__ void __launch_bounds__(RT_WARPS * 32) k_router(DecodeParams P) {
 constexpr int NCW = 8;                      // consumer warps
 constexpr int XK_THREADS = (NCW + 1) * 32;  // + one producer warp
 constexpr int SCHED_SMEM_WORDS = SCHED_HDR + 3 * kDecodeMaxT * kMaxTopK + 2 * kDecodeMaxT * kMaxTopK;
-
-template <int TYPE>
-__device__ __forceinline__ float unit_dot_t(uint32_t row, int u, const XU& x) {
-    if (TYPE == T_Q4_K) return dot_qk45<false>(row, u, x);
-    if (TYPE == T_Q5_K) return dot_qk45<true>(row, u, x);
-    if (TYPE == T_Q6_K) return dot_q6_k(row, u, x);
-    return dot_q8_0(row, u, x);
-}
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
     const float s = g / (1.0f + expf(-g));  // moe.cu:64
@@ -989,6 +956,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
         // also publishes the routing to the workspace): no cross-CTA step
         // between the router's logits and this CTA's weight loads
         topk_and_schedule(P, s_sched, s_w, c == 0, 3);
+        if (tid == 0) QMOE_TRACE(P, 1, 6);
     } else {
         // the other warps: input planes, shared-expert gate, residual rows
         constexpr int NTH = FX_THREADS - RT_WARPS * 32;
@@ -1012,6 +980,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
         x_planes_smem<NTH>(xs, P, t2);  // its loads go out before the store below
         if (t2 < n32) store32(t2, v0);
         for (int q = t2 + NTH; q < n32; q += NTH) store32(q, load32(q));
+        if (t2 == 0) QMOE_TRACE(P, 1, 7);
     }
     __syncthreads();
     if (tid == 0) QMOE_TRACE(P, 1, 2);
@@ -1239,6 +1208,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
         }
         if (rend < nsrc) asm volatile("bar.sync 2, %0;" ::"r"((FX_NCW + 1) * 32) : "memory");  // slots may be refilled
     }
+    if (tid == 0) QMOE_TRACE(P, 2, 4);
     asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
     if (tid == 0) QMOE_TRACE(P, 2, 5);
 

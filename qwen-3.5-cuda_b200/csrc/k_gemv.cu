@@ -13,6 +13,8 @@
 #include "qmoe_internal.h"
 #include "qmoe_dq1.cuh"
 
+#include <algorithm>
+
 namespace qmoe {
 
 constexpr unsigned GFULL = 0xffffffffu;
@@ -64,6 +66,132 @@ __global__ void __launch_bounds__(GV_WARPS * 32)
     if (lane == 0) y[row] = r;
 }
 
+// ---------------------------------------------------------------------------
+// Streaming GEMV for the block-quantised types Q4_K / Q5_K / Q6_K / Q8_0
+// (K a multiple of 256, at most 4096): the matmul_dispatch path for large
+// matrices (LM head, attention and GDN projections).
+//
+// One CTA per SM, persistent: a producer lane streams chunks of RS
+// consecutive weight rows into a shared-memory ring with 1-D bulk copies
+// (TMA, cp.async.bulk + mbarrier transaction counts), straight from the GGUF
+// payload; 8 consumer warps dot them against the 24-bit planes of x
+// (qmoe_dev.cuh), built once per CTA.  A lane decodes whole 64-element units
+// (qmoe_units.cuh: scales once per unit, dp4a over the nibble/byte words) and
+// keeps its unit's activation planes in registers for the whole launch, so
+// neither x nor the per-element type switch is re-read per row.  Results
+// match an F32 dot product to ~2^-22 relative; the reduction order differs
+// from the reference's, so outputs are not bit-identical (k_gemv is).
+// ---------------------------------------------------------------------------
+constexpr int GS_NCW = 8;                      // consumer warps
+constexpr int GS_THREADS = (GS_NCW + 1) * 32;  // + one producer warp
+constexpr int GS_MAX_STAGES = 12;
+
+struct GemvStream {
+    const uint8_t* w;     // first byte of row 0
+    const uint8_t* wend;  // one past the tensor's last payload byte
+    const float* x;
+    float* y;
+    int M, K;
+    uint32_t rb;     // bytes per row
+    int rs;          // rows per ring stage
+    int nst;         // ring stages
+    uint32_t stage;  // bytes per stage (16-byte multiple)
+    uint32_t off_x, off_ring;
+};
+
+template <int TYPE, int UPL>  // UPL: units per lane (K/64 = 32 * UPL when UPL > 0; UPL == 0: K < 2048)
+__global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_stream(GemvStream p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + GS_MAX_STAGES;
+    uint8_t* xs = smem + p.off_x;
+    uint8_t* ring = smem + p.off_ring;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int nchunk = (p.M + p.rs - 1) / p.rs;
+    const int nmine = c < nchunk ? (nchunk - 1 - c) / G + 1 : 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < p.nst; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, GS_NCW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == GS_NCW) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            for (int kk = 0, ch = c, slot = 0, round = 0; kk < nmine; ++kk, ch += G) {
+                if (kk >= p.nst) mbar_wait(empty + slot, (round - 1) & 1, nullptr);
+                const int r0 = ch * p.rs, nr = min(p.rs, p.M - r0);
+                const uint8_t* src = p.w + static_cast<uint64_t>(r0) * p.rb;
+                uint8_t* dst = ring + static_cast<size_t>(slot) * p.stage;
+                const uint64_t bytes = static_cast<uint64_t>(nr) * p.rb;
+                // the 16-byte aligned superset of the rows (plain loads for a ragged tail)
+                const uintptr_t s = reinterpret_cast<uintptr_t>(src), lo = s & ~uintptr_t(15);
+                const uintptr_t hi = (s + bytes + 15) & ~uintptr_t(15), lim = reinterpret_cast<uintptr_t>(p.wend);
+                const uintptr_t hf = hi <= lim ? hi : (lim & ~uintptr_t(15));
+                const uint32_t tx = hf > lo ? static_cast<uint32_t>(hf - lo) : 0u;
+                for (uintptr_t a = (hf > lo ? hf : lo); a < s + bytes; ++a)
+                    dst[a - lo] = *reinterpret_cast<const uint8_t*>(a);
+                mbar_arrive_expect_tx(full + slot, tx);
+                if (tx) bulk_g2s(dst, reinterpret_cast<const void*>(lo), tx, full + slot, nullptr);
+                if (++slot == p.nst) { slot = 0; ++round; }
+            }
+        }
+        return;
+    }
+    // ---------------- consumers ----------------
+    // x -> 24-bit planes (each warp quantises 128-element chunks)
+    for (int g = tid; g < p.K / 4; g += GS_NCW * 32)
+        write_planes4(__ldg(reinterpret_cast<const float4*>(p.x) + g), xs, p.K, 4 * g, lane);
+    asm volatile("bar.sync 1, %0;" ::"r"(GS_NCW * 32) : "memory");
+    const XPlanesView xv{smem_u32(xs), smem_u32(xs) + static_cast<uint32_t>(p.K),
+                         smem_u32(xs) + 2u * static_cast<uint32_t>(p.K), smem_u32(xs) + 3u * static_cast<uint32_t>(p.K)};
+    constexpr int NU = UPL > 0 ? UPL : 1;
+    const int U = p.K >> 6;
+    const int lgU = 31 - __clz(U);
+    const int lgG = UPL > 0 ? 5 : lgU;         // lanes per row: 32, or U when U < 32
+    const int rpw = UPL > 0 ? 1 : 32 >> lgU;   // rows per warp step
+    const int ul = lane & ((1 << lgG) - 1), rsub = lane >> lgG;
+    int unit[NU];
+    XU xr[NU];
+#pragma unroll
+    for (int m = 0; m < NU; ++m) {
+        unit[m] = UPL > 0 ? 32 * m + unit_of_lane<TYPE>(lane, 5) : unit_of_lane<TYPE>(ul, lgU);
+        load_xu<TYPE>(xr[m], xv, unit[m]);
+    }
+    for (int kk = 0, ch = c, slot = 0, round = 0; kk < nmine; ++kk, ch += G) {
+        const int r0 = ch * p.rs, nr = min(p.rs, p.M - r0);
+        mbar_wait(full + slot, round & 1, nullptr);
+        const uint32_t base = smem_u32(ring) + static_cast<uint32_t>(slot) * p.stage +
+                              static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.w + static_cast<uint64_t>(r0) * p.rb) & 15u);
+        // two rows per warp step, as independent dependency chains (a row
+        // past the chunk's end is computed on the last row and dropped)
+        for (int rr = warp * rpw; rr < nr; rr += 2 * GS_NCW * rpw) {
+            const int ra = rr + rsub, rb = rr + GS_NCW * rpw + rsub;
+            const uint32_t pa = base + static_cast<uint32_t>(min(ra, nr - 1)) * p.rb;
+            const uint32_t pb = base + static_cast<uint32_t>(min(rb, nr - 1)) * p.rb;
+            float va = 0.0f, vb = 0.0f;
+#pragma unroll
+            for (int m = 0; m < NU; ++m) {
+                va += unit_dot_t<TYPE>(pa, unit[m], xr[m]);
+                vb += unit_dot_t<TYPE>(pb, unit[m], xr[m]);
+            }
+            for (int o = (1 << lgG) >> 1; o; o >>= 1) {
+                va += __shfl_xor_sync(GFULL, va, o);
+                vb += __shfl_xor_sync(GFULL, vb, o);
+            }
+            if (ul == 0 && ra < nr) p.y[r0 + ra] = va;
+            if (ul == 0 && rb < nr) p.y[r0 + rb] = vb;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        if (++slot == p.nst) { slot = 0; ++round; }
+    }
+}
+
 __global__ void k_dequant_row(const uint8_t* __restrict__ w, int type, float* __restrict__ out, uint64_t start, int cols) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += blockDim.x * gridDim.x)
         out[i] = dq1(w, type, start + i);
@@ -73,6 +201,85 @@ cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, in
                         cudaStream_t s) {
     const int grid = (M + GV_WARPS - 1) / GV_WARPS;
     k_gemv<<<grid, GV_WARPS * 32, 0, s>>>(w, type, x, y, M, K, off);
+    return cudaGetLastError();
+}
+
+namespace {
+typedef void (*GsKern)(GemvStream);
+template <int TYPE>
+GsKern pick_stream(int upl) {
+    switch (upl) {
+        case 0: return k_gemv_stream<TYPE, 0>;
+        case 1: return k_gemv_stream<TYPE, 1>;
+        case 2: return k_gemv_stream<TYPE, 2>;
+        default: return nullptr;
+    }
+}
+int g_sms[64], g_optin[64];
+}  // namespace
+
+// The streaming kernel applies to Q4_K / Q5_K / Q6_K / Q8_0 rows of K = 256 *
+// 2^j elements (K <= 4096) whose first row starts on a boundary the unit
+// decoders can read (16 bytes for the K-quants with 16-byte blocks, 4 for
+// Q8_0, 2 for Q6_K).
+bool gemv_stream_supported(const uint8_t* w, int type, int K, uint64_t off) {
+    if (type != T_Q4_K && type != T_Q5_K && type != T_Q6_K && type != T_Q8_0) return false;
+    if (K < 256 || K > 4096 || (K & (K - 1))) return false;
+    const int be = type == T_Q8_0 ? 32 : 256, bb = type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : 34;
+    if (off % be) return false;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(w) + off / be * bb;
+    const uintptr_t need = (type == T_Q4_K || type == T_Q5_K) ? 16 : type == T_Q8_0 ? 4 : 2;
+    return a % need == 0;
+}
+
+cudaError_t launch_gemv_stream(const uint8_t* w, int type, uint64_t w_bytes, const float* x, float* y, int M, int K,
+                               uint64_t off, cudaStream_t s) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int& sms = g_sms[dev & 63];
+    int& optin = g_optin[dev & 63];
+    if (!sms) {
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
+    }
+    const int be = type == T_Q8_0 ? 32 : 256, bb = type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : 34;
+    GemvStream p;
+    p.w = w + off / be * bb;
+    p.wend = w + w_bytes;
+    p.x = x;
+    p.y = y;
+    p.M = M;
+    p.K = K;
+    p.rb = static_cast<uint32_t>(K / be * bb);
+    const int U = K / 64;
+    const int upl = U >= 32 ? U / 32 : 0;
+    const int rpw = U >= 32 ? 1 : 32 / U;
+    // stages of up to ~32 KB (whole double warp steps), as many as fit beside the planes
+    int steps = 2;
+    while (2 * steps * GS_NCW * rpw * p.rb <= 32768u && steps < 8) steps *= 2;
+    p.rs = steps * GS_NCW * rpw;
+    p.stage = (static_cast<uint32_t>(p.rs) * p.rb + 32u + 127u) & ~127u;
+    p.off_x = 256;
+    p.off_ring = (p.off_x + static_cast<uint32_t>(K) * 4u + 127u) & ~127u;  // planes: 3K bytes + K/2 meta
+    const size_t budget = static_cast<size_t>(optin) - 1024;
+    if (p.off_ring + p.stage > budget) return cudaErrorInvalidValue;
+    p.nst = static_cast<int>(std::min<size_t>(GS_MAX_STAGES, (budget - p.off_ring) / p.stage));
+    const size_t smem = p.off_ring + static_cast<size_t>(p.nst) * p.stage;
+    GsKern kern = nullptr;
+    switch (type) {
+        case T_Q4_K: kern = pick_stream<T_Q4_K>(upl); break;
+        case T_Q5_K: kern = pick_stream<T_Q5_K>(upl); break;
+        case T_Q6_K: kern = pick_stream<T_Q6_K>(upl); break;
+        case T_Q8_0: kern = pick_stream<T_Q8_0>(upl); break;
+        default: break;
+    }
+    if (!kern) return cudaErrorInvalidValue;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) !=
+        cudaSuccess)
+        return e;
+    const int nchunk = (M + p.rs - 1) / p.rs;
+    kern<<<std::min(nchunk, sms), GS_THREADS, smem, s>>>(p);
     return cudaGetLastError();
 }
 

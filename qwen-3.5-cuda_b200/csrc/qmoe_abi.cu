@@ -35,6 +35,9 @@ int decode_num_sms();
 cudaError_t launch_gemv(const uint8_t* w, int type, const float* x, float* y, int M, int K, uint64_t off,
                         cudaStream_t s);
 cudaError_t launch_dequant_row(const uint8_t* w, int type, float* out, uint64_t start, int cols, cudaStream_t s);
+bool gemv_stream_supported(const uint8_t* w, int type, int K, uint64_t off);
+cudaError_t launch_gemv_stream(const uint8_t* w, int type, uint64_t w_bytes, const float* x, float* y, int M, int K,
+                               uint64_t off, cudaStream_t s);
 cudaError_t launch_synth(void* dst, int type, uint64_t nblocks, uint64_t seed, uint64_t stream_id, float sigma,
                          cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
@@ -208,6 +211,7 @@ const char* qmoe_status_string(int s) {
         case QMOE_ERR_ROUTING: return "invalid/non-finite MoE routing result";
         case QMOE_ERR_NOT_NORMALIZED: return "MoE routing weights are not normalized";
         case QMOE_ERR_TIMEOUT: return "device-side wait timed out";
+        case QMOE_ERR_COMM: return "collective communication error";
         default: return "unknown status";
     }
 }
@@ -221,6 +225,19 @@ uint64_t qmoe_tensor_bytes(uint32_t t, uint64_t n) {
 }
 
 int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, int K, uint64_t off, qmoe_stream_t stream) {
+    if (!w || !w->data || !x || !y) return QMOE_ERR_ARG;
+    if (!gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
+    if (M <= 0 || K <= 0 || off + static_cast<uint64_t>(M) * K > w->num_elements) return QMOE_ERR_SHAPE;
+    const uint8_t* wp = static_cast<const uint8_t*>(w->data);
+    const int type = static_cast<int>(w->ggml_type);
+    if (gemv_stream_supported(wp, type, K, off) && reinterpret_cast<uintptr_t>(x) % 16 == 0)
+        return cuda_status(launch_gemv_stream(wp, type, qmoe_tensor_bytes(w->ggml_type, w->num_elements), x, y, M, K,
+                                              off, reinterpret_cast<cudaStream_t>(stream)));
+    return cuda_status(launch_gemv(wp, type, x, y, M, K, off, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int qmoe_gemv_exact(const qmoe_tensor* w, const float* x, float* y, int M, int K, uint64_t off,
+                    qmoe_stream_t stream) {
     if (!w || !w->data || !x || !y) return QMOE_ERR_ARG;
     if (!gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
     if (M <= 0 || K <= 0 || off + static_cast<uint64_t>(M) * K > w->num_elements) return QMOE_ERR_SHAPE;
@@ -603,6 +620,23 @@ int qmoe_block_forward_prenorm(const qmoe_block* B, const qmoe_dims* D, const fl
     if (!norm_weight) return QMOE_ERR_ARG;
     if (!(eps > 0.0f)) return QMOE_ERR_ARG;
     return block_forward_impl(B, D, resid, out, resid, norm_weight, eps, T, ws, ws_bytes, stream);
+}
+
+int qmoe_stack_forward(const qmoe_block* blocks, const float* const* norm_weights, int n_layers, const qmoe_dims* D,
+                       float eps, float* resid, float* tmp, int T, void* ws, size_t ws_bytes, qmoe_stream_t stream) {
+    if (!blocks || !norm_weights || n_layers <= 0 || !resid || !tmp || resid == tmp) return QMOE_ERR_ARG;
+    // layers alternate between the two buffers; an odd count ends in tmp and is copied back
+    const float* x = resid;
+    for (int l = 0; l < n_layers; ++l) {
+        float* out = (l & 1) ? resid : tmp;
+        const int st = qmoe_block_forward_prenorm(blocks + l, D, x, norm_weights[l], eps, out, T, ws, ws_bytes, stream);
+        if (st != QMOE_OK) return st;
+        x = out;
+    }
+    if (n_layers & 1)
+        return cuda_status(cudaMemcpyAsync(resid, tmp, sizeof(float) * static_cast<size_t>(T) * D->d_model,
+                                           cudaMemcpyDeviceToDevice, reinterpret_cast<cudaStream_t>(stream)));
+    return QMOE_OK;
 }
 
 int qmoe_trace_enable(uint64_t* buf, size_t bytes) {

@@ -256,4 +256,36 @@ __device__ __forceinline__ float planes_combine(int P0, int P1, int P2) {
     return fmaf(256.0f, static_cast<float>(p12), static_cast<float>(P0));
 }
 
+// 24-bit planes of four consecutive elements e0..e0+3 per lane,
+// where the 8 lanes 8m..8m+7 of a warp hold one 32-block: block maximum over
+// the 8 lanes, 16-run sums over 4 lanes, one 32-bit store per plane.
+__device__ __forceinline__ void write_planes4(float4 v, uint8_t* base, int K, int e0, int lane) {
+    uint32_t ab = max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                      max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
+    float s16 = (v.x + v.y) + (v.z + v.w);
+    s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
+    s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
+    const bool bad = ab >= 0x7F800000u;
+    const uint32_t eb = ab >> 23;
+    int sh = eb == 0 ? 126 : 21 - (static_cast<int>(eb) - 127);
+    sh = sh > 126 ? 126 : sh;
+    const float mul = __uint_as_float(static_cast<uint32_t>(sh + 127) << 23);
+    float scale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+    if (bad) scale = __uint_as_float(0x7FC00000u);
+    const uint32_t X0 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.x * mul));
+    const uint32_t X1 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.y * mul));
+    const uint32_t X2 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.z * mul));
+    const uint32_t X3 = bad ? 0u : static_cast<uint32_t>(__float2int_rn(v.w * mul));
+    const uint32_t w0 = (X0 & 255u) | ((X1 & 255u) << 8) | ((X2 & 255u) << 16) | ((X3 & 255u) << 24);
+    const uint32_t w1 = ((X0 >> 8) & 255u) | (((X1 >> 8) & 255u) << 8) | (((X2 >> 8) & 255u) << 16) | (((X3 >> 8) & 255u) << 24);
+    const uint32_t w2 = ((X0 >> 16) & 255u) | (((X1 >> 16) & 255u) << 8) | (((X2 >> 16) & 255u) << 16) | (((X3 >> 16) & 255u) << 24);
+    const uint32_t o = pswz(static_cast<uint32_t>(e0));
+    *reinterpret_cast<uint32_t*>(base + o) = w0;
+    *reinterpret_cast<uint32_t*>(base + K + o) = w1;
+    *reinterpret_cast<uint32_t*>(base + 2 * K + o) = w2;
+    if ((lane & 3) == 0) reinterpret_cast<float2*>(base + 3 * K)[e0 >> 4] = make_float2(scale, s16);
+}
+
 }  // namespace qmoe

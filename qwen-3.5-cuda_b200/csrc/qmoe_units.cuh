@@ -211,6 +211,15 @@ __device__ __forceinline__ float unit_dot(int type, uint32_t row, int u, const X
     }
 }
 
+// The unit dot of a weight type known at compile time.
+template <int TYPE>
+__device__ __forceinline__ float unit_dot_t(uint32_t row, int u, const XU& x) {
+    if (TYPE == T_Q4_K) return dot_qk45<false>(row, u, x);
+    if (TYPE == T_Q5_K) return dot_qk45<true>(row, u, x);
+    if (TYPE == T_Q6_K) return dot_q6_k(row, u, x);
+    return dot_q8_0(row, u, x);
+}
+
 // Sum over the U lanes (aligned group) that share one row.
 template <int U>
 __device__ __forceinline__ float group_sum(float v) {

@@ -23,6 +23,7 @@ QMOE_ERR_CUDA = 7
 QMOE_ERR_ROUTING = 10
 QMOE_ERR_NOT_NORMALIZED = 11
 QMOE_ERR_TIMEOUT = 12
+QMOE_ERR_COMM = 13
 
 WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR, WS_INPUT, WS_INPUT16 = range(10)
 
@@ -53,6 +54,7 @@ SIGNATURES = [
     ("qmoe_status_string", ctypes.c_char_p, [c_int]),
     ("qmoe_type_supported", c_int, [c_uint32]),
     ("qmoe_gemv", c_int, [POINTER(QmoeTensor), c_void_p, c_void_p, c_int, c_int, c_uint64, c_void_p]),
+    ("qmoe_gemv_exact", c_int, [POINTER(QmoeTensor), c_void_p, c_void_p, c_int, c_int, c_uint64, c_void_p]),
     ("qmoe_dequant_row", c_int, [POINTER(QmoeTensor), c_void_p, c_int, c_int, c_void_p]),
     ("qmoe_workspace_size", c_size_t, [POINTER(QmoeDims), c_int]),
     ("qmoe_ws_view", c_void_p, [c_void_p, POINTER(QmoeDims), c_int, c_int]),
@@ -92,6 +94,8 @@ SIGNATURES = [
                                    c_void_p, c_size_t, c_void_p]),
     ("qmoe_block_forward_prenorm", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_void_p, c_float,
                                            c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    ("qmoe_stack_forward", c_int, [POINTER(QmoeBlock), POINTER(c_void_p), c_int, POINTER(QmoeDims), c_float,
+                                   c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     ("qmoe_check_errors", c_int, [c_void_p, POINTER(QmoeDims), POINTER(c_uint32), c_void_p]),
     ("qmoe_trace_enable", c_int, [c_void_p, c_size_t]),
     ("qmoe_trace_bytes", c_size_t, []),

@@ -71,10 +71,16 @@ def test_gemv_vs_oracle(ty, K):
     x = torch.from_numpy(xh).cuda()
     y = torch.empty(M, dtype=torch.float32, device="cuda")
     t = _tensor(w, ty, n)
-    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, row0 * K, None))
+    # the reference-order kernel (bit-level checks below) ...
+    _lib.check(_lib.lib().qmoe_gemv_exact(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, row0 * K, None))
     torch.cuda.synchronize()
     want = orc.gemv(h, int(ty), n, xh, M, K, row0 * K)
     got = y.cpu().numpy()
+    # ... and the default path (the streaming unit decoder where it applies)
+    yd = torch.empty(M, dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(t), x.data_ptr(), yd.data_ptr(), M, K, row0 * K, None))
+    torch.cuda.synchronize()
+    assert np.allclose(yd.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
     if ty == GgmlType.F32:
         assert np.array_equal(got, want)  # same reduction order, bit for bit
     else:
@@ -90,6 +96,30 @@ def test_gemv_vs_oracle(ty, K):
             assert np.array_equal(want, ref)
         else:
             assert np.allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("ty", [GgmlType.Q4_K, GgmlType.Q5_K, GgmlType.Q6_K, GgmlType.Q8_0])
+@pytest.mark.parametrize("K,M,row0", [(256, 1000, 3), (1024, 777, 0), (2048, 1203, 5), (4096, 301, 2)])
+def test_gemv_stream_vs_oracle(ty, K, M, row0):
+    """The streaming GEMV (bulk-copied row chunks, unit decoders against the
+    24-bit planes of x) over many chunks and CTAs, a ragged last chunk and a
+    row offset: within 1e-5 of the oracle's F32 products."""
+    import torch
+    rows = M + row0 + 1
+    n = rows * K
+    h = np.empty(calculate_tensor_bytes(ty, n), dtype=np.uint8)
+    synth.fill(h, ty, n, 7, 19, 0.02)
+    xh = np.random.default_rng(K + M).standard_normal(K).astype(np.float32)
+    w = torch.from_numpy(h).cuda()
+    x = torch.from_numpy(xh).cuda()
+    y = torch.full((M + 1,), float("nan"), dtype=torch.float32, device="cuda")
+    t = _tensor(w, ty, n)
+    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, row0 * K, None))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    want = orc.gemv(h, int(ty), n, xh, M, K, row0 * K)
+    assert np.isnan(got[M])  # nothing written past row M-1
+    assert np.allclose(got[:M], want, rtol=1e-5, atol=1e-5), np.max(np.abs(got[:M] - want))
 
 
 def _router_block(dims, bias, seed):
