@@ -12,7 +12,7 @@ cuda="${CUDA_HOME:-/usr/local/cuda}"
 g++ -std=c++17 -O2 -Wall -Wextra -Werror \
     -I "$root/include" -I "$here/compat" -I "$cuda/include" \
     "$here/shim_test.cpp" "$root/qwen-3.5-cuda_b200/cpp/matmul_q4_shim.cpp" \
-    "$root/qwen-3.5-cuda_b200/cpp/layer_moe_shim.cpp" \
+    "$root/qwen-3.5-cuda_b200/cpp/layer_moe_shim.cpp" "$root/qwen-3.5-cuda_b200/cpp/moe_prefill_shim.cpp" \
     -L "$root/qwen-3.5-cuda_b200/qmoe" -lqmoe -L "$root/oracle" -loracle -L "$cuda/lib64" -lcudart \
     -Wl,-rpath,"$root/qwen-3.5-cuda_b200/qmoe" -Wl,-rpath,"$root/oracle" -Wl,-rpath,"$cuda/lib64" \
     -o "$out/shim_test"

@@ -13,6 +13,7 @@
 
 #include "layer_moe.hpp"
 #include "matmul_q4.hpp"
+#include "moe_prefill.hpp"
 #include "qmoe.h"
 #include "quantized.hpp"
 
@@ -214,6 +215,83 @@ int main() {
     bad = 0;
     for (int i = 0; i < d; ++i) bad += close(y[i], want[i]) ? 0 : 1;
     CHECK(bad == 0, "after a barrier timeout: %d of %d MoE outputs outside tolerance", bad, d);
+
+    // MoePrefill: the MoE halves of two layers for a batch of T = 20 tokens
+    // (tensor-core path) with a token mixer between them, against the same
+    // layer loop written out with the C-ABI (bit-identical: same kernels)
+    {
+        const int T = 20, L = 2;
+        const float eps = 1e-6f;
+        Tensor xs = make("xs", GgmlType::F32, {d, T}, seed, 20, 1.0f);
+        Tensor nw0 = make("post_norm0", GgmlType::F32, {d}, seed, 21, 0.1f);
+        Tensor nw1 = make("post_norm1", GgmlType::F32, {d}, seed, 22, 0.1f);
+        std::vector<MoeLayerTensors> layers(L);
+        for (int l = 0; l < L; ++l)
+            layers[l] = MoeLayerTensors{&router.q, &eg.q, &eu.q, &ed.q, &sgate.q, &sg.q, &su.q, &sd.q,
+                                        static_cast<const float*>((l ? nw1 : nw0).q.device_ptr)};
+        float *stream_buf = nullptr, *a = nullptr, *b = nullptr;
+        const size_t nb = sizeof(float) * static_cast<size_t>(T) * d;
+        CUDA_CHECK(cudaMalloc(&stream_buf, nb));
+        CUDA_CHECK(cudaMalloc(&a, nb));
+        CUDA_CHECK(cudaMalloc(&b, nb));
+        CUDA_CHECK(cudaMemcpy(stream_buf, xs.q.device_ptr, nb, cudaMemcpyDeviceToDevice));
+        CUDA_CHECK(cudaMemcpy(a, xs.q.device_ptr, nb, cudaMemcpyDeviceToDevice));
+        std::vector<int> mixed;
+        // the mixer stands in for attention/GDN + residual add: here it halves the stream
+        auto mix = [&](int l, float* buf, int n) {
+            mixed.push_back(l);
+            CHECK(n == T, "mixer got %d tokens", n);
+            std::vector<float> h(static_cast<size_t>(n) * d);
+            CUDA_CHECK(cudaMemcpyAsync(h.data(), buf, sizeof(float) * h.size(), cudaMemcpyDeviceToHost, ctx.stream()));
+            CUDA_CHECK(cudaStreamSynchronize(ctx.stream()));
+            for (float& v : h) v *= 0.5f;
+            CUDA_CHECK(cudaMemcpyAsync(buf, h.data(), sizeof(float) * h.size(), cudaMemcpyHostToDevice, ctx.stream()));
+        };
+        MoePrefill pre;
+        pre.init(cfg, 64);
+        pre.forward(stream_buf, T, layers, eps, ctx, mix);
+        pre.check_routing(ctx);
+        CHECK(mixed.size() == 2 && mixed[0] == 0 && mixed[1] == 1, "mixer calls");
+        // the same loop by hand
+        qmoe_dims dm{d, E, k, F, Fs};
+        const size_t wsb = qmoe_workspace_size(&dm, T);
+        void* ws2 = nullptr;
+        CUDA_CHECK(cudaMalloc(&ws2, wsb));
+        CHECK(qmoe_workspace_init(ws2, wsb, nullptr) == QMOE_OK, "ws init");
+        auto qt = [](const Tensor& t) {
+            qmoe_tensor v{};
+            v.data = t.q.device_ptr;
+            v.ggml_type = static_cast<uint32_t>(t.q.type);
+            v.num_elements = t.q.num_elements;
+            return v;
+        };
+        qmoe_block blk{qt(router), qt(eg), qt(eu), qt(ed), qt(sgate), qt(sg), qt(su), qt(sd), nullptr};
+        float* cur = a;
+        for (int l = 0; l < L; ++l) {
+            mix(l, cur, T);
+            float* nxt = cur == a ? b : a;
+            CHECK(qmoe_block_forward_prenorm(&blk, &dm, cur, layers[l].post_norm, eps, nxt, T, ws2, wsb, ctx.stream()) ==
+                      QMOE_OK,
+                  "block_forward_prenorm");
+            cur = nxt;
+        }
+        ctx.synchronize();
+        std::vector<float> got(static_cast<size_t>(T) * d), ref(static_cast<size_t>(T) * d);
+        CUDA_CHECK(cudaMemcpy(got.data(), stream_buf, nb, cudaMemcpyDeviceToHost));
+        CUDA_CHECK(cudaMemcpy(ref.data(), cur, nb, cudaMemcpyDeviceToHost));
+        CHECK(std::memcmp(got.data(), ref.data(), nb) == 0, "MoePrefill differs from the layer loop over the C-ABI");
+        bool finite = true;
+        for (float v : got) finite = finite && std::isfinite(v);
+        CHECK(finite, "MoePrefill output not finite");
+        expect_throw([&] { pre.forward(stream_buf, 65, layers, eps, ctx); },
+                     "MoePrefill: batch of 65 tokens exceeds max_tokens 64");
+        pre.free_buffers();
+        pre.free_buffers();
+        cudaFree(ws2);
+        cudaFree(stream_buf);
+        cudaFree(a);
+        cudaFree(b);
+    }
 
     std::printf(g_fail ? "shim_test: %d failures\n" : "shim_test: all checks passed\n", g_fail);
     return g_fail ? 1 : 0;
