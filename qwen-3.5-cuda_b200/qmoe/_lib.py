@@ -108,7 +108,22 @@ SIGNATURES = [
     ("qmoe_tensor_bytes", c_uint64, [c_uint32, c_uint64]),
 ]
 
+# include/qmoe_ep.h, exported by libqmoe_ep.so (the expert-parallel host layer over NCCL)
+EP_LIB_PATH = Path(__file__).resolve().parent / "libqmoe_ep.so"
+QMOE_EP_DIRECT = 1
+EP_SIGNATURES = [
+    ("qmoe_ep_unique_id", c_int, [c_void_p]),
+    ("qmoe_ep_comm_init", c_int, [c_void_p, c_int, c_int, POINTER(c_void_p)]),
+    ("qmoe_ep_comm_destroy", c_int, [c_void_p]),
+    ("qmoe_ep_init", c_int, [c_void_p, POINTER(QmoeDims), c_int, c_int, POINTER(c_void_p)]),
+    ("qmoe_ep_is_direct", c_int, [c_void_p]),
+    ("qmoe_ep_forward", c_int, [c_void_p, POINTER(QmoeBlock), POINTER(QmoeBlock), c_void_p, c_void_p, c_void_p,
+                                c_float, c_void_p, c_void_p, c_int, c_void_p]),
+    ("qmoe_ep_finalize", c_int, [c_void_p]),
+]
+
 _lib = None
+_ep_lib = None
 
 
 def lib() -> ctypes.CDLL:
@@ -124,6 +139,22 @@ def lib() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = L
     return _lib
+
+
+def ep_lib() -> ctypes.CDLL:
+    """libqmoe_ep.so (loads libqmoe.so and NCCL; raises if it has not been built)."""
+    global _ep_lib
+    if _ep_lib is None:
+        lib()  # the C-ABI it calls into, from this directory
+        if not EP_LIB_PATH.exists():
+            raise ImportError(f"qmoe expert-parallel library not built: {EP_LIB_PATH} is missing")
+        L = ctypes.CDLL(str(EP_LIB_PATH))
+        for name, res, args in EP_SIGNATURES:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _ep_lib = L
+    return _ep_lib
 
 
 def status_string(st: int) -> str:

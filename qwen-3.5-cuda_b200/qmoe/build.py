@@ -17,6 +17,8 @@ CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 BUILD = ROOT / "_build"
 LIB = PKG / "libqmoe.so"
+EP_LIB = PKG / "libqmoe_ep.so"
+CUDA = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -65,6 +67,13 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         objs.append(o)
     if force or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-shared", "-Xcompiler", "-fopenmp", "-o", str(LIB), *map(str, objs)])
+    # the expert-parallel host layer over NCCL: its own library, so libqmoe
+    # itself does not depend on NCCL
+    ep_src = ROOT / "cpp" / "ep_host.cpp"
+    if force or _stale(EP_LIB, [ep_src, LIB, INCLUDE / "qmoe.h", INCLUDE / "qmoe_ep.h"]):
+        _run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden", "-Wall", "-Wextra", "-Werror",
+              f"-I{INCLUDE}", f"-I{CUDA}/include", str(ep_src), "-o", str(EP_LIB), f"-L{PKG}", "-lqmoe",
+              "-lnccl", f"-L{CUDA}/lib64", "-lcudart", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{CUDA}/lib64"])
     return LIB
 
 
