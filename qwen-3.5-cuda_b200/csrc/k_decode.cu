@@ -872,7 +872,8 @@ __device__ __forceinline__ void copy_g2s16(uint8_t* dst, const uint8_t* src, uin
 }
 
 template <int TR, int TS, int DR, int DS>
-__global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLayout L) {
+__global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant__ DecodeParams P,
+                                                          const __grid_constant__ FxLayout L) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     uint64_t* gfull = reinterpret_cast<uint64_t*>(smem);  // [8 slots][4 sub-chunks]
@@ -884,7 +885,6 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
     float* s_w = reinterpret_cast<float*>(smem + L.off_w);
     float* s_sg = reinterpret_cast<float*>(smem + L.off_sg);
     float* s_res = reinterpret_cast<float*>(smem + L.off_res);
-    float* ybuf = reinterpret_cast<float*>(smem + L.off_yb);
     uint8_t* gst = smem + L.off_gu;
     uint8_t* hs = smem + L.off_gu;  // the gate/up stages are free once every item is done
     uint8_t* dst = smem + L.off_dn;
@@ -1065,7 +1065,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
                 const int key = (tok << 1) | (routed ? 1 : 0);
                 if (key != cur_key) {
                     const XPlanesView xv = planes_view(smem_u32(xs) + static_cast<uint32_t>(tok) * static_cast<uint32_t>(P.xq_stride), d);
-                    if (routed) load_xu<TR>(xr, xv, u_r); else load_xu<TS>(xr, xv, u_s);
+                    if (TR == TS || routed) load_xu<TR>(xr, xv, u_r); else load_xu<TS>(xr, xv, u_s);
                     cur_key = key;
                 }
                 const int rl = (st << lgR) + rsub;
@@ -1076,7 +1076,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
                     if (tid == 0 && kk == 0) QMOE_TRACE(P, 1, 3);
                 }
                 float g, up;
-                if (routed) {
+                if (TR == TS || routed) {  // one copy of the dot code when the types agree
                     g = unit_dot_t<TR>(dg + static_cast<uint32_t>(rl) * rb, u_r, xr);
                     up = unit_dot_t<TR>(du + static_cast<uint32_t>(rl) * rb, u_r, xr);
                 } else {
@@ -1182,7 +1182,8 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
                 if (vi != cur_vi) {
                     const XPlanesView hv =
                         planes_view(smem_u32(hs) + static_cast<uint32_t>(vid) * static_cast<uint32_t>(P.hq_stride), P.H);
-                    if (shv) load_xu<DS>(xr, hv, unit_of_lane<DS>(lane & (Us - 1), lgUs));
+                    if (DS == DR) load_xu<DR>(xr, hv, unit_of_lane<DR>(lane & ((1 << lgUv) - 1), lgUv));
+                    else if (shv) load_xu<DS>(xr, hv, unit_of_lane<DS>(lane & (Us - 1), lgUs));
                     else load_xu<DR>(xr, hv, unit_of_lane<DR>(lane & (Ur - 1), lgUr));
                     cur_vi = vi;
                 }
@@ -1190,13 +1191,17 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
                 const int rl = (st << (5 - lgUv)) + rsub;
                 const bool valid = rl < nrow;
                 float y = 0.0f;
-                if (valid)
+                // one copy of the dot code when the shared and routed down types agree
+                if (valid && DS == DR)
+                    y = unit_dot_t<DR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(shv ? rbsd : rbd),
+                                       unit_of_lane<DR>(ul, lgUv), xr);
+                else if (valid)
                     y = shv ? unit_dot_t<DS>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbsd),
                                              unit_of_lane<DS>(ul, lgUs), xr)
                             : unit_dot_t<DR>(wbase + static_cast<uint32_t>(rl) * static_cast<uint32_t>(rbd),
                                              unit_of_lane<DR>(ul, lgUr), xr);
                 for (int o = (1 << lgUv) >> 1; o; o >>= 1) y += __shfl_xor_sync(FULL, y, o);
-                if (valid && ul == 0) stsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
+                if (valid && ul == 0) stsf(smem_u32(smem + L.off_yb) + 4u * static_cast<uint32_t>(vid * Rd + rl), y);
                 if (++st == (shv ? steps_s : steps_r)) {
                     st = 0;
                     if (++vi == cend && cc + 1 < nsrc) {
@@ -1213,12 +1218,13 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(DecodeParams P, FxLay
     if (tid == 0) QMOE_TRACE(P, 2, 5);
 
     // combine (moe.cu:76-81 and :90-96, accumulation order of layer_moe.cpp:127-153)
+    const uint32_t ybuf = smem_u32(smem + L.off_yb);
     for (int idx = tid; idx < P.T * nrow; idx += FX_NCW * 32) {
         const int t = idx / nrow, r = idx - t * nrow;
         float acc = 0.0f;
         for (int j = 0; j < P.k; ++j)
-            acc = fmaf(s_w[t * P.k + j], ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((t * P.k + j) * Rd + r)), acc);
-        if (sh) acc = fmaf(ldsf(smem_u32(ybuf) + 4u * static_cast<uint32_t>((P.T * P.k + t) * Rd + r)), s_sg[t], acc);
+            acc = fmaf(s_w[t * P.k + j], ldsf(ybuf + 4u * static_cast<uint32_t>((t * P.k + j) * Rd + r)), acc);
+        if (sh) acc = fmaf(ldsf(ybuf + 4u * static_cast<uint32_t>((P.T * P.k + t) * Rd + r)), s_sg[t], acc);
         if (!(s_w[t * P.k] == s_w[t * P.k])) acc = __uint_as_float(0x7FC00000u);  // routing error: NaN weights
         const size_t o = static_cast<size_t>(t) * d + r0d + r;
         P.out[o] = P.residual ? s_res[t * Rd + r] + acc : acc;

@@ -18,6 +18,21 @@ __device__ __forceinline__ float fkey_inv(uint32_t key) {
     return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
 }
 
+// Sum of lanes 0..k-1's v in lane order (one rounding per add, as a
+// sequential loop): the first eight values are gathered with independent
+// shuffles, then added in order.
+__device__ __forceinline__ float ordered_sum(float v, int k) {
+    float g[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = __shfl_sync(0xffffffffu, v, j);
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s = j < k ? s + g[j] : s;
+#pragma unroll 1
+    for (int j = 8; j < k; ++j) s += __shfl_sync(0xffffffffu, v, j);
+    return s;
+}
+
 // Top-k selection and softmax of one token by one warp (moe.cu:7-52 and the
 // checks of layer_moe.cpp:114-124): lane j < k returns the j-th selected
 // expert and its weight; `flag` is EF_ROUTING / EF_NOT_NORMALIZED / 0 on
@@ -68,17 +83,13 @@ __device__ __forceinline__ void select_token(const float* logits, int E, int k, 
             my_v = fkey_inv(mk);
         }
     }
-    float mx = __shfl_sync(0xffffffffu, my_v, 0);
-#pragma unroll 1
-    for (int j = 1; j < k; ++j) mx = fmaxf(mx, __shfl_sync(0xffffffffu, my_v, j));
+    // the selection is in descending order, so the largest selected logit
+    // (moe.cu:41-44) is lane 0's
+    const float mx = __shfl_sync(0xffffffffu, my_v, 0);
     const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
-    float sum = 0.0f;
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) sum += __shfl_sync(0xffffffffu, ex, j);
+    const float sum = ordered_sum(ex, k);
     wj = ex / sum;
-    float rs = 0.0f;
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) rs += __shfl_sync(0xffffffffu, wj, j);
+    const float rs = ordered_sum(wj, k);
     const bool lane_ok = lane >= k || (my_idx >= 0 && my_idx < E && isfinite(wj) && wj >= 0.0f);
     const bool ok = finite && __all_sync(0xffffffffu, lane_ok);
     flag = 0;
