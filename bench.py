@@ -297,7 +297,10 @@ def run_ours(args):
         line["ref_gpu"] = ref_gpu_baseline(blocks, inputs, dims, steps=4)
     if world == 1 and not args.no_extra:
         line["prefill"] = measure_prefill(blocks[0], dims)
+        line["prefill_stack"] = measure_prefill_stack(blocks, dims)
+        line["prefill_stack"]["token_by_token_tokens_per_s"] = round(1e6 / (value * L), 1)
         line["config3"] = measure_config3(dims)
+        line["gemv"] = measure_gemv(dims)
     if not args.no_extra:
         del blocks, cblocks
         line["ep_prefill"] = measure_ep(world, rank, dims)
@@ -463,9 +466,28 @@ def measure_ep(world, rank, dims):
                 lb, ld = ep.local_block(c, dc, rank, world)
                 entry["placement"] = "contiguous"
             be = ep.CudaBackend(c, lb, dc, ld, world, max_tokens=Tl, max_rows=2 * Tl, placement=pl)
-            moe = ep.ExpertParallelMoE(be, E, k, d, direct=True)
-            backends.append(be)
-            got = moe.forward(x)
+            if EP_IMPL == "abi":
+                # the C-ABI host layer (include/qmoe_ep.h): exchange and ordering in
+                # C++ over the library's own NCCL communicator; `be` only routes
+                # once more below to read the top-k ids for the parity check
+                abi = _ep_abi_context(dc, Tl, rank, world)
+                backends.append(abi)
+                pl_dev = be.placement
+                got = torch.empty_like(x)
+
+                def fwd_abi():
+                    _lib.check(_lib.ep_lib().qmoe_ep_forward(
+                        abi.ctx, ctypes.byref(c), ctypes.byref(lb), None if pl_dev is None else pl_dev.data_ptr(),
+                        x.data_ptr(), None, 1e-6, None, got.data_ptr(), Tl, None), "ep_forward")
+                fwd_abi()
+                be.route(x)
+                moe = None
+                entry["exchange"] = "C-ABI (qmoe_ep_forward, libqmoe_ep.so): NCCL from C++"
+            else:
+                moe = ep.ExpertParallelMoE(be, E, k, d, direct=True)
+                backends.append(be)
+                got = moe.forward(x)
+                entry["exchange"] = "Python (qmoe/ep.py over torch.distributed)"
             idx = be.topk_idx()
             want = out_all[rank * Tl:(rank + 1) * Tl]
             chk = torch.tensor([0.0 if torch.equal(idx, want_idx) else 1.0, float((got - want).abs().max())],
@@ -484,7 +506,10 @@ def measure_ep(world, rank, dims):
                                                     f"of ~{orc_rep['sample_tokens']} of them"}}
 
             def run():
-                moe.forward(x)
+                if moe is None:
+                    fwd_abi()
+                else:
+                    moe.forward(x)
         for _ in range(3):
             run()
         torch.cuda.synchronize()
@@ -518,6 +543,42 @@ def measure_ep(world, rank, dims):
     return res
 
 
+EP_IMPL = "abi"
+
+
+class _EpAbi:
+    """A qmoe_ep context (include/qmoe_ep.h) over its own NCCL communicator."""
+
+    def __init__(self, ctx, comm):
+        self.ctx, self.comm = ctx, comm
+
+    def close(self):
+        from qmoe import _lib
+        _lib.check(_lib.ep_lib().qmoe_ep_finalize(self.ctx), "ep_finalize")
+        _lib.check(_lib.ep_lib().qmoe_ep_comm_destroy(self.comm), "ep_comm_destroy")
+
+
+def _ep_abi_context(dc, max_tokens, rank, world):
+    """Rank 0 makes the NCCL id, torch.distributed hands it to every rank, each
+    rank builds its communicator and an expert-parallel context with the
+    peer-memory return."""
+    import torch.distributed as dist
+
+    from qmoe import _lib
+    L = _lib.ep_lib()
+    obj = [None]
+    if rank == 0:
+        uid = (ctypes.c_uint8 * 128)()
+        _lib.check(L.qmoe_ep_unique_id(uid), "ep_unique_id")
+        obj[0] = bytes(uid)
+    dist.broadcast_object_list(obj, src=0)
+    comm, ctx = ctypes.c_void_p(), ctypes.c_void_p()
+    _lib.check(L.qmoe_ep_comm_init((ctypes.c_uint8 * 128).from_buffer_copy(obj[0]), world, rank, ctypes.byref(comm)),
+               "ep_comm_init")
+    _lib.check(L.qmoe_ep_init(comm, ctypes.byref(dc), max_tokens, _lib.QMOE_EP_DIRECT, ctypes.byref(ctx)), "ep_init")
+    return _EpAbi(ctx, comm)
+
+
 def _ep_oracle_parity(blk, dims, x_local, idx_local, out_local, bias_h, world):
     """One rank's share of the expert-parallel parity: its tokens' expert ids
     against the oracle's routing, and the outputs of a sample of them."""
@@ -540,6 +601,7 @@ def measure_config3(dims):
     """mixed-quant decode (gate/up Q4_K, down Q6_K, shared
     Q8_0, per-expert router bias ~N(0,1)) at B = 1, 2, 4, 8 tokens per call,
     through 8 layers (~4 GB of weights, larger than L2)."""
+    import numpy as np
     import torch
 
     from qmoe import _lib, synth
@@ -557,31 +619,155 @@ def measure_config3(dims):
         bufs = [torch.empty_like(x), torch.empty_like(x)]
         gamma = torch.ones(dims.d_model, dtype=torch.float32, device="cuda")
 
-        def step():
+        def step(sp):
             cur = x
             for l in range(L):
                 o = bufs[l % 2]
                 _lib.check(_lib.lib().qmoe_block_forward_prenorm(ctypes.byref(cbs[l]), ctypes.byref(dc),
                                                                  cur.data_ptr(), gamma.data_ptr(), EPS,
-                                                                 o.data_ptr(), B, ws.data_ptr(), n, None))
+                                                                 o.data_ptr(), B, ws.data_ptr(), n, sp))
                 cur = o
 
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                step(s.cuda_stream)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step(torch.cuda.current_stream().cuda_stream)
         for _ in range(3):
-            step()
+            g.replay()
         torch.cuda.synchronize()
         reps = 20
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            step()
+            g.replay()
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (reps * L)
         st, flags, _ = _check_errors(_lib, ws, dc)
+        # distinct experts hit by the B tokens of the last layer's call (its offsets)
+        offs = _ws_view(_lib, ws, dc, B, _lib.WS_OFFSETS, dims.num_experts + 1, np.int32)
+        U = int((np.diff(offs) > 0).sum())
+        nbytes = 2_097_152 + U * 2_039_808 + 3_342_336 + 8_192 + B * 16_384
+        gbs = nbytes / (us * 1e-6) / 1e9
         res.append({"B": B, "us_per_block": round(us, 2), "us_per_token_block": round(us / B, 2),
-                    "error_flags": flags})
+                    "distinct_experts": U, "algorithmic_bytes": nbytes, "achieved_gbs": round(gbs, 1),
+                    "frac_of_hbm": round(gbs / _peaks()[0], 4), "error_flags": flags})
+        del g
     return {"config": "config3: mixed-quant decode (gate/up Q4_K, down Q6_K, shared Q8_0, router bias N(0,1)), "
-                      "8 layers, eager launches", "results": res}
+                      "8 layers, one CUDA graph per step; bytes = router + U x (Q4_K gate/up + Q6_K down) + "
+                      "Q8_0 shared + gate vector + B x (x, out), U = distinct experts hit", "results": res}
+
+
+LM_HEAD_ROWS = 248_320  # vocabulary rows of the LM head (src/model.cpp:216)
+
+
+def measure_gemv(dims):
+    """The matmul_dispatch path at the LM head's shape (248,320 x 2048,
+    src/model.cpp:216): the streaming unit-decode GEMV (qmoe_gemv) and the
+    reference-order kernel (qmoe_gemv_exact) for Q4_K, Q6_K and Q8_0 weights,
+    HBM roofline on the weight bytes; outputs of a row sample checked against
+    the oracle's F32 products."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as orc
+    from qmoe import _lib
+    M, K = LM_HEAD_ROWS, dims.d_model
+    out = {"shape": [M, K], "what": "y = W x, one token (LM head of src/model.cpp:216 and the other "
+                                    "matmul_dispatch callers)", "types": {}}
+    peak = _peaks()
+    for ty, name in ((12, "Q4_K"), (14, "Q6_K"), (8, "Q8_0")):
+        n = M * K
+        nb = _lib.lib().qmoe_tensor_bytes(ty, n)
+        w = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        _lib.check(_lib.lib().qmoe_synth_fill(w.data_ptr(), ty, n, SEED + 21, ty, 0.02, None))
+        x = synth_inputs_1(K)
+        t = _lib.QmoeTensor(w.data_ptr(), ty, 0, n)
+        ent = {}
+        ys = {}
+        for impl, fn in (("stream", _lib.lib().qmoe_gemv), ("exact", _lib.lib().qmoe_gemv_exact)):
+            y = torch.empty(M, device="cuda")
+            for _ in range(3):
+                _lib.check(fn(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, 0, None))
+            torch.cuda.synchronize()
+            reps = 10 if impl == "stream" else 3
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn(ctypes.byref(t), x.data_ptr(), y.data_ptr(), M, K, 0, None)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            gbs = (nb + 4 * K + 4 * M) / (us * 1e-6) / 1e9
+            ent[impl] = {"us": round(us, 1), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak[0], 4)}
+            ys[impl] = y
+        # parity: 4 blocks of 64 rows against the oracle (F32 products), stream vs exact over all rows
+        wh = w.cpu().numpy()
+        xh = x.cpu().numpy()
+        worst = 0.0
+        for r0 in (0, 77_777, 160_000, M - 64):
+            want = orc.gemv(wh, ty, n, xh, 64, K, r0 * K)
+            worst = max(worst, float(np.max(np.abs(ys["stream"][r0:r0 + 64].cpu().numpy() - want))))
+        ent["parity"] = {"stream_vs_oracle_max_abs": worst, "rows_checked": 256,
+                         "stream_vs_exact_max_abs_all_rows": float((ys["stream"] - ys["exact"]).abs().max()),
+                         "within_1e-5": worst <= 1e-5}
+        ent["bytes"] = nb
+        ent["speedup_vs_exact"] = round(ent["exact"]["us"] / ent["stream"]["us"], 1)
+        out["types"][name] = ent
+        del w
+    out["peak"] = {"hbm_gbs": peak[0], "kind": peak[1]}
+    return out
+
+
+def synth_inputs_1(K):
+    from qmoe import synth
+    return synth.inputs(1, K, seed=SEED + 22, tag=9)[0].contiguous()
+
+
+def measure_prefill_stack(blocks, dims, T=4096):
+    """The batched layer loop (qmoe_stack_forward): T=4096 tokens through the
+    MoE halves of all 40 layers of the decode stack (pre-norm and residual
+    fused), the multi-token loop the reference does not have -- it feeds a
+    prompt token by token (src/main.cpp:391-393), i.e. at the decode rate."""
+    import torch
+
+    from qmoe import _lib, synth
+    L = len(blocks)
+    dc = dims.c()
+    n = _lib.lib().qmoe_workspace_size(ctypes.byref(dc), T)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_workspace_init(ws.data_ptr(), n, None))
+    x0 = synth.inputs(T, dims.d_model, seed=SEED + 9, tag=11)
+    resid, tmp = x0.clone(), torch.empty_like(x0)
+    norms = torch.ones(dims.d_model, device="cuda")
+    cb = (_lib.QmoeBlock * L)(*[b.c() for b in blocks])
+    nptr = (ctypes.c_void_p * L)(*([norms.data_ptr()] * L))
+
+    def run():
+        _lib.check(_lib.lib().qmoe_stack_forward(cb, nptr, L, ctypes.byref(dc), EPS, resid.data_ptr(),
+                                                 tmp.data_ptr(), T, ws.data_ptr(), n, None), "stack_forward")
+
+    resid.copy_(x0)
+    run()
+    torch.cuda.synchronize()
+    reps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    st, flags, _ = _check_errors(_lib, ws, dc)
+    finite = bool(torch.isfinite(resid).all())
+    return {"config": f"T={T} tokens through the MoE halves of {L} layers (qmoe_stack_forward, tensor-core path), "
+                      "random-routing Q4_K stack of the decode line",
+            "us_per_pass": round(us, 1), "tokens_per_s": round(T / (us * 1e-6), 0),
+            "us_per_block": round(us / L, 1), "finite": finite, "error_flags": flags}
 
 
 def _bf16_peak():
@@ -853,9 +1039,13 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill (config 4) and mixed decode (config 3) lines")
-    ap.add_argument("--only", choices=["prefill", "config3", "ep"],
+    ap.add_argument("--only", choices=["prefill", "config3", "ep", "gemv"],
                     help="run one extra measurement alone and print its object (profiling runs)")
+    ap.add_argument("--ep-impl", choices=["abi", "python"], default="abi",
+                    help="expert-parallel exchange at N > 1: the C-ABI host layer (default) or qmoe/ep.py")
     args = ap.parse_args()
+    global EP_IMPL
+    EP_IMPL = args.ep_impl
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -884,6 +1074,8 @@ def run_only(what):
         res = measure_prefill(synth.Block(dims, synth.Q4K_TYPES, seed=SEED, layer=0, device="cuda"), dims)
     elif what == "config3":
         res = measure_config3(dims)
+    elif what == "gemv":
+        res = measure_gemv(dims)
     else:
         res = measure_ep(world, rank, dims)
     if world > 1:

@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(GV_WARPS * 32)
 // match an F32 dot product to ~2^-22 relative; the reduction order differs
 // from the reference's, so outputs are not bit-identical (k_gemv is).
 // ---------------------------------------------------------------------------
-constexpr int GS_NCW = 8;                      // consumer warps
+constexpr int GS_NCW = 16;                     // consumer warps
 constexpr int GS_THREADS = (GS_NCW + 1) * 32;  // + one producer warp
 constexpr int GS_MAX_STAGES = 12;
 
