@@ -717,6 +717,27 @@ def measure_gemv(dims):
                          "within_1e-5": worst <= 1e-5}
         ent["bytes"] = nb
         ent["speedup_vs_exact"] = round(ent["exact"]["us"] / ent["stream"]["us"], 1)
+        if ty == 14:  # the load-time repack into 16-byte-aligned super-blocks (qmoe_repack)
+            nr = _lib.lib().qmoe_repack_bytes(ty, n, _lib.QMOE_LAYOUT_Q6K_A16)
+            wr = torch.empty(nr, dtype=torch.uint8, device="cuda")
+            _lib.check(_lib.lib().qmoe_repack(ctypes.byref(t), _lib.QMOE_LAYOUT_Q6K_A16, wr.data_ptr(), nr, None))
+            tr = _lib.QmoeTensor(wr.data_ptr(), ty, _lib.QMOE_LAYOUT_Q6K_A16, n)
+            yr = torch.empty(M, device="cuda")
+            for _ in range(3):
+                _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(tr), x.data_ptr(), yr.data_ptr(), M, K, 0, None))
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                _lib.lib().qmoe_gemv(ctypes.byref(tr), x.data_ptr(), yr.data_ptr(), M, K, 0, None)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / 10
+            gbs = (nr + 4 * K + 4 * M) / (us * 1e-6) / 1e9
+            ent["repacked_a16"] = {"us": round(us, 1), "bytes": nr, "gbs": round(gbs, 1),
+                                   "frac_of_hbm": round(gbs / peak[0], 4),
+                                   "bit_identical_to_gguf_layout": bool(torch.equal(yr, ys["stream"]))}
+            del wr
         out["types"][name] = ent
         del w
     out["peak"] = {"hbm_gbs": peak[0], "kind": peak[1]}

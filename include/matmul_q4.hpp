@@ -22,6 +22,16 @@ void matmul_dispatch(const QuantTensor& weight, const float* x, float* y, int M,
 // out[0..cols) = row `row` of tensor, dequantised to F32, asynchronous on `stream`.
 void dequantize_row(const QuantTensor& tensor, float* out, int row, int cols, cudaStream_t stream = nullptr);
 
+// Optional load-time repack (no counterpart in the reference, whose loader
+// uploads every tensor as stored, src/loader_gguf.cpp:322-381): for a Q6_K
+// tensor read only by matmul_dispatch (the LM head of Q4_K_M models, for
+// example), moves its super-blocks into 16-byte-aligned 224-byte slots
+// (qmoe_repack, QMOE_LAYOUT_Q6K_A16): a new cudaMalloc allocation replaces
+// device_ptr (the old one is freed; the loader's unload frees the new one),
+// size_bytes and layout are updated.  Other types are left as they are.
+// Returns true if the tensor was repacked.  Synchronises `stream`.
+bool repack_tensor(QuantTensor& tensor, cudaStream_t stream = nullptr);
+
 }  // namespace qwen
 
 #endif  // QWEN_MATMUL_Q4_HPP

@@ -15,6 +15,8 @@
  *   qmoe_gemv_exact       src/cuda/matmul_q4.cu:140-167 gemv_kernel (same
  *                         operation order, bit-identical output)
  *   qmoe_dequant_row      include/matmul_q4.hpp:24-30 dequantize_row
+ *   qmoe_repack           src/loader_gguf.cpp:322-381 (an optional repack step
+ *                         after a tensor's upload; the reference uploads raw)
  *   qmoe_router_topk      src/layer_moe.cpp:98-99     router GEMV + moe_topk
  *                         (src/cuda/moe.cu:7-57), plus the host checks of
  *                         src/layer_moe.cpp:102-124 moved onto the device
@@ -72,9 +74,18 @@ enum qmoe_status {
 typedef struct qmoe_tensor {
     const void* data;       /* device pointer to the raw GGUF payload, 16-byte aligned */
     uint32_t ggml_type;     /* GgmlType id (include/quantized.hpp:12-36) */
-    uint32_t reserved;      /* must be 0 */
+    uint32_t layout;        /* QMOE_LAYOUT_GGUF (0): the GGUF bytes in place; other values:
+                               a repacked copy made by qmoe_repack */
     uint64_t num_elements;  /* logical element count */
 } qmoe_tensor;
+
+/* Byte layouts of a tensor's payload (qmoe_tensor.layout). */
+enum qmoe_layout {
+    QMOE_LAYOUT_GGUF = 0,     /* the GGUF blocks as stored in the file, read in place */
+    QMOE_LAYOUT_Q6K_A16 = 1   /* Q6_K only: each 210-byte super-block in a 224-byte slot
+                                 (14 zero bytes after it), so every block starts on a
+                                 16-byte boundary; read by qmoe_gemv */
+};
 
 /* MoE dimensions (reference ModelConfig MoE fields, include/config.hpp:33-37). */
 typedef struct qmoe_dims {
@@ -139,6 +150,18 @@ QMOE_API int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, in
  * the reference kernel's output. */
 QMOE_API int qmoe_gemv_exact(const qmoe_tensor* w, const float* x, float* y, int M, int K,
               uint64_t element_offset, qmoe_stream_t stream);
+
+/* Load-time repack (the GGUF loader's upload, src/loader_gguf.cpp:322-381,
+ * may call it once per tensor): bytes of a tensor of `ggml_type` and
+ * `num_elements` in `layout` (0 if that layout does not apply to the type),
+ * and the copy of src (GGUF layout) into dst in `layout`.  Only
+ * QMOE_LAYOUT_Q6K_A16 of Q6_K tensors is defined: +6.7% bytes, and
+ * qmoe_gemv's unit decoder reads aligned 16-byte words instead of two reads
+ * and a funnel shift per word.  The block entry points take GGUF layouts only
+ * (QMOE_ERR_UNSUPPORTED otherwise). */
+QMOE_API uint64_t qmoe_repack_bytes(uint32_t ggml_type, uint64_t num_elements, uint32_t layout);
+QMOE_API int qmoe_repack(const qmoe_tensor* src, uint32_t layout, void* dst, size_t dst_bytes,
+                         qmoe_stream_t stream);
 
 /* out[cols] = elements [row*cols, row*cols + cols) of W, dequantised to F32. */
 QMOE_API int qmoe_dequant_row(const qmoe_tensor* w, float* out, int row, int cols, qmoe_stream_t stream);

@@ -29,6 +29,8 @@ struct QuantTensor {
     uint64_t size_bytes;
     uint64_t offset;              // byte offset in the GGUF payload
     void* device_ptr = nullptr;   // device copy of the payload
+    uint32_t layout = 0;          // byte layout of device_ptr (qmoe_layout: 0 = the GGUF blocks as
+                                  // uploaded; set by repack_tensor, include/matmul_q4.hpp)
 };
 
 namespace detail {

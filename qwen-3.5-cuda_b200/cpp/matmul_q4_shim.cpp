@@ -17,6 +17,7 @@ qmoe_tensor view(const QuantTensor& t) {
     v.data = t.device_ptr;
     v.ggml_type = static_cast<uint32_t>(t.type);
     v.num_elements = t.num_elements;
+    v.layout = t.layout;
     return v;
 }
 
@@ -46,6 +47,26 @@ void dequantize_row(const QuantTensor& t, float* out, int row, int cols, cudaStr
     const int st = qmoe_dequant_row(&v, out, row, cols, stream);
     if (st == QMOE_ERR_SHAPE) throw std::runtime_error("row is outside tensor '" + t.name + "'");
     if (st != QMOE_OK) raise_status(st, "dequantize_row");
+}
+
+bool repack_tensor(QuantTensor& t, cudaStream_t stream) {
+    if (!t.device_ptr) throw std::runtime_error("tensor '" + t.name + "' is not loaded");
+    if (t.type != GgmlType::Q6_K || t.layout != QMOE_LAYOUT_GGUF) return false;
+    const uint64_t n = qmoe_repack_bytes(static_cast<uint32_t>(t.type), t.num_elements, QMOE_LAYOUT_Q6K_A16);
+    if (n == 0) return false;
+    void* dst = nullptr;
+    if (cudaMalloc(&dst, n) != cudaSuccess) throw std::runtime_error("CUDA Error: out of memory repacking '" + t.name + "'");
+    const qmoe_tensor v = view(t);
+    const int st = qmoe_repack(&v, QMOE_LAYOUT_Q6K_A16, dst, n, stream);
+    if (st != QMOE_OK || cudaStreamSynchronize(stream) != cudaSuccess) {
+        cudaFree(dst);
+        raise_status(st != QMOE_OK ? st : QMOE_ERR_CUDA, "repack_tensor");
+    }
+    cudaFree(t.device_ptr);
+    t.device_ptr = dst;
+    t.size_bytes = n;
+    t.layout = QMOE_LAYOUT_Q6K_A16;
+    return true;
 }
 
 }  // namespace qwen

@@ -192,6 +192,30 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_stream(GemvStream p) {
     }
 }
 
+// Q6_K -> the 16-byte-aligned layout: super-block b's 210 bytes at 224*b,
+// then 14 zero bytes.  One thread per 16-byte output chunk; the source is
+// read in 2-byte words (GGUF Q6_K blocks are 2-byte aligned).
+__global__ void k_repack_q6k_a16(const uint8_t* __restrict__ src, uint4* __restrict__ dst, uint64_t nblocks) {
+    const uint64_t nchunks = nblocks * 14;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < nchunks;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint64_t b = i / 14;
+        const int j = static_cast<int>(i - b * 14);
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src + b * 210 + 16 * j);
+        const int nw = j < 13 ? 8 : 1;  // the last chunk holds bytes 208..209, then padding
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        for (int k = 0; k < nw; ++k) w[k >> 1] |= static_cast<uint32_t>(__ldg(s16 + k)) << (16 * (k & 1));
+        dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+cudaError_t launch_repack_q6k_a16(const uint8_t* src, void* dst, uint64_t nblocks, cudaStream_t s) {
+    const uint64_t nchunks = nblocks * 14;
+    const int grid = static_cast<int>(std::min<uint64_t>((nchunks + 255) / 256, 148ull * 16));
+    k_repack_q6k_a16<<<grid, 256, 0, s>>>(src, static_cast<uint4*>(dst), nblocks);
+    return cudaGetLastError();
+}
+
 __global__ void k_dequant_row(const uint8_t* __restrict__ w, int type, float* __restrict__ out, uint64_t start, int cols) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += blockDim.x * gridDim.x)
         out[i] = dq1(w, type, start + i);
@@ -222,13 +246,19 @@ int g_sms[64], g_optin[64];
 // 2^j elements (K <= 4096) whose first row starts on a boundary the unit
 // decoders can read (16 bytes for the K-quants with 16-byte blocks, 4 for
 // Q8_0, 2 for Q6_K).
+// Block bytes of the types the streaming kernel reads (T_Q6_K_A16: the
+// repacked Q6_K layout of qmoe_repack).
+static int stream_block_bytes(int type) {
+    return type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : type == T_Q6_K_A16 ? 224 : 34;
+}
+
 bool gemv_stream_supported(const uint8_t* w, int type, int K, uint64_t off) {
-    if (type != T_Q4_K && type != T_Q5_K && type != T_Q6_K && type != T_Q8_0) return false;
+    if (type != T_Q4_K && type != T_Q5_K && type != T_Q6_K && type != T_Q6_K_A16 && type != T_Q8_0) return false;
     if (K < 256 || K > 4096 || (K & (K - 1))) return false;
-    const int be = type == T_Q8_0 ? 32 : 256, bb = type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : 34;
+    const int be = type == T_Q8_0 ? 32 : 256, bb = stream_block_bytes(type);
     if (off % be) return false;
     const uintptr_t a = reinterpret_cast<uintptr_t>(w) + off / be * bb;
-    const uintptr_t need = (type == T_Q4_K || type == T_Q5_K) ? 16 : type == T_Q8_0 ? 4 : 2;
+    const uintptr_t need = (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K_A16) ? 16 : type == T_Q8_0 ? 4 : 2;
     return a % need == 0;
 }
 
@@ -243,7 +273,7 @@ cudaError_t launch_gemv_stream(const uint8_t* w, int type, uint64_t w_bytes, con
         if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
         if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
     }
-    const int be = type == T_Q8_0 ? 32 : 256, bb = type == T_Q4_K ? 144 : type == T_Q5_K ? 176 : type == T_Q6_K ? 210 : 34;
+    const int be = type == T_Q8_0 ? 32 : 256, bb = stream_block_bytes(type);
     GemvStream p;
     p.w = w + off / be * bb;
     p.wend = w + w_bytes;
@@ -271,6 +301,7 @@ cudaError_t launch_gemv_stream(const uint8_t* w, int type, uint64_t w_bytes, con
         case T_Q4_K: kern = pick_stream<T_Q4_K>(upl); break;
         case T_Q5_K: kern = pick_stream<T_Q5_K>(upl); break;
         case T_Q6_K: kern = pick_stream<T_Q6_K>(upl); break;
+        case T_Q6_K_A16: kern = pick_stream<T_Q6_K_A16>(upl); break;
         case T_Q8_0: kern = pick_stream<T_Q8_0>(upl); break;
         default: break;
     }

@@ -4,6 +4,7 @@
 #include <cstring>
 #include "qmoe_dev.cuh"
 #include "qmoe_internal.h"
+#include "qmoe_units.cuh"
 #include "qmoe_tgemm.h"
 
 namespace qmoe {
@@ -38,6 +39,7 @@ cudaError_t launch_dequant_row(const uint8_t* w, int type, float* out, uint64_t 
 bool gemv_stream_supported(const uint8_t* w, int type, int K, uint64_t off);
 cudaError_t launch_gemv_stream(const uint8_t* w, int type, uint64_t w_bytes, const float* x, float* y, int M, int K,
                                uint64_t off, cudaStream_t s);
+cudaError_t launch_repack_q6k_a16(const uint8_t* src, void* dst, uint64_t nblocks, cudaStream_t s);
 cudaError_t launch_synth(void* dst, int type, uint64_t nblocks, uint64_t seed, uint64_t stream_id, float sigma,
                          cudaStream_t s);
 cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets, int32_t* perm, int32_t* inv_perm,
@@ -86,6 +88,7 @@ int check_dims(const qmoe_dims* D) {
 
 int check_tensor(const qmoe_tensor& t, uint64_t need, bool (*typeok)(uint32_t)) {
     if (!t.data) return QMOE_ERR_ARG;
+    if (t.layout != QMOE_LAYOUT_GGUF) return QMOE_ERR_UNSUPPORTED;  // the block kernels read GGUF blocks
     if (!typeok(t.ggml_type)) return QMOE_ERR_TYPE;
     if (t.num_elements < need) return QMOE_ERR_SHAPE;
     const int be = blk_elems(static_cast<int>(t.ggml_type));
@@ -229,10 +232,20 @@ int qmoe_gemv(const qmoe_tensor* w, const float* x, float* y, int M, int K, uint
     if (!gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
     if (M <= 0 || K <= 0 || off + static_cast<uint64_t>(M) * K > w->num_elements) return QMOE_ERR_SHAPE;
     const uint8_t* wp = static_cast<const uint8_t*>(w->data);
-    const int type = static_cast<int>(w->ggml_type);
+    int type = static_cast<int>(w->ggml_type);
+    uint64_t wbytes = qmoe_tensor_bytes(w->ggml_type, w->num_elements);
+    if (w->layout == QMOE_LAYOUT_Q6K_A16) {
+        if (type != T_Q6_K) return QMOE_ERR_UNSUPPORTED;
+        type = T_Q6_K_A16;
+        wbytes = qmoe_repack_bytes(w->ggml_type, w->num_elements, w->layout);
+        // the repacked layout has only the streaming kernel
+        if (!gemv_stream_supported(wp, type, K, off) || reinterpret_cast<uintptr_t>(x) % 16)
+            return QMOE_ERR_UNSUPPORTED;
+    } else if (w->layout != QMOE_LAYOUT_GGUF) {
+        return QMOE_ERR_UNSUPPORTED;
+    }
     if (gemv_stream_supported(wp, type, K, off) && reinterpret_cast<uintptr_t>(x) % 16 == 0)
-        return cuda_status(launch_gemv_stream(wp, type, qmoe_tensor_bytes(w->ggml_type, w->num_elements), x, y, M, K,
-                                              off, reinterpret_cast<cudaStream_t>(stream)));
+        return cuda_status(launch_gemv_stream(wp, type, wbytes, x, y, M, K, off, reinterpret_cast<cudaStream_t>(stream)));
     return cuda_status(launch_gemv(wp, type, x, y, M, K, off, reinterpret_cast<cudaStream_t>(stream)));
 }
 
@@ -240,13 +253,35 @@ int qmoe_gemv_exact(const qmoe_tensor* w, const float* x, float* y, int M, int K
                     qmoe_stream_t stream) {
     if (!w || !w->data || !x || !y) return QMOE_ERR_ARG;
     if (!gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
+    if (w->layout != QMOE_LAYOUT_GGUF) return QMOE_ERR_UNSUPPORTED;
     if (M <= 0 || K <= 0 || off + static_cast<uint64_t>(M) * K > w->num_elements) return QMOE_ERR_SHAPE;
     return cuda_status(launch_gemv(static_cast<const uint8_t*>(w->data), static_cast<int>(w->ggml_type), x, y, M, K,
                                    off, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+uint64_t qmoe_repack_bytes(uint32_t t, uint64_t n, uint32_t layout) {
+    if (layout == QMOE_LAYOUT_GGUF) return qmoe_tensor_bytes(t, n);
+    if (layout == QMOE_LAYOUT_Q6K_A16 && static_cast<int>(t) == T_Q6_K && n % 256 == 0) return n / 256 * 224;
+    return 0;
+}
+
+int qmoe_repack(const qmoe_tensor* src, uint32_t layout, void* dst, size_t dst_bytes, qmoe_stream_t stream) {
+    if (!src || !src->data || !dst) return QMOE_ERR_ARG;
+    if (src->layout != QMOE_LAYOUT_GGUF) return QMOE_ERR_UNSUPPORTED;
+    const uint64_t need = qmoe_repack_bytes(src->ggml_type, src->num_elements, layout);
+    if (need == 0) return layout == QMOE_LAYOUT_Q6K_A16 ? QMOE_ERR_TYPE : QMOE_ERR_UNSUPPORTED;
+    if (dst_bytes < need) return QMOE_ERR_SHAPE;
+    if (!aligned16(dst)) return QMOE_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (layout == QMOE_LAYOUT_GGUF)
+        return cuda_status(cudaMemcpyAsync(dst, src->data, need, cudaMemcpyDeviceToDevice, s));
+    if (reinterpret_cast<uintptr_t>(src->data) % 2) return QMOE_ERR_ALIGN;
+    return cuda_status(launch_repack_q6k_a16(static_cast<const uint8_t*>(src->data), dst, src->num_elements / 256, s));
+}
+
 int qmoe_dequant_row(const qmoe_tensor* w, float* out, int row, int cols, qmoe_stream_t stream) {
     if (!w || !w->data || !out || !gemv_type(w->ggml_type)) return QMOE_ERR_TYPE;
+    if (w->layout != QMOE_LAYOUT_GGUF) return QMOE_ERR_UNSUPPORTED;
     const uint64_t start = static_cast<uint64_t>(row) * cols;
     if (row < 0 || cols <= 0 || start + cols > w->num_elements) return QMOE_ERR_SHAPE;
     return cuda_status(launch_dequant_row(static_cast<const uint8_t*>(w->data), static_cast<int>(w->ggml_type), out,

@@ -23,7 +23,12 @@
 namespace qmoe {
 
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14,
-             T_BF16 = 30 };
+             T_BF16 = 30,
+             // not a GGML id: Q6_K super-blocks repacked into 224-byte slots
+             // (210 payload bytes + 14 zero bytes), every block 16-byte aligned
+             T_Q6_K_A16 = 0x100 | T_Q6_K };
+
+__host__ __device__ constexpr bool is_q6k(int type) { return type == T_Q6_K || type == T_Q6_K_A16; }
 
 // Activation planes + meta of one unit, in registers.
 struct XU {
@@ -34,7 +39,7 @@ struct XU {
 
 // Element index of run q (0..3) of unit u for a weight type.
 __device__ __forceinline__ int unit_run_start(int type, int u, int q) {
-    if (type == T_Q6_K) return 256 * (u >> 2) + 128 * ((u >> 1) & 1) + 32 * q + 16 * (u & 1);
+    if (is_q6k(type)) return 256 * (u >> 2) + 128 * ((u >> 1) & 1) + 32 * q + 16 * (u & 1);
     return 64 * u + 16 * q;
 }
 
@@ -44,7 +49,7 @@ __device__ __forceinline__ int unit_run_start(int type, int u, int q) {
 // quarter-warp reads eight distinct bank groups of the swizzled planes.
 template <int TYPE>
 __device__ __forceinline__ int unit_of_lane(int i, int lgU) {
-    if (TYPE != T_Q6_K || lgU < 4) return i;
+    if (!is_q6k(TYPE) || lgU < 4) return i;
     const int m = 2 * ((i >> 1) & 3) + ((i >> 3) & 1) + 8 * (i >> 4);
     return 2 * m + (i & 1);
 }
@@ -61,7 +66,7 @@ __device__ __forceinline__ void load_xu(XU& x, const XPlanesView& xv, int u) {
         x.x1[4 * q] = b.x; x.x1[4 * q + 1] = b.y; x.x1[4 * q + 2] = b.z; x.x1[4 * q + 3] = b.w;
         x.x2[4 * q] = c.x; x.x2[4 * q + 1] = c.y; x.x2[4 * q + 2] = c.z; x.x2[4 * q + 3] = c.w;
     }
-    if (TYPE == T_Q6_K) {
+    if (is_q6k(TYPE)) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const float2 m = ldsf2(xv.meta + 8u * static_cast<uint32_t>(unit_run_start(TYPE, u, q) >> 4));
@@ -158,14 +163,28 @@ __device__ __forceinline__ float dot_q8_0(uint32_t row, int u, const XU& x) {
     return d0 * (x.sc[0] * planes_combine(a0, a1, a2)) + d1 * (x.sc[2] * planes_combine(b0, b1, b2));
 }
 
-// Q6_K unit dot (210-byte blocks: 2-byte aligned in general).
+// Q6_K unit dot.  BB = 210: GGUF blocks, 2-byte aligned in general (each
+// 16-byte read is two aligned reads and a funnel shift); BB = 224: the
+// repacked layout, every block 16-byte aligned (plain 16-byte reads).
+template <int BB = 210>
 __device__ __forceinline__ float dot_q6_k(uint32_t row, int u, const XU& x) {
-    const uint32_t blk = row + 210u * static_cast<uint32_t>(u >> 2);
+    const uint32_t blk = row + static_cast<uint32_t>(BB) * static_cast<uint32_t>(u >> 2);
     const int h = (u >> 1) & 1, a = u & 1;
-    uint4 l0 = lds128_any(blk + 64 * h + 16 * a);
-    uint4 l1 = lds128_any(blk + 64 * h + 32 + 16 * a);
-    uint4 qh = lds128_any(blk + 128 + 32 * h + 16 * a);
-    uint32_t s0 = lds32_any(blk + 192 + 8 * h), s1 = lds32_any(blk + 196 + 8 * h);
+    uint4 l0, l1, qh;
+    uint32_t s0, s1;
+    if (BB % 16 == 0) {
+        l0 = lds128(blk + 64 * h + 16 * a);
+        l1 = lds128(blk + 64 * h + 32 + 16 * a);
+        qh = lds128(blk + 128 + 32 * h + 16 * a);
+        s0 = lds32(blk + 192 + 8 * h);
+        s1 = lds32(blk + 196 + 8 * h);
+    } else {
+        l0 = lds128_any(blk + 64 * h + 16 * a);
+        l1 = lds128_any(blk + 64 * h + 32 + 16 * a);
+        qh = lds128_any(blk + 128 + 32 * h + 16 * a);
+        s0 = lds32_any(blk + 192 + 8 * h);
+        s1 = lds32_any(blk + 196 + 8 * h);
+    }
     const float d = h2f_bits(lds16(blk + 208));
     // scales[8h + 2q + a], q = 0..3 -> bytes a, a+2 of s0 and a, a+2 of s1
     const uint32_t sa = 8u * static_cast<uint32_t>(a);
@@ -216,7 +235,8 @@ template <int TYPE>
 __device__ __forceinline__ float unit_dot_t(uint32_t row, int u, const XU& x) {
     if (TYPE == T_Q4_K) return dot_qk45<false>(row, u, x);
     if (TYPE == T_Q5_K) return dot_qk45<true>(row, u, x);
-    if (TYPE == T_Q6_K) return dot_q6_k(row, u, x);
+    if (TYPE == T_Q6_K) return dot_q6_k<210>(row, u, x);
+    if (TYPE == T_Q6_K_A16) return dot_q6_k<224>(row, u, x);
     return dot_q8_0(row, u, x);
 }
 

@@ -24,12 +24,13 @@ QMOE_ERR_ROUTING = 10
 QMOE_ERR_NOT_NORMALIZED = 11
 QMOE_ERR_TIMEOUT = 12
 QMOE_ERR_COMM = 13
+QMOE_LAYOUT_GGUF, QMOE_LAYOUT_Q6K_A16 = 0, 1
 
 WS_LOGITS, WS_TOPK_IDX, WS_TOPK_W, WS_OFFSETS, WS_PERM, WS_INV_PERM, WS_HIDDEN, WS_ERROR, WS_INPUT, WS_INPUT16 = range(10)
 
 
 class QmoeTensor(ctypes.Structure):
-    _fields_ = [("data", c_void_p), ("ggml_type", c_uint32), ("reserved", c_uint32), ("num_elements", c_uint64)]
+    _fields_ = [("data", c_void_p), ("ggml_type", c_uint32), ("layout", c_uint32), ("num_elements", c_uint64)]
 
 
 class QmoeDims(ctypes.Structure):
@@ -56,6 +57,8 @@ SIGNATURES = [
     ("qmoe_gemv", c_int, [POINTER(QmoeTensor), c_void_p, c_void_p, c_int, c_int, c_uint64, c_void_p]),
     ("qmoe_gemv_exact", c_int, [POINTER(QmoeTensor), c_void_p, c_void_p, c_int, c_int, c_uint64, c_void_p]),
     ("qmoe_dequant_row", c_int, [POINTER(QmoeTensor), c_void_p, c_int, c_int, c_void_p]),
+    ("qmoe_repack_bytes", c_uint64, [c_uint32, c_uint64, c_uint32]),
+    ("qmoe_repack", c_int, [POINTER(QmoeTensor), c_uint32, c_void_p, c_size_t, c_void_p]),
     ("qmoe_workspace_size", c_size_t, [POINTER(QmoeDims), c_int]),
     ("qmoe_ws_view", c_void_p, [c_void_p, POINTER(QmoeDims), c_int, c_int]),
     ("qmoe_router_topk", c_int, [POINTER(QmoeBlock), POINTER(QmoeDims), c_void_p, c_int, c_void_p, c_void_p,

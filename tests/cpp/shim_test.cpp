@@ -216,6 +216,27 @@ int main() {
     for (int i = 0; i < d; ++i) bad += close(y[i], want[i]) ? 0 : 1;
     CHECK(bad == 0, "after a barrier timeout: %d of %d MoE outputs outside tolerance", bad, d);
 
+    // repack_tensor: a Q6_K tensor read by matmul_dispatch moves to the
+    // 16-byte-aligned layout; the products are bit-identical, and a Q4_K
+    // tensor is left alone
+    {
+        const int rows = 300;
+        Tensor head = make("output.weight", GgmlType::Q6_K, {d, rows}, seed, 30, 0.02f);
+        std::vector<float> a(rows), b(rows);
+        matmul_dispatch(head.q, dx, dy, rows, d, ctx.stream());
+        ctx.synchronize();
+        CUDA_CHECK(cudaMemcpy(a.data(), dy, sizeof(float) * rows, cudaMemcpyDeviceToHost));
+        const uint64_t before = head.q.size_bytes;
+        CHECK(repack_tensor(head.q, ctx.stream()), "Q6_K tensor not repacked");
+        CHECK(head.q.layout == QMOE_LAYOUT_Q6K_A16 && head.q.size_bytes == before / 210 * 224, "repacked layout/size");
+        matmul_dispatch(head.q, dx, dy, rows, d, ctx.stream());
+        ctx.synchronize();
+        CUDA_CHECK(cudaMemcpy(b.data(), dy, sizeof(float) * rows, cudaMemcpyDeviceToHost));
+        CHECK(std::memcmp(a.data(), b.data(), sizeof(float) * rows) == 0, "GEMV on the repacked tensor differs");
+        CHECK(!repack_tensor(eg.q, ctx.stream()) && eg.q.layout == 0, "Q4_K tensor must stay as uploaded");
+        cudaFree(head.q.device_ptr);
+    }
+
     // MoePrefill: the MoE halves of two layers for a batch of T = 20 tokens
     // (tensor-core path) with a token mixer between them, against the same
     // layer loop written out with the C-ABI (bit-identical: same kernels)

@@ -123,3 +123,29 @@ def test_python_mirror_errors_match_reference_messages():
         matmul.matmul_dispatch(t, 0x1000, 0x2000, 512, 2048)
     with pytest.raises(RuntimeError, match="cannot dequantize"):
         matmul.dequantize_row(t, 0x1000, 0, 2048)
+
+
+def test_repack_sizes_and_argument_checks_without_gpu():
+    L = _lib.lib()
+    A16 = _lib.QMOE_LAYOUT_Q6K_A16
+    assert L.qmoe_repack_bytes(14, 2048 * 512, A16) == 2048 * 512 // 256 * 224
+    assert L.qmoe_repack_bytes(14, 2048 * 512, 0) == 2048 * 512 // 256 * 210
+    assert L.qmoe_repack_bytes(12, 2048 * 512, A16) == 0      # Q6_K only
+    assert L.qmoe_repack_bytes(14, 2048 * 512, 7) == 0        # unknown layout
+    q6 = _lib.QmoeTensor(0x10000, 14, 0, 256 * 64)
+    q4 = _lib.QmoeTensor(0x10000, 12, 0, 256 * 64)
+    assert L.qmoe_repack(ctypes.byref(q4), A16, 0x20000, 1 << 20, None) == _lib.QMOE_ERR_TYPE
+    assert L.qmoe_repack(ctypes.byref(q6), 7, 0x20000, 1 << 20, None) == _lib.QMOE_ERR_UNSUPPORTED
+    assert L.qmoe_repack(ctypes.byref(q6), A16, 0x20000, 100, None) == _lib.QMOE_ERR_SHAPE
+    assert L.qmoe_repack(ctypes.byref(q6), A16, 0x20008, 1 << 20, None) == _lib.QMOE_ERR_ALIGN
+    # the block entry points read GGUF layouts only
+    dims = Dims()
+    dc = dims.c()
+    blk = _block_with(dims)
+    blk.gate_exps.layout = A16
+    assert L.qmoe_block_forward(ctypes.byref(blk), ctypes.byref(dc), 0x30000, 0x40000, None, 1, 0x20000, 1 << 40,
+                                None) == _lib.QMOE_ERR_UNSUPPORTED
+    # a repacked view of a type that has no repacked layout: rejected before any launch
+    q4r = _lib.QmoeTensor(0x10000, 12, A16, 512 * 2048)
+    assert L.qmoe_gemv(ctypes.byref(q4r), 0x1000, 0x2000, 512, 2048, 0, None) == _lib.QMOE_ERR_UNSUPPORTED
+

@@ -122,6 +122,42 @@ def test_gemv_stream_vs_oracle(ty, K, M, row0):
     assert np.allclose(got[:M], want, rtol=1e-5, atol=1e-5), np.max(np.abs(got[:M] - want))
 
 
+@pytest.mark.parametrize("K,M,row0", [(2048, 1203, 5), (256, 777, 3), (4096, 301, 2)])
+def test_gemv_on_repacked_q6k(K, M, row0):
+    """qmoe_repack to QMOE_LAYOUT_Q6K_A16 (each 210-byte super-block in a
+    224-byte slot) and qmoe_gemv on the repacked copy: the bytes match the
+    padded GGUF blocks and the products are bit-identical to the GEMV on the
+    GGUF layout (same unit decoder, aligned reads)."""
+    import torch
+    ty = GgmlType.Q6_K
+    rows = M + row0 + 1
+    n = rows * K
+    h = np.empty(calculate_tensor_bytes(ty, n), dtype=np.uint8)
+    synth.fill(h, ty, n, 9, 23, 0.02)
+    w = torch.from_numpy(h).cuda()
+    t = _tensor(w, ty, n)
+    nb = _lib.lib().qmoe_repack_bytes(int(ty), n, _lib.QMOE_LAYOUT_Q6K_A16)
+    assert nb == n // 256 * 224
+    wr = torch.full((nb,), 0x5A, dtype=torch.uint8, device="cuda")
+    _lib.check(_lib.lib().qmoe_repack(ctypes.byref(t), _lib.QMOE_LAYOUT_Q6K_A16, wr.data_ptr(), nb, None))
+    torch.cuda.synchronize()
+    want_bytes = np.zeros((n // 256, 224), dtype=np.uint8)
+    want_bytes[:, :210] = h.reshape(-1, 210)
+    assert np.array_equal(wr.cpu().numpy().reshape(-1, 224), want_bytes)
+    tr = _lib.QmoeTensor(wr.data_ptr(), int(ty), _lib.QMOE_LAYOUT_Q6K_A16, n)
+    x = torch.from_numpy(np.random.default_rng(K).standard_normal(K).astype(np.float32)).cuda()
+    y0 = torch.empty(M, device="cuda")
+    y1 = torch.full((M,), float("nan"), device="cuda")
+    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(t), x.data_ptr(), y0.data_ptr(), M, K, row0 * K, None))
+    _lib.check(_lib.lib().qmoe_gemv(ctypes.byref(tr), x.data_ptr(), y1.data_ptr(), M, K, row0 * K, None))
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    # the repacked layout is read by the streaming GEMV only
+    assert _lib.lib().qmoe_gemv_exact(ctypes.byref(tr), x.data_ptr(), y1.data_ptr(), M, K, 0, None) == \
+        _lib.QMOE_ERR_UNSUPPORTED
+    assert _lib.lib().qmoe_dequant_row(ctypes.byref(tr), y1.data_ptr(), 0, K, None) == _lib.QMOE_ERR_UNSUPPORTED
+
+
 def _router_block(dims, bias, seed):
     return synth.Block(dims, synth.Q4K_TYPES, seed=seed, device="cuda", bias=bias)
 
