@@ -432,13 +432,16 @@ __device__ __forceinline__ int ilog2(int v) { return 31 - __clz(v); }
 // planes in shared memory (token stride xq_stride).  Each warp quantises
 // 128-element chunks (lanes 8m..8m+7 hold one 32-block); every load is issued
 // before the first plane is written.  NTHREADS is a multiple of 32 and
-// T * d / 4 a multiple of 32, so each chunk test is warp-uniform.
+// T * d / 4 a multiple of 32, so each chunk test is warp-uniform.  Two chunks
+// per thread are unrolled (all of them for one token at d = 2048): this code
+// runs cold while the routing warps run, and every further inlined copy of
+// the plane writer takes instruction fetches from the routing.
 template <int NTHREADS>
 __device__ __forceinline__ void x_planes_smem(uint8_t* xs, const DecodeParams& P, int tid) {
     const int lq = ilog2(P.d) - 2;  // float4s per token = 2^lq
     const int nv = P.T << lq;
     const int lane = tid & 31;
-    constexpr int J = 8;
+    constexpr int J = 2;
     float4 v[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
