@@ -920,6 +920,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
     const int lgF = ilog2(P.F / ITEM_ROWS);
     const int Rd = L.Rd, r0d = c * Rd;
     const int nrow = max(0, min(Rd, d - r0d));
+    const int dnst = L.dnst;
     const uint32_t half_bytes = L.half_bytes;
 
     if (tid == 0) {
@@ -965,13 +966,104 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
         if (sp.tx) bulk_g2s(dd, sp.lo, sp.tx, dfull + slot, P.ctrl);
     };
 
-    // prologue: loads that do not depend on the routing
-    if (warp == FX_NCW && lane == 0) {
-        if (c < nb_sh) issue_gu(0, true, -1, c * ITEM_ROWS);
-        if (sh && nrow > 0) issue_dn(0, 0);
+    // The producer lane issues every copy of the first round through one
+    // loop body: the prologue's routing-independent copies (the shared
+    // expert's down rows in every CTA, a shared gate/up item in the first
+    // CTAs) run it before the routing is known, so the instructions that
+    // issue the routed copies right after the routing are already fetched
+    // (code that runs for the first time in a launch stalls on instruction
+    // fetches, and those stalls would also slow the consumers' first pass).
+    // Job q < ngu: gate/up sub-chunk (item kk = kb + q / gsub, slot kk,
+    // sub-chunk q % gsub, gate and up rows); otherwise down rows of source
+    // cc = cb + q - ngu into down slot cc.  Every field is a select, so both
+    // kinds run the same instructions.
+    if (warp == FX_NCW) {
+        // ---------------- producer ----------------
+        const int lgsub = L.gsub == 4 ? 2 : 0;
+        int ni = 0, nsrc = sh;
+#pragma unroll 1
+        for (int phase = 0; phase < 2; ++phase) {
+            if (phase) {
+                // the routing warps have written the schedule
+                asm volatile("bar.sync 5, %0;" ::"r"((RT_WARPS + 1) * 32) : "memory");
+                const int nact = s_sched[0];
+                const int nitems = nb_sh + (nact << lgF);
+                ni = c < nitems ? (nitems - 1 - c) / G + 1 : 0;
+                nsrc = nact + sh;
+            }
+            if (lane == 0) {
+                const int kb = (phase && c < nb_sh) ? 1 : 0;  // a shared item 0 went out in the prologue
+                const int ke = phase ? min(ni, L.gnst) : (c < nb_sh ? 1 : 0);
+                const int ccb = phase ? sh : 0;
+                const int cce = nrow > 0 ? (phase ? min(nsrc, dnst) : sh) : 0;
+                const int ngu = max(ke - kb, 0) << lgsub;
+                const int nj = ngu + max(cce - ccb, 0);
+#pragma unroll 1
+                for (int q = 0; q < nj; ++q) {
+                    const bool gu = q < ngu;
+                    const int kk = kb + (q >> lgsub);
+                    const int jsub = q & (L.gsub - 1);
+                    const int cc = ccb + (q - ngu);
+                    const int it = c + kk * G;
+                    const int jr = max(it - nb_sh, 0);
+                    const bool shj = gu ? it < nb_sh : cc < sh;
+                    const int si = gu ? (jr >> lgF) : max(cc - sh, 0);
+                    const int expert = shj ? 0 : s_sched[SCHED_HDR + 3 * si];
+                    const uint64_t rbj = gu ? (shj ? rbs : rbg) : (shj ? rbsd : rbd);
+                    const int rsub = ITEM_ROWS >> lgsub;
+                    const int r0 = (shj ? it : (jr & ((1 << lgF) - 1))) * ITEM_ROWS + jsub * rsub;
+                    const uint64_t row = gu ? (shj ? static_cast<uint64_t>(r0) : static_cast<uint64_t>(expert) * P.F + r0)
+                                            : (shj ? static_cast<uint64_t>(r0d) : static_cast<uint64_t>(expert) * d + r0d);
+                    const uint8_t* b0 = gu ? (shj ? P.sgate.p : P.gate.p) : (shj ? P.sdown.p : P.down.p);
+                    const uint8_t* e0 = gu ? (shj ? P.sgate.end : P.gate.end) : (shj ? P.sdown.end : P.down.end);
+                    const uint8_t* b1 = shj ? P.sup.p : P.up.p;
+                    const uint8_t* e1 = shj ? P.sup.end : P.up.end;
+                    const uint32_t n0 = static_cast<uint32_t>((gu ? rsub : nrow) * rbj);
+                    const uint32_t n1 = gu ? n0 : 0u;
+                    uint8_t* d0 = gu ? gst + static_cast<size_t>(kk) * 2 * half_bytes + static_cast<size_t>(jsub) * n0
+                                     : dst + static_cast<size_t>(cc) * L.dstage;
+                    uint8_t* d1 = d0 + half_bytes;
+                    uint64_t* bar = gu ? gfull + 4 * kk + jsub : dfull + cc;
+                    const uint8_t *lo0 = nullptr, *lo1 = nullptr;
+                    uint32_t tx0 = 0, tx1 = 0;
+#pragma unroll 1
+                    for (int h = 0; h < (n1 ? 2 : 1); ++h) {
+                        const StagePlan sp = plan_stage(h ? d1 : d0, (h ? b1 : b0) + row * rbj, h ? n1 : n0, h ? e1 : e0);
+                        if (h) { lo1 = sp.lo; tx1 = sp.tx; } else { lo0 = sp.lo; tx0 = sp.tx; }
+                    }
+                    mbar_arrive_expect_tx(bar, tx0 + tx1);
+#pragma unroll 1
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t tx = h ? tx1 : tx0;
+                        if (tx) bulk_g2s(h ? d1 : d0, h ? lo1 : lo0, tx, bar, P.ctrl);
+                    }
+                }
+            }
+        }
+        if (lane == 0) {  // later items of this CTA, as ring slots are released
+            int kk = min(ni, L.gnst), it = c + kk * G, slot = kk % L.gnst, round = kk / L.gnst;
+            for (; kk < ni; ++kk, it += G) {
+                mbar_wait(gempty + slot, (round - 1) & 1, P.ctrl);
+                if (it < nb_sh) {
+                    issue_gu(slot, true, -1, it * ITEM_ROWS);
+                } else {
+                    const int jr = it - nb_sh;
+                    issue_gu(slot, false, s_sched[SCHED_HDR + 3 * (jr >> lgF)], (jr & ((1 << lgF) - 1)) * ITEM_ROWS);
+                }
+                if (++slot == L.gnst) { slot = 0; ++round; }
+            }
+        }
+        for (int rb0 = dnst; rb0 < nsrc; rb0 += dnst) {  // later down rounds, if the sources do not all fit
+            asm volatile("bar.sync 2, %0;" ::"r"((FX_NCW + 1) * 32) : "memory");
+            if (lane == 0 && nrow > 0)
+                for (int cc = rb0; cc < min(nsrc, rb0 + dnst); ++cc) issue_dn(cc, cc - rb0);
+        }
+        return;
     }
-    if (tid == 0) pdl_wait();  // the router has finished: schedule and block input are valid
-    __syncthreads();
+
+    // ---------------- consumers ----------------
+    if (tid == 0) pdl_wait();  // the router has finished: logits and block input are valid
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");
     if (tid == 0) QMOE_TRACE(P, 1, 1);
     if (warp < RT_WARPS) {
         // every CTA selects the experts itself from the router logits (CTA 0
@@ -979,9 +1071,10 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
         // between the router's logits and this CTA's weight loads
         topk_and_schedule(P, s_sched, s_w, c == 0, 3);
         if (tid == 0) QMOE_TRACE(P, 1, 6);
+        asm volatile("bar.arrive 5, %0;" ::"r"((RT_WARPS + 1) * 32) : "memory");  // to the producer
     } else {
         // the other warps: input planes, shared-expert gate, residual rows
-        constexpr int NTH = FX_THREADS - RT_WARPS * 32;
+        constexpr int NTH = (FX_NCW - RT_WARPS) * 32;
         const int t2 = tid - RT_WARPS * 32;
         const int nres = (P.residual && nrow > 0) ? P.T * nrow : 0;
         const int n32 = P.T + nres;
@@ -1004,7 +1097,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
         for (int q = t2 + NTH; q < n32; q += NTH) store32(q, load32(q));
         if (t2 == 0) QMOE_TRACE(P, 1, 7);
     }
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(FX_NCW * 32) : "memory");  // schedule, planes and gates are written
     if (tid == 0) QMOE_TRACE(P, 1, 2);
     const int nact = s_sched[0];
     const int npairs = s_sched[1];
@@ -1013,39 +1106,6 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
     const int nitems = nb_sh + (nact << lgF);
     const int ni = c < nitems ? (nitems - 1 - c) / G + 1 : 0;
     const int nsrc = nact + sh;
-    const int dnst = L.dnst;
-
-    if (warp == FX_NCW) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            auto issue_item = [&](int slot, int i) {
-                if (i < nb_sh) {
-                    issue_gu(slot, true, -1, i * ITEM_ROWS);
-                } else {
-                    const int j = i - nb_sh;
-                    issue_gu(slot, false, s_sched[SCHED_HDR + 3 * (j >> lgF)], (j & ((1 << lgF) - 1)) * ITEM_ROWS);
-                }
-            };
-            int kk = 0, i = c, slot = 0, round = 0;
-            for (; kk < ni && kk < L.gnst; ++kk, i += G) {  // first fill of the ring
-                if (kk > 0 || i >= nb_sh) issue_item(slot, i);  // a shared item 0 went out in the prologue
-                if (++slot == L.gnst) { slot = 0; ++round; }
-            }
-            if (nrow > 0)  // this CTA's down rows of the routed sources (first round)
-                for (int cc = sh; cc < min(nsrc, dnst); ++cc) issue_dn(cc, cc);
-            for (; kk < ni; ++kk, i += G) {
-                mbar_wait(gempty + slot, (round - 1) & 1, P.ctrl);
-                issue_item(slot, i);
-                if (++slot == L.gnst) { slot = 0; ++round; }
-            }
-        }
-        for (int rb0 = dnst; rb0 < nsrc; rb0 += dnst) {  // later down rounds, if the sources do not all fit
-            asm volatile("bar.sync 2, %0;" ::"r"((FX_NCW + 1) * 32) : "memory");
-            if (lane == 0 && nrow > 0)
-                for (int cc = rb0; cc < min(nsrc, rb0 + dnst); ++cc) issue_dn(cc, cc - rb0);
-        }
-        return;
-    }
 
     // ---------------- consumers: gate/up items ----------------
     {
