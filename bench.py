@@ -73,7 +73,7 @@ def _peaks():
 # same kernel on the same workload shape (dram__bytes_read.sum +
 # dram__bytes_write.sum; the capture command is in
 # profiles/k_experts_decode_q4k.md).  Imported, not measured by this run.
-EXPERT_TRAFFIC_BYTES = 16_045_824
+EXPERT_TRAFFIC_BYTES = 16_035_840
 
 
 class ClockSampler(threading.Thread):
