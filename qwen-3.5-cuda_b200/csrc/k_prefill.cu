@@ -815,50 +815,72 @@ __global__ void __launch_bounds__(256) k_pf_count(const int32_t* __restrict__ id
     for (int e = threadIdx.x; e < E; e += blockDim.x) counts[blockIdx.x * E + e] = __popcll(mask[e]);
 }
 
-// counts[b][e] -> first position of block b's pairs of expert e; offsets[E+1]
-__global__ void __launch_bounds__(256) k_pf_scan(int32_t* __restrict__ counts, int nb, int E, int32_t* __restrict__ offsets) {
+// counts[b][e] -> first position of block b's pairs of expert e; offsets[E+1].
+// One CTA of SCAN_SEG x 256 threads: thread (seg, e) owns expert e's counts
+// in the seg-th quarter of the token blocks, so the dependent global
+// round trips per thread are a quarter of the blocks: segment sums, then
+// each segment's start (expert base from the scan over experts + the
+// earlier segments of the same expert), then the running sum written back.
+constexpr int SCAN_SEG = 4;
+__global__ void __launch_bounds__(SCAN_SEG * 256) k_pf_scan(int32_t* __restrict__ counts, int nb, int E,
+                                                            int32_t* __restrict__ offsets) {
+    static_assert(kMaxExperts <= 256, "one thread per expert and segment");
+    __shared__ int s_seg[SCAN_SEG][256];
+    __shared__ int s_base[256];
     __shared__ int s_wsum[8];
-    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
-    constexpr int U = 16;  // loads issued ahead of the dependent stores
-    int run = 0;
+    const int e = threadIdx.x & 255, seg = threadIdx.x >> 8, lane = e & 31, warp = e >> 5;
+    const int per = (nb + SCAN_SEG - 1) / SCAN_SEG;
+    const int b_lo = min(nb, seg * per), b_hi = min(nb, b_lo + per);
+    constexpr int U = 8;  // loads issued ahead of the dependent adds / stores (64 registers)
+    int sum = 0;
     if (e < E)
-        for (int b0 = 0; b0 < nb; b0 += U) {
+        for (int b0 = b_lo; b0 < b_hi; b0 += U) {
             int c[U];
 #pragma unroll
-            for (int j = 0; j < U; ++j) c[j] = b0 + j < nb ? counts[(b0 + j) * E + e] : 0;
+            for (int j = 0; j < U; ++j) c[j] = b0 + j < b_hi ? counts[(b0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < U; ++j) sum += c[j];
+        }
+    s_seg[seg][e] = e < E ? sum : 0;
+    __syncthreads();
+    if (seg == 0) {
+        // exclusive scan of the experts' totals (threads 0..255)
+        int tot = 0;
+        for (int q = 0; q < SCAN_SEG; ++q) tot += s_seg[q][e];
+        int inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (lane == 31) s_wsum[warp] = inc;
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // the first 256 threads only
+        int base = 0, total = 0;
+        for (int w = 0; w < 8; ++w) {
+            base += w < warp ? s_wsum[w] : 0;
+            total += s_wsum[w];
+        }
+        const int off = base + inc - tot;
+        s_base[e] = off;
+        if (e < E) offsets[e] = off;
+        if (e == 0) offsets[E] = total;
+    }
+    __syncthreads();
+    if (e < E) {
+        int run = s_base[e];  // + expert e's pairs in the earlier segments
+        for (int q = 0; q < seg; ++q) run += s_seg[q][e];
+        for (int b0 = b_lo; b0 < b_hi; b0 += U) {
+            int c[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) c[j] = b0 + j < b_hi ? counts[(b0 + j) * E + e] : 0;
 #pragma unroll
             for (int j = 0; j < U; ++j)
-                if (b0 + j < nb) {
+                if (b0 + j < b_hi) {
                     counts[(b0 + j) * E + e] = run;
                     run += c[j];
                 }
         }
-    int inc = run;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
     }
-    if (lane == 31) s_wsum[warp] = inc;
-    __syncthreads();
-    int base = 0, total = 0;
-    for (int w = 0; w < 8; ++w) {
-        base += w < warp ? s_wsum[w] : 0;
-        total += s_wsum[w];
-    }
-    const int off = base + inc - run;
-    if (e < E) {
-        offsets[e] = off;
-        for (int b0 = 0; b0 < nb; b0 += U) {
-            int c[U];
-#pragma unroll
-            for (int j = 0; j < U; ++j) c[j] = b0 + j < nb ? counts[(b0 + j) * E + e] : 0;
-#pragma unroll
-            for (int j = 0; j < U; ++j)
-                if (b0 + j < nb) counts[(b0 + j) * E + e] = c[j] + off;
-        }
-    }
-    if (e == 0) offsets[E] = total;
 }
 
 __global__ void __launch_bounds__(256) k_pf_place(const int32_t* __restrict__ idx, int T, int k, int E,
@@ -1062,7 +1084,7 @@ static cudaError_t pf_dispatch(const int32_t* idx, int T, int k, int E, int32_t*
                                const int32_t* qmap = nullptr, int32_t* out_pos = nullptr) {
     const int nb = (T + DB - 1) / DB;
     k_pf_count<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp);
-    k_pf_scan<<<1, 256, 0, s>>>(B.disp, nb, E, offsets);
+    k_pf_scan<<<1, SCAN_SEG * 256, 0, s>>>(B.disp, nb, E, offsets);
     k_pf_place<<<nb, 256, 0, s>>>(idx, T, k, E, B.disp, perm, inv_perm);
     k_pf_plan<<<64, 256, 0, s>>>(offsets, perm, E, k, B.tok_of_pos, B.tile_start, qmap, out_pos);
     return cudaGetLastError();
