@@ -47,6 +47,15 @@ cudaError_t launch_dispatch(const int32_t* idx, int NP, int E, int32_t* offsets,
 size_t dispatch_scratch_bytes(int E);
 cudaError_t dispatch_noalloc_scratch(int32_t** p);
 
+// The fused expert kernel serves calls of up to kFusedMaxT tokens; larger
+// decode batches run gate/up and down as two kernels, which measured faster
+// at 8 tokens (at one CTA per SM the fused kernel's shared memory then holds
+// one gate/up slot and few down slots, so its items and down rounds
+// serialise) and slower at 4 (the fused kernel also saves the router's
+// routing step); outputs are bit-identical either way.
+constexpr int kFusedMaxT = 4;
+static bool use_fused(const DecodeParams& P) { return P.T <= kFusedMaxT && fused_supported(P); }
+
 __global__ void k_set_sink(uint32_t* ctrl, unsigned long long sink) {
     *reinterpret_cast<unsigned long long*>(ctrl + CTRL_SINK) = sink;
 }
@@ -396,7 +405,7 @@ int qmoe_expert_block(const qmoe_block* B, const qmoe_dims* D, int T, float* out
     DecodeParams P = make_params(B, D, nullptr, out, residual, T, ws);
     if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (fused_supported(P)) return cuda_status(launch_experts(P, s));
+    if (use_fused(P)) return cuda_status(launch_experts(P, s));
     cudaError_t e = launch_gateup(P, s);
     if (e == cudaSuccess) e = launch_down(P, s);
     return cuda_status(e);
@@ -596,7 +605,7 @@ int qmoe_block_kernel_count(const qmoe_block* B, const qmoe_dims* D, int T) {
     for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
         const int nt = std::min(kDecodeMaxT, T - t0);
         DecodeParams P = make_params(B, D, nullptr, nullptr, nullptr, nt, nullptr);
-        n += fused_supported(P) ? 2 : 3;
+        n += use_fused(P) ? 2 : 3;
     }
     return n;
 }
@@ -631,7 +640,7 @@ static int block_forward_impl(const qmoe_block* B, const qmoe_dims* D, const flo
             P.eps = eps;
         }
         if (!decode_supported(P)) return QMOE_ERR_UNSUPPORTED;
-        const bool fused = fused_supported(P);
+        const bool fused = use_fused(P);
         P.route_in_router = fused ? 0 : 1;
         cudaError_t e = launch_router(P, s);
         if (fused) {

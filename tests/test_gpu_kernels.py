@@ -229,6 +229,9 @@ CASES = [
     ("q4k_T1", REAL, synth.Q4K_TYPES, False, 1),
     ("mixed_bias_T1", REAL, synth.MIXED_TYPES, True, 1),
     ("mixed_bias_T2", REAL, synth.MIXED_TYPES, True, 2),
+    # fused kernel with several items per CTA and several down rounds
+    ("mixed_bias_T3", REAL, synth.MIXED_TYPES, True, 3),
+    # gate/up and down as two kernels (batches of more than 4 tokens)
     ("mixed_bias_T8", REAL, synth.MIXED_TYPES, True, 8),
     ("small_q5k_q80", synth.Dims(512, 64, 6, 256, 512),
      {**synth.Q4K_TYPES, "gate_exps": GgmlType.Q5_K, "up_exps": GgmlType.Q5_K, "down_exps": GgmlType.Q8_0,
@@ -265,7 +268,8 @@ def test_block_forward_vs_oracle(name, dims, types, bias, T):
     assert st == 0 and flags == 0
 
 
-@pytest.mark.parametrize("name,dims,types,bias,T", [CASES[1], CASES[3], CASES[5]], ids=[CASES[i][0] for i in (1, 3, 5)])
+@pytest.mark.parametrize("name,dims,types,bias,T", [CASES[i] for i in (1, 3, 4, 6)],
+                         ids=[CASES[i][0] for i in (1, 3, 4, 6)])
 def test_stage_entry_points_vs_block_forward(name, dims, types, bias, T):
     """router_topk -> expert_gateup -> down_combine (two expert kernels) and
     block_forward (fused expert kernel where an instance exists) agree with
