@@ -658,7 +658,6 @@ __global__ void __launch_bounds__(XK_THREADS, 2)
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* hbar = full + 72;
     int* s_sched = reinterpret_cast<int*>(smem + 1280);
     uint8_t* hs = reinterpret_cast<uint8_t*>(s_sched) + align_up(SCHED_SMEM_WORDS * 4, 128);
     const uint32_t hs_bytes = static_cast<uint32_t>(P.hq_stride) * static_cast<uint32_t>(nvec);
@@ -1337,10 +1336,6 @@ DevCache& dev_cache() {
     }
     return c;
 }
-
-// Preferred shared-memory budget per expert-kernel CTA: small enough that a
-// gate/up CTA and a down CTA fit on one SM together (PDL overlap).
-constexpr size_t kCoResidentSmem = 110 * 1024;
 
 template <typename... Args>
 cudaError_t launch(void (*kern)(Args...), int grid, int block, size_t smem, cudaStream_t s, Args... args) {

@@ -53,6 +53,7 @@ constexpr int PROD_THREADS = PROD_WARPS * 32;
 constexpr int EPI_WARP0 = 16;          // warps 16..19: TMEM epilogue (lane quarter = warp % 4)
 constexpr int MMA_WARP = 20;           // one thread issues the MMAs
 constexpr int THREADS = 21 * 32;
+static_assert(EPI_WARP0 == PROD_WARPS && MMA_WARP == EPI_WARP0 + 4 && THREADS == (MMA_WARP + 1) * 32, "warp roles");
 constexpr uint32_t A_BYTES = BM * 64;    // 8 KB: fp16 activations of one stage
 constexpr uint32_t B_BYTES = BN * 64;    // 16 KB: fp16 weights of one stage
 constexpr uint32_t RAW_SLOT = 32;        // Q4_K bytes per producer thread and stage: block header + 16 qs bytes
