@@ -315,7 +315,10 @@ QMOE_API int qmoe_ep_combine_routed(const qmoe_block* blk, const qmoe_dims* dims
                             size_t workspace_bytes, qmoe_stream_t stream);
 
 /* Number of kernels one qmoe_block_forward call with these arguments launches
- * (for profiling and launch accounting); negative status on bad arguments. */
+ * (for profiling and launch accounting), assuming a workspace of
+ * qmoe_workspace_size(dims, T) bytes: T > 8 with that workspace runs the
+ * prefill path, a smaller one runs chunks of 8 tokens through the decode
+ * kernels.  Negative status on bad arguments. */
 QMOE_API int qmoe_block_kernel_count(const qmoe_block* blk, const qmoe_dims* dims, int T);
 
 /* The whole MoE block for T tokens: router_topk, expert_gateup, down_combine.

@@ -1243,6 +1243,16 @@ cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStre
     return pf_shared_combine(P, B, B.Y, P.inv_perm, s);
 }
 
+// Kernels one launch_prefill call issues: routing (norm, router rows, router
+// tile, top-k), dispatch (count, scan, place, plan), the routed products
+// (row gather + TMA gate/up + TMA down, or the two cp.async GEMMs), the
+// shared expert's two GEMMs when there is one, and the combine.
+int prefill_kernel_count(const DecodeParams& P) {
+    const bool tma_routed = P.gate.type == P.up.type && tgemm_supported(P.gate.type, 0, P.F, P.d) &&
+                            tgemm_supported(P.down.type, 1, P.d, P.F);
+    return 4 + 4 + (tma_routed ? 3 : 2) + (P.has_shared ? 2 : 0) + 1;
+}
+
 // Expert-parallel pieces.  Route: x_in, X16 and top-k of T local tokens.
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s) { return pf_route(P, B, s); }
 

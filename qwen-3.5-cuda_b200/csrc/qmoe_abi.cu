@@ -15,6 +15,7 @@ bool decode_supported(const DecodeParams& P);
 bool fused_supported(const DecodeParams& P);
 bool prefill_supported(const DecodeParams& P);
 cudaError_t launch_prefill(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
+int prefill_kernel_count(const DecodeParams& P);
 cudaError_t launch_ep_route(const DecodeParams& P, const PrefillBufs& B, cudaStream_t s);
 cudaError_t launch_ep_experts(const DecodeParams& P, const PrefillBufs& B, const __half* x16, const int32_t* meta,
                               const int32_t* qmap, int32_t* out_pos, __half* y, int y_rows, const TgScatter* sc,
@@ -601,6 +602,10 @@ int qmoe_block_kernel_count(const qmoe_block* B, const qmoe_dims* D, int T) {
     int st;
     if (T <= 0) return -QMOE_ERR_ARG;
     if ((st = check_dims(D)) || (st = check_block(B, D))) return -st;
+    if (T > kDecodeMaxT) {  // the prefill path (with a workspace sized for T)
+        DecodeParams P = make_params(B, D, nullptr, nullptr, nullptr, T, nullptr);
+        if (prefill_supported(P)) return prefill_kernel_count(P);
+    }
     int n = 0;
     for (int t0 = 0; t0 < T; t0 += kDecodeMaxT) {
         const int nt = std::min(kDecodeMaxT, T - t0);

@@ -103,3 +103,18 @@ def test_prefill_prenorm_residual_matches_decode_slabs():
     torch.cuda.synchronize()
     assert np.array_equal(idx_pf, np.concatenate(idx_dec))
     assert_close(out_pf.cpu().numpy(), out_dec.cpu().numpy(), "prefill vs decode")
+
+
+@pytest.mark.parametrize("types,want", [(synth.Q4K_TYPES, 14), (synth.MIXED_TYPES, 13)], ids=["q4k", "mixed"])
+def test_prefill_kernel_count(types, want):
+    """qmoe_block_kernel_count on the prefill path: routing 4, dispatch 4, the
+    routed products (gather + two TMA GEMMs for Q4_K, two cp.async GEMMs
+    otherwise), the shared expert's two GEMMs and the combine; decode-sized
+    calls stay at 2 (fused) or 3 kernels."""
+    dims = synth.Dims()
+    blk = synth.Block(dims, types, seed=5, device="cuda")
+    c, dc = blk.c(), dims.c()
+    L = _lib.lib()
+    assert L.qmoe_block_kernel_count(ctypes.byref(c), ctypes.byref(dc), 4096) == want
+    assert L.qmoe_block_kernel_count(ctypes.byref(c), ctypes.byref(dc), 1) == 2
+    assert L.qmoe_block_kernel_count(ctypes.byref(c), ctypes.byref(dc), 8) == 3
