@@ -220,9 +220,10 @@ QMOE_API int qmoe_down_combine(const qmoe_block* blk, const qmoe_dims* dims, int
                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
 
 /* expert_gateup + down_combine in one step for the routing the workspace holds
- * (after qmoe_router_topk, T <= 8): a single fused launch -- gate/up items,
- * a device-wide barrier, down rows, combine -- where the weight types have a
- * fused instance, else the two kernels.  Same result as the two calls. */
+ * (after qmoe_router_topk, T <= 8): for up to 4 tokens a single fused launch
+ * -- gate/up items, a device-wide barrier, down rows, combine -- where the
+ * weight types have a fused instance, else (and for 5-8 tokens) the two
+ * kernels.  Same result as the two calls. */
 QMOE_API int qmoe_expert_block(const qmoe_block* blk, const qmoe_dims* dims, int T,
                       float* out, const float* residual,
                       void* workspace, size_t workspace_bytes, qmoe_stream_t stream);
