@@ -97,6 +97,13 @@ def test_block_argument_checks_without_gpu():
     bad = Dims(num_experts=512).c()
     assert L.qmoe_block_forward(ctypes.byref(_block_with(dims)), ctypes.byref(bad), 0x30000, 0x40000, None, 1, ws,
                                 big, None) == _lib.QMOE_ERR_UNSUPPORTED
+    # the launch count reports argument errors as negative statuses before
+    # it looks at the device
+    cnt = L.qmoe_block_kernel_count
+    assert cnt(ctypes.byref(_block_with(dims)), ctypes.byref(dc), 0) == -_lib.QMOE_ERR_ARG
+    assert cnt(ctypes.byref(_block_with(dims, gate_exps=_lib.QmoeTensor(0x10000, 3, 0, E * F * d))), ctypes.byref(dc),
+               1) == -_lib.QMOE_ERR_TYPE
+    assert cnt(ctypes.byref(_block_with(dims)), ctypes.byref(bad), 1) == -_lib.QMOE_ERR_UNSUPPORTED
 
 
 def test_gemv_argument_checks_without_gpu():
