@@ -974,7 +974,7 @@ __global__ void __launch_bounds__(FX_THREADS, 1) k_experts(const __grid_constant
     // fetches, and those stalls would also slow the consumers' first pass).
     // Job q < ngu: gate/up sub-chunk (item kk = kb + q / gsub, slot kk,
     // sub-chunk q % gsub, gate and up rows); otherwise down rows of source
-    // cc = cb + q - ngu into down slot cc.  Every field is a select, so both
+    // cc = ccb + q - ngu into down slot cc.  Every field is a select, so both
     // kinds run the same instructions.
     if (warp == FX_NCW) {
         // ---------------- producer ----------------
